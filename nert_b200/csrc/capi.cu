@@ -1,0 +1,416 @@
+// The extern "C" boundary (include/nert_b200.h): validation, then a launch on
+// the device's stream. C++ exceptions never cross it.
+
+#include "../../include/nert_b200.h"
+#include "igemm.cuh"
+#include "ops.cuh"
+#include "runtime.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace nb2 {
+const char* last_error();
+}
+
+using namespace nb2;
+
+namespace {
+
+template <typename F>
+int guard(F&& f) {
+    try {
+        f();
+        return NB2_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("out of host memory");
+        return NB2_ERR_NOMEM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return NB2_ERR_INVALID;
+    }
+}
+
+void need(bool ok, const std::string& msg) {
+    if (!ok) {
+        fail(kStatusInvalid, msg);
+    }
+}
+
+nb2_device* bind(nb2_device* dev) {
+    need(dev != nullptr, "null device");
+    dev->make_current();
+    return dev;
+}
+
+ConvGeom to_geom(const nb2_conv_geom* c) {
+    need(c != nullptr, "Conv: null geometry");
+    ConvGeom g{};
+    g.N = c->n;
+    g.C = c->c;
+    g.H = c->h;
+    g.W = c->w;
+    g.M = c->m;
+    g.KH = c->kh;
+    g.KW = c->kw;
+    g.OH = c->oh;
+    g.OW = c->ow;
+    g.sh = c->stride_h;
+    g.sw = c->stride_w;
+    g.ph = c->pad_top;
+    g.pw = c->pad_left;
+    g.dh = c->dil_h;
+    g.dw = c->dil_w;
+    g.group = c->group;
+    // Same checks and output formula as the reference Conv row
+    // (src/kernels/conv.cpp:151-218, WindowOutput :122-135).
+    need(g.N > 0 && g.C > 0 && g.H > 0 && g.W > 0 && g.M > 0 && g.KH > 0 && g.KW > 0,
+         "Conv: non-positive dimension");
+    need(g.group > 0, "Conv: group must be positive");
+    need(g.C % g.group == 0, "Conv: input channels are not divisible by group");
+    need(g.M % g.group == 0, "Conv: output channels are not divisible by group");
+    need(g.sh > 0 && g.sw > 0 && g.dh > 0 && g.dw > 0, "Conv: stride and dilation must be positive");
+    need(c->pad_top >= 0 && c->pad_left >= 0 && c->pad_bottom >= 0 && c->pad_right >= 0,
+         "Conv: pads must be non-negative");
+    auto out_dim = [](int64_t in, int64_t k, int64_t d, int64_t pb, int64_t pe, int64_t s) {
+        const int64_t numer = in + pb + pe - (d * (k - 1) + 1);
+        return numer < 0 ? int64_t{-1} : numer / s + 1;
+    };
+    const int64_t oh = out_dim(g.H, g.KH, g.dh, c->pad_top, c->pad_bottom, g.sh);
+    const int64_t ow = out_dim(g.W, g.KW, g.dw, c->pad_left, c->pad_right, g.sw);
+    need(oh > 0 && ow > 0, "Conv: window is larger than the padded input");
+    need(oh == g.OH && ow == g.OW, "Conv: output shape does not match the convolution");
+    need(g.KH * g.dh < 32768 && g.KW * g.dw < 32768, "Conv: kernel extent too large");
+    return g;
+}
+
+struct HostStage {
+    // pinned bounce buffer per device, grown on demand
+    static void* get(nb2_device* dev, size_t bytes) {
+        if (bytes > dev->pinned_bytes) {
+            check_cuda(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
+            if (dev->pinned) {
+                check_cuda(cudaFreeHost(dev->pinned), "cudaFreeHost");
+                dev->pinned = nullptr;
+                dev->pinned_bytes = 0;
+            }
+            const size_t sz = std::max<size_t>(bytes, 1 << 20);
+            check_cuda(cudaMallocHost(&dev->pinned, sz), "cudaMallocHost");
+            dev->pinned_bytes = sz;
+        }
+        return dev->pinned;
+    }
+};
+
+} // namespace
+
+extern "C" {
+
+const char* nb2_last_error(void) { return nb2::last_error(); }
+
+int nb2_device_open(int ordinal, nb2_device** out) {
+    return guard([&] {
+        need(out != nullptr, "null output pointer");
+        *out = nb2::device(ordinal);
+    });
+}
+
+int nb2_device_ordinal(const nb2_device* dev) { return dev ? dev->ordinal : -1; }
+
+void* nb2_device_stream(nb2_device* dev) { return dev ? static_cast<void*>(dev->stream) : nullptr; }
+
+int nb2_device_set_precision(nb2_device* dev, int precision) {
+    return guard([&] {
+        need(dev != nullptr, "null device");
+        need(precision == NB2_PREC_3XTF32 || precision == NB2_PREC_1XTF32, "unknown precision");
+        dev->precision = precision;
+    });
+}
+
+int nb2_device_get_precision(const nb2_device* dev) { return dev ? dev->precision : -1; }
+
+int nb2_device_synchronize(nb2_device* dev) {
+    return guard([&] {
+        bind(dev);
+        const int code = dev->take_device_error();
+        if (code != 0) {
+            fail(kStatusDevice, "a kernel reported device error " + std::to_string(code) +
+                                    (code == 1 ? " (bounded wait expired)" : code == 2 ? " (index out of range)" : ""));
+        }
+    });
+}
+
+int nb2_device_malloc(nb2_device* dev, int64_t bytes, void** out) {
+    return guard([&] {
+        need(out != nullptr, "null output pointer");
+        *out = nullptr;
+        if (bytes <= 0) {
+            return;
+        }
+        bind(dev);
+        if (cudaMalloc(out, static_cast<size_t>(bytes)) != cudaSuccess) {
+            cudaGetLastError();
+            *out = nullptr;
+            fail(kStatusNoMem, "cudaMalloc of " + std::to_string(bytes) + " bytes failed");
+        }
+    });
+}
+
+int nb2_device_free(nb2_device* dev, void* ptr) {
+    return guard([&] {
+        if (ptr == nullptr) {
+            return;
+        }
+        bind(dev);
+        check_cuda(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
+        check_cuda(cudaFree(ptr), "cudaFree");
+    });
+}
+
+int nb2_memcpy_h2d(nb2_device* dev, void* dst, const void* src, int64_t bytes) {
+    return guard([&] {
+        if (bytes == 0) {
+            return;
+        }
+        need(bytes > 0 && dst != nullptr && src != nullptr, "h2d: bad arguments");
+        bind(dev);
+        std::lock_guard<std::mutex> lock(dev->mu);
+        // Chunked through the pinned buffer so the caller may free `src`
+        // as soon as we return, while the copy stays ordered on the stream.
+        const size_t chunk = 64u << 20;
+        const auto* s = static_cast<const uint8_t*>(src);
+        auto* d = static_cast<uint8_t*>(dst);
+        size_t left = static_cast<size_t>(bytes);
+        void* pin = HostStage::get(dev, std::min(left, chunk));
+        while (left > 0) {
+            const size_t n = std::min(left, chunk);
+            check_cuda(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
+            std::memcpy(pin, s, n);
+            check_cuda(cudaMemcpyAsync(d, pin, n, cudaMemcpyHostToDevice, dev->stream), "cudaMemcpyAsync(H2D)");
+            s += n;
+            d += n;
+            left -= n;
+        }
+        check_cuda(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
+    });
+}
+
+int nb2_memcpy_d2h(nb2_device* dev, void* dst, const void* src, int64_t bytes) {
+    return guard([&] {
+        if (bytes == 0) {
+            return;
+        }
+        need(bytes > 0 && dst != nullptr && src != nullptr, "d2h: bad arguments");
+        bind(dev);
+        check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToHost, dev->stream),
+                   "cudaMemcpyAsync(D2H)");
+        const int code = dev->take_device_error();
+        if (code != 0) {
+            fail(kStatusDevice, "a kernel reported device error " + std::to_string(code));
+        }
+    });
+}
+
+int nb2_memcpy_d2d(nb2_device* dev, void* dst, const void* src, int64_t bytes) {
+    return guard([&] {
+        need(bytes >= 0, "d2d: negative size");
+        bind(dev);
+        nb2::copy(dev, src, dst, bytes);
+    });
+}
+
+int nb2_conv2d_packed_size(const nb2_conv_geom* g, int64_t* bytes) {
+    return guard([&] {
+        need(bytes != nullptr, "null output pointer");
+        *bytes = static_cast<int64_t>(conv_packed_bytes(to_geom(g)));
+    });
+}
+
+int nb2_conv2d_pack(nb2_device* dev, const nb2_conv_geom* g, const float* w, void* packed) {
+    return guard([&] {
+        const ConvGeom geom = to_geom(g);
+        need(w != nullptr && packed != nullptr, "Conv: null buffer");
+        bind(dev);
+        conv_pack(dev, geom, w, packed);
+    });
+}
+
+int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* x, const void* packed,
+                          const float* bias, const float* residual, int act, float* y) {
+    return guard([&] {
+        const ConvGeom geom = to_geom(g);
+        need(x != nullptr && packed != nullptr && y != nullptr, "Conv: null buffer");
+        bind(dev);
+        Epilogue ep;
+        ep.bias = bias;
+        ep.res = residual;
+        ep.act = act;
+        conv_run(dev, geom, x, packed, y, ep);
+    });
+}
+
+int nb2_conv2d(nb2_device* dev, const nb2_conv_geom* g, const float* x, const float* w, const float* bias,
+               const float* residual, int act, float* y) {
+    return guard([&] {
+        const ConvGeom geom = to_geom(g);
+        need(x != nullptr && w != nullptr && y != nullptr, "Conv: null buffer");
+        bind(dev);
+        void* packed = dev->scratch(conv_packed_bytes(geom));
+        conv_pack(dev, geom, w, packed);
+        Epilogue ep;
+        ep.bias = bias;
+        ep.res = residual;
+        ep.act = act;
+        conv_run(dev, geom, x, packed, y, ep);
+    });
+}
+
+int nb2_gemm(nb2_device* dev, const float* a, const float* b, const float* c, int c_rank, float* y, int64_t m,
+             int64_t n, int64_t k, int trans_a, int trans_b, float alpha, float beta, int act) {
+    return guard([&] {
+        need(m > 0 && n > 0 && k > 0, "Gemm: non-positive dimension");
+        need(a != nullptr && b != nullptr && y != nullptr, "Gemm: null buffer");
+        need(c_rank >= 0 && c_rank <= 2, "Gemm: bias shape must be [N] or [M,N]");
+        need(c_rank == 0 || c != nullptr, "Gemm: null buffer");
+        bind(dev);
+        GemmGeom g{};
+        g.M = m;
+        g.N = n;
+        g.K = k;
+        g.trans_a = trans_a;
+        g.trans_b = trans_b;
+        g.lda = trans_a ? m : k;
+        g.ldb = trans_b ? k : n;
+        g.ldc = n;
+        void* packed = dev->scratch(gemm_packed_bytes(g));
+        gemm_pack_b(dev, g, b, packed);
+        Epilogue ep;
+        ep.alpha = alpha;
+        if (c_rank == 1) {
+            ep.bias = c;
+            ep.bias_scale = beta;
+        } else if (c_rank == 2) {
+            ep.res = c;
+            ep.res_scale = beta;
+        }
+        ep.act = act;
+        gemm_run(dev, g, a, packed, y, ep);
+    });
+}
+
+int nb2_matmul(nb2_device* dev, const float* a, const int64_t* a_dims, int a_rank, const float* b,
+               const int64_t* b_dims, int b_rank, float* y) {
+    return guard([&] {
+        need(a_rank >= 1 && b_rank >= 1 && a_rank <= 8 && b_rank <= 8, "MatMul: operand rank must be 1..8");
+        need(a != nullptr && b != nullptr && y != nullptr, "MatMul: null buffer");
+        std::vector<int64_t> ad(a_dims, a_dims + a_rank), bd(b_dims, b_dims + b_rank);
+        // 1-D promotion (src/kernels/mat_mul.cpp:79-169)
+        if (ad.size() == 1) {
+            ad.insert(ad.begin(), 1);
+        }
+        if (bd.size() == 1) {
+            bd.push_back(1);
+        }
+        const int64_t M = ad[ad.size() - 2], K = ad.back();
+        const int64_t K2 = bd[bd.size() - 2], N = bd.back();
+        need(K == K2, "MatMul: contraction dimension mismatch");
+        need(M > 0 && N > 0 && K > 0, "MatMul: non-positive dimension");
+        std::vector<int64_t> abatch(ad.begin(), ad.end() - 2), bbatch(bd.begin(), bd.end() - 2);
+        const size_t r = std::max(abatch.size(), bbatch.size());
+        abatch.insert(abatch.begin(), r - abatch.size(), 1);
+        bbatch.insert(bbatch.begin(), r - bbatch.size(), 1);
+        int64_t batch = 1, a_count = 1, b_count = 1;
+        for (size_t i = 0; i < r; ++i) {
+            need(abatch[i] == bbatch[i] || abatch[i] == 1 || bbatch[i] == 1, "MatMul: batch dims do not broadcast");
+            batch *= std::max(abatch[i], bbatch[i]);
+            a_count *= abatch[i];
+            b_count *= bbatch[i];
+        }
+        need((a_count == batch || a_count == 1) && (b_count == batch || b_count == 1),
+             "MatMul: partial batch broadcasting is not supported");
+        bind(dev);
+        GemmGeom g{};
+        g.N = N;
+        g.K = K;
+        g.trans_a = 0;
+        g.trans_b = 0;
+        g.lda = K;
+        g.ldb = N;
+        g.ldc = N;
+        if (b_count == 1) {
+            // B shared by every batch: fold the batch into M (one GEMM).
+            g.M = M * batch;
+            g.batch = 1;
+        } else {
+            g.M = M;
+            g.batch = batch;
+            g.a_zstride = a_count == 1 ? 0 : M * K;
+            g.b_zstride = K * N;
+            g.c_zstride = M * N;
+        }
+        void* packed = dev->scratch(gemm_packed_bytes(g));
+        gemm_pack_b(dev, g, b, packed);
+        gemm_run(dev, g, a, packed, y, Epilogue{});
+    });
+}
+
+int nb2_unary(nb2_device* dev, int op, const float* x, float* y, int64_t count) {
+    return guard([&] {
+        need(count >= 0, "unary: negative count");
+        need(op >= 0 && op <= kUGeluErf, "unary: unknown op");
+        need(count == 0 || (x != nullptr && y != nullptr), "unary: null buffer");
+        bind(dev);
+        unary(dev, op, x, y, count);
+    });
+}
+
+int nb2_binary(nb2_device* dev, int op, int dtype, const void* a, const int64_t* a_dims, int a_rank, const void* b,
+               const int64_t* b_dims, int b_rank, void* y, const int64_t* y_dims, int y_rank) {
+    return guard([&] {
+        need(op >= 0 && op <= kBPow, "binary: unknown op");
+        need(a_rank >= 0 && b_rank >= 0 && y_rank >= 0 && y_rank <= kMaxRank, "binary: bad rank");
+        std::vector<int64_t> ad(a_dims, a_dims + a_rank), bd(b_dims, b_dims + b_rank), yd(y_dims, y_dims + y_rank);
+        // the output must be the broadcast of the inputs
+        const size_t r = std::max(ad.size(), bd.size());
+        need(yd.size() == r, "binary: output rank does not match the broadcast");
+        for (size_t i = 0; i < r; ++i) {
+            const int64_t x1 = i + ad.size() >= r ? ad[i + ad.size() - r] : 1;
+            const int64_t x2 = i + bd.size() >= r ? bd[i + bd.size() - r] : 1;
+            need(x1 == x2 || x1 == 1 || x2 == 1, "binary: shapes do not broadcast");
+            need(yd[i] == std::max(x1, x2), "binary: output shape does not match the broadcast");
+        }
+        bind(dev);
+        binary(dev, op, dtype, a, ad, b, bd, y, yd);
+    });
+}
+
+int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
+                  const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4],
+                  const int64_t dilations[2]) {
+    return guard([&] {
+        PoolGeom g{x_dims[0], x_dims[1], x_dims[2], x_dims[3], y_dims[2], y_dims[3], kernel[0], kernel[1],
+                   strides[0], strides[1], pads[0], pads[1], dilations[0], dilations[1]};
+        need(y_dims[0] == g.N && y_dims[1] == g.C, "MaxPool: output shape does not match the pooling window");
+        need(g.KH > 0 && g.KW > 0, "MaxPool: kernel dimensions must be positive");
+        need(g.sh > 0 && g.sw > 0 && g.dh > 0 && g.dw > 0, "MaxPool: stride and dilation must be positive");
+        need(x != nullptr && y != nullptr, "MaxPool: null buffer");
+        bind(dev);
+        maxpool2d(dev, g, x, y);
+    });
+}
+
+int nb2_row_mean(nb2_device* dev, const float* x, int64_t rows, int64_t inner, float* y) {
+    return guard([&] {
+        need(rows >= 0 && inner > 0, "mean: bad extents");
+        need(rows == 0 || (x != nullptr && y != nullptr), "mean: null buffer");
+        bind(dev);
+        row_mean(dev, x, y, rows, inner);
+    });
+}
+
+} // extern "C"

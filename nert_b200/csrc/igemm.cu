@@ -1,0 +1,655 @@
+// tcgen05 contraction engine for Conv / Gemm / MatMul on sm_100a.
+//
+// Replaces the reference's cuDNN Conv row (src/cuda/conv.cu:230-530, FP32 FMA
+// math, no tensor cores) and cuBLAS Gemm/MatMul rows (src/cuda/gemm.cu:84-166,
+// src/cuda/mat_mul.cu:94-198, pedantic FP32). The reference CPU oracle
+// accumulates in double and rounds once (src/kernels/conv.cpp:263-289,
+// gemm.cpp:122-136); this engine keeps fp32 accuracy on tf32 tensor cores with
+// the 3xTF32 split of Ootomo & Yokota (2022): x = hi + lo with hi = tf32(x),
+// and D += A_lo*B_hi + A_hi*B_lo + A_hi*B_hi accumulated in fp32 in TMEM
+// (A_lo*B_lo, ~2^-22 relative, is dropped). 1xTF32 keeps only A_hi*B_hi.
+//
+// CTA = 10 warps, one 128 x BN output tile, BK = 32 fp32 (one 128-byte
+// swizzle row) per pipeline stage:
+//   warps 0-7  gather A (im2col / dense), split hi/lo, write the 128B-swizzled
+//              K-major tile; then the epilogue (TMEM -> registers -> global);
+//   warp 8     TMA loads of the pre-split B planes;
+//   warp 9     one thread issues tcgen05.mma (M=128, N=BN, K=8) into TMEM.
+// Every mbarrier wait is bounded (ptx.cuh); a timeout sets the device error
+// word and the CTA unwinds, frees its TMEM and returns.
+
+#include "igemm.cuh"
+#include "ptx.cuh"
+
+#include <algorithm>
+#include <cstring>
+
+namespace nb2 {
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+namespace {
+
+enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3 };
+
+struct Args {
+    int M, N, K, nkb;
+    int mode;
+    const float* a;
+    int64_t a_zstride;
+    int64_t lda;
+    int vec4; // dense K-major rows are 16-byte aligned with K % 4 == 0
+    // conv geometry
+    int C, H, W, OH, OW, KW, sh, sw, ph, pw, dh, dw, Cg;
+    int64_t HW, OHW, img_stride;
+    const int2* ktab;
+    // B
+    int b_zrows;
+    // epilogue
+    float* out;
+    int64_t out_zstride, out_img_stride, ldc;
+    int conv_out;
+    const float* bias;
+    int bias_zstride;
+    float bias_scale;
+    const float* res;
+    float res_scale;
+    float alpha;
+    int act;
+    int* err;
+};
+
+template <int BN, bool THREE>
+struct Cfg {
+    static constexpr int kAPlane = 128 * 128;
+    static constexpr int kBPlane = BN * 128;
+    static constexpr int kPlanes = THREE ? 2 : 1;
+    static constexpr int kStageBytes = (kAPlane + kBPlane) * kPlanes;
+    static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static constexpr int kThreads = 320;
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+    switch (act) {
+    case kActRelu:
+        return v > 0.0f ? v : 0.0f;
+    case kActSilu:
+        return v * (1.0f / (1.0f + expf(-v)));
+    case kActSigmoid:
+        return 1.0f / (1.0f + expf(-v));
+    default:
+        return v;
+    }
+}
+
+// Per-thread producer state: one output row (pixel / matrix row) of the tile
+// and one 16-wide half of every 32-wide K block.
+struct RowState {
+    bool ok;
+    const float* base; // mode-dependent base pointer
+    int ih0, iw0;      // conv: top-left input coordinate of the window
+    int m;
+    // conv tap-major running position
+    int cin, kh, kw;
+};
+
+__device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, int half, float (&v)[16]) {
+    if (p.mode == kAConvTap) {
+        // K ordered (kh, kw, cin) with Cg % 32 == 0: the whole 32-wide block
+        // sits on one filter tap, so validity is one test per block.
+        const int ih = rs.ih0 + rs.kh * p.dh;
+        const int iw = rs.iw0 + rs.kw * p.dw;
+        const bool ok = rs.ok && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
+        const float* src = rs.base + (int64_t)(rs.cin + half * 16) * p.HW + (int64_t)ih * p.W + iw;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            v[i] = ok ? __ldg(src + (int64_t)i * p.HW) : 0.0f;
+        }
+        // advance to the next block
+        rs.cin += 32;
+        if (rs.cin >= p.Cg) {
+            rs.cin = 0;
+            if (++rs.kw == p.KW) {
+                rs.kw = 0;
+                ++rs.kh;
+            }
+        }
+    } else if (p.mode == kAConvGeneric) {
+        const int k0 = kb * 32 + half * 16;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int2 e = __ldg(p.ktab + k0 + i);
+            const int dhk = e.y >> 16;
+            const int dwk = e.y & 0xFFFF;
+            const bool ok = rs.ok && e.y >= 0 && (unsigned)(rs.ih0 + dhk) < (unsigned)p.H &&
+                            (unsigned)(rs.iw0 + dwk) < (unsigned)p.W;
+            v[i] = ok ? __ldg(rs.base + e.x) : 0.0f;
+        }
+    } else if (p.mode == kADenseK) {
+        const int k0 = kb * 32 + half * 16;
+        if (p.vec4) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int k = k0 + q * 4;
+                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (rs.ok && k < p.K) {
+                    t = __ldg(reinterpret_cast<const float4*>(rs.base + k));
+                }
+                v[q * 4 + 0] = t.x;
+                v[q * 4 + 1] = t.y;
+                v[q * 4 + 2] = t.z;
+                v[q * 4 + 3] = t.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int k = k0 + i;
+                v[i] = (rs.ok && k < p.K) ? __ldg(rs.base + k) : 0.0f;
+            }
+        }
+    } else { // kADenseM: A stored [K][M] (transposed), row m is a column
+        const int k0 = kb * 32 + half * 16;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int k = k0 + i;
+            v[i] = (rs.ok && k < p.K) ? __ldg(rs.base + (int64_t)k * p.lda) : 0.0f;
+        }
+    }
+}
+
+template <bool THREE>
+__device__ __forceinline__ void store16(uint8_t* a_hi, uint8_t* a_lo, int r, int half, const float (&v)[16]) {
+    const uint32_t row_hi = smem_u32(a_hi) + r * 128;
+    const uint32_t row_lo = smem_u32(a_lo) + r * 128;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int c = half * 4 + q;
+        const uint32_t off = static_cast<uint32_t>((c ^ (r & 7)) << 4);
+        float h0 = to_tf32(v[q * 4 + 0]), h1 = to_tf32(v[q * 4 + 1]);
+        float h2 = to_tf32(v[q * 4 + 2]), h3 = to_tf32(v[q * 4 + 3]);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(row_hi + off), "f"(h0), "f"(h1), "f"(h2),
+                     "f"(h3)
+                     : "memory");
+        if (THREE) {
+            float l0 = v[q * 4 + 0] - h0, l1 = v[q * 4 + 1] - h1;
+            float l2 = v[q * 4 + 2] - h2, l3 = v[q * 4 + 3] - h3;
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(row_lo + off), "f"(l0), "f"(l1),
+                         "f"(l2), "f"(l3)
+                         : "memory");
+        }
+    }
+}
+
+// All 32 lanes wait; the outcome is made warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, err);
+    return __all_sync(0xffffffffu, ok);
+}
+
+template <int BN, bool THREE>
+__global__ void __launch_bounds__(320, 1)
+    igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
+                 const __grid_constant__ CUtensorMap tm_lo) {
+    using C = Cfg<BN, THREE>;
+    constexpr int S = C::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+    uint64_t* full_b = full_a + S;
+    uint64_t* empty = full_b + S;
+    uint64_t* acc_full = empty + S;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    auto a_hi = [&](int s) { return smem + s * C::kStageBytes; };
+    auto a_lo = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane; };
+    auto b_hi = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane * C::kPlanes; };
+    auto b_lo = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane * C::kPlanes + C::kBPlane; };
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int z = blockIdx.z;
+    const int m0 = blockIdx.x * 128;
+    const int n0 = blockIdx.y * BN;
+    const int nkb = p.nkb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_a[s], 8);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 8 && lane == 0) {
+        prefetch_tmap(&tm_hi);
+        if (THREE) {
+            prefetch_tmap(&tm_lo);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 8) {
+        // ---------------- producers ----------------
+        const int r = (warp & 3) * 32 + lane;
+        const int half = warp >> 2;
+        RowState rs;
+        rs.m = m0 + r;
+        rs.ok = rs.m < p.M;
+        rs.cin = 0;
+        rs.kh = 0;
+        rs.kw = 0;
+        const float* az = p.a + (int64_t)z * p.a_zstride;
+        if (p.mode == kAConvTap || p.mode == kAConvGeneric) {
+            const int mm = rs.ok ? rs.m : 0;
+            const int n_img = mm / (int)p.OHW;
+            const int pix = mm - n_img * (int)p.OHW;
+            const int oh = pix / p.OW;
+            const int ow = pix - oh * p.OW;
+            rs.ih0 = oh * p.sh - p.ph;
+            rs.iw0 = ow * p.sw - p.pw;
+            const float* img = az + (int64_t)n_img * p.img_stride;
+            rs.base = (p.mode == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
+        } else if (p.mode == kADenseK) {
+            rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
+        } else {
+            rs.base = az + (rs.ok ? rs.m : 0);
+        }
+
+        bool alive = true;
+        float cur[16], nxt[16];
+        gather16(p, rs, 0, half, cur);
+        for (int kb = 0; kb < nkb; ++kb) {
+            if (kb + 1 < nkb) {
+                gather16(p, rs, kb + 1, half, nxt);
+            }
+            const int s = kb % S;
+            const uint32_t ph = (kb / S) & 1;
+            if (!warp_wait(&empty[s], ph ^ 1, abort_flag, p.err)) {
+                alive = false;
+                break;
+            }
+            store16<THREE>(a_hi(s), a_lo(s), r, half, cur);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&full_a[s]);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                cur[i] = nxt[i];
+            }
+        }
+
+        // ---------------- epilogue ----------------
+        if (alive && warp_wait(acc_full, 0, abort_flag, p.err)) {
+            tc_fence_after();
+            const int quarter = warp & 3;
+            const int col_base = (warp >> 2) * (BN / 2);
+            const bool row_ok = rs.m < p.M;
+            int64_t row_off;
+            int64_t col_stride;
+            if (p.conv_out) {
+                const int mm = row_ok ? rs.m : 0;
+                const int n_img = mm / (int)p.OHW;
+                const int pix = mm - n_img * (int)p.OHW;
+                row_off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix;
+                col_stride = p.OHW;
+            } else {
+                row_off = (int64_t)z * p.out_zstride + (int64_t)(row_ok ? rs.m : 0) * p.ldc;
+                col_stride = 1;
+            }
+            const float* bias = p.bias ? p.bias + (int64_t)z * p.bias_zstride : nullptr;
+#pragma unroll 1
+            for (int cc = 0; cc < BN / 2; cc += 16) {
+                float acc[16];
+                tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col_base + cc, acc);
+                if (row_ok) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = n0 + col_base + cc + j;
+                        if (n < p.N) {
+                            float v = p.alpha * acc[j];
+                            if (bias) {
+                                v += p.bias_scale * __ldg(bias + n);
+                            }
+                            const int64_t off = row_off + (int64_t)n * col_stride;
+                            if (p.res) {
+                                v += p.res_scale * __ldg(p.res + off);
+                            }
+                            p.out[off] = apply_act(v, p.act);
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 8) {
+        // ---------------- TMA producer for B ----------------
+        if (lane == 0) {
+            int issued = 0;
+            const int row = n0 + z * p.b_zrows;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (kb / S) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.err)) {
+                    break;
+                }
+                mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
+                tma_load_2d(b_hi(s), &tm_hi, kb * 32, row, &full_b[s]);
+                if (THREE) {
+                    tma_load_2d(b_lo(s), &tm_lo, kb * 32, row, &full_b[s]);
+                }
+                ++issued;
+            }
+            // Never leave with a bulk copy still landing in shared memory.
+            for (int kb = issued - 1; kb >= 0 && kb >= issued - S; --kb) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&full_b[kb % S], (kb / S) & 1) && clock64() - t0 < kWaitBoundCycles) {
+                }
+            }
+        }
+    } else {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(128, BN);
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb % S;
+                const uint32_t ph = (kb / S) & 1;
+                if (!mbar_wait(&full_a[s], ph, abort_flag, p.err) || !mbar_wait(&full_b[s], ph, abort_flag, p.err)) {
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
+                const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+                    const uint64_t adh = sdesc_k128(ah + kk * 32);
+                    const uint64_t bdh = sdesc_k128(bh + kk * 32);
+                    if (THREE) {
+                        const uint64_t adl = sdesc_k128(al + kk * 32);
+                        const uint64_t bdl = sdesc_k128(bl + kk * 32);
+                        mma_tf32(tmem, adl, bdh, idesc, first);
+                        mma_tf32(tmem, adh, bdl, idesc, 1u);
+                        mma_tf32(tmem, adh, bdh, idesc, 1u);
+                    } else {
+                        mma_tf32(tmem, adh, bdh, idesc, first);
+                    }
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(acc_full);
+            // Wait for this thread's own MMAs before the CTA may free TMEM.
+            const long long t0 = clock64();
+            while (!mbar_try_wait(acc_full, 0) && clock64() - t0 < kWaitBoundCycles) {
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// ---- packing -------------------------------------------------------------
+
+enum BLayout : int { kBRowsK = 0, kBKRows = 1, kBConvTap = 2 };
+
+// out[z*rows + row][k] = hi/lo split of B(row, k), zero for k >= K.
+// 32x32 tiles through shared memory so both the read and the write coalesce.
+__global__ void pack_b_kernel(const float* __restrict__ src, int layout, int rows, int K, int Kpad, int64_t ld,
+                              int64_t zstride, int Cg, int KHKW, float* __restrict__ hi, float* __restrict__ lo) {
+    __shared__ float tile[32][33];
+    const int k0 = blockIdx.x * 32;
+    const int r0 = blockIdx.y * 32;
+    const int z = blockIdx.z;
+    const float* s = src + (int64_t)z * zstride;
+    const int tx = threadIdx.x, ty = threadIdx.y; // 32 x 8
+    for (int i = ty; i < 32; i += 8) {
+        if (layout == kBKRows) {
+            // consecutive threads walk rows (contiguous in src)
+            const int k = k0 + i, row = r0 + tx;
+            tile[tx][i] = (k < K && row < rows) ? s[(int64_t)k * ld + row] : 0.0f;
+        } else {
+            const int k = k0 + tx, row = r0 + i;
+            float v = 0.0f;
+            if (k < K && row < rows) {
+                if (layout == kBRowsK) {
+                    v = s[(int64_t)row * ld + k];
+                } else { // conv weight [M][Cg][KHKW], k = tap*Cg + cin
+                    const int tap = k / Cg, cin = k - tap * Cg;
+                    v = s[((int64_t)row * Cg + cin) * KHKW + tap];
+                }
+            }
+            tile[i][tx] = v;
+        }
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int row = r0 + i, k = k0 + tx;
+        if (row < rows && k < Kpad) {
+            const float v = tile[i][tx];
+            uint32_t h;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
+            const float hv = __uint_as_float(h);
+            const int64_t o = ((int64_t)z * rows + row) * Kpad + k;
+            hi[o] = hv;
+            lo[o] = v - hv;
+        }
+    }
+}
+
+// Per-k tap table for the generic conv gather: x = cin*H*W + kh*dh*W + kw*dw,
+// y = (kh*dh << 16) | kw*dw, or y = -1 for the zero padding k >= K.
+__global__ void conv_ktab_kernel(int2* tab, int K, int Kpad, int KHKW, int KW, int dh, int dw, int64_t HW, int W) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= Kpad) {
+        return;
+    }
+    if (k >= K) {
+        tab[k] = make_int2(0, -1);
+        return;
+    }
+    const int cin = k / KHKW;
+    const int t = k - cin * KHKW;
+    const int kh = t / KW, kw = t - kh * KW;
+    tab[k] = make_int2(static_cast<int>(cin * HW + (int64_t)kh * dh * W + (int64_t)kw * dw), ((kh * dh) << 16) | (kw * dw));
+}
+
+void make_tmap(CUtensorMap* map, const float* base, int64_t kpad, int64_t rows, int box_rows) {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kpad), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kpad * 4)};
+    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_tiled()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        fail(kStatusCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+    }
+}
+
+template <int BN, bool THREE>
+void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo) {
+    using C = Cfg<BN, THREE>;
+    static bool attr_set[64] = {};
+    if (!attr_set[dev->ordinal]) {
+        check_cuda(cudaFuncSetAttribute(igemm_kernel<BN, THREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::kSmemBytes),
+                   "cudaFuncSetAttribute(igemm)");
+        attr_set[dev->ordinal] = true;
+    }
+    igemm_kernel<BN, THREE><<<grid, C::kThreads, C::kSmemBytes, dev->stream>>>(a, hi, lo);
+    check_cuda(cudaGetLastError(), "igemm launch");
+}
+
+void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total) {
+    const int64_t kpad = static_cast<int64_t>(a.nkb) * 32;
+    const int bn = n_per_z <= 64 ? 64 : 128;
+    CUtensorMap hi, lo;
+    make_tmap(&hi, packed, kpad, rows_total, bn);
+    make_tmap(&lo, packed + rows_total * kpad, kpad, rows_total, bn);
+    a.err = dev->err_word;
+    const dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>((n_per_z + bn - 1) / bn),
+                    static_cast<unsigned>(z));
+    if (grid.y > 65535 || grid.z > 65535) {
+        fail(kStatusUnsupported, "igemm: grid too large");
+    }
+    const bool three = dev->precision == kPrec3xTF32;
+    if (bn == 64) {
+        three ? launch_bn<64, true>(dev, a, grid, hi, lo) : launch_bn<64, false>(dev, a, grid, hi, lo);
+    } else {
+        three ? launch_bn<128, true>(dev, a, grid, hi, lo) : launch_bn<128, false>(dev, a, grid, hi, lo);
+    }
+}
+
+void fill_epilogue(Args& a, const Epilogue& ep) {
+    a.alpha = ep.alpha;
+    a.bias = ep.bias;
+    a.bias_scale = ep.bias_scale;
+    a.res = ep.res;
+    a.res_scale = ep.res_scale;
+    a.act = ep.act;
+}
+
+} // namespace
+
+// ---- Conv ------------------------------------------------------------------
+
+size_t conv_packed_bytes(const ConvGeom& g) {
+    const int64_t kpad = round_up(g.K(), 32);
+    size_t bytes = static_cast<size_t>(2 * g.M * kpad * 4);
+    if (!g.tap_major()) {
+        bytes += static_cast<size_t>(kpad * 8);
+    }
+    return bytes;
+}
+
+void conv_pack(nb2_device* dev, const ConvGeom& g, const float* w, void* packed) {
+    const int64_t K = g.K(), kpad = round_up(K, 32);
+    float* hi = static_cast<float*>(packed);
+    float* lo = hi + g.M * kpad;
+    const int layout = g.tap_major() ? kBConvTap : kBRowsK;
+    const dim3 grid(static_cast<unsigned>(kpad / 32), static_cast<unsigned>((g.M + 31) / 32), 1);
+    pack_b_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(w, layout, static_cast<int>(g.M), static_cast<int>(K),
+                                                        static_cast<int>(kpad), K, 0, static_cast<int>(g.Cg()),
+                                                        static_cast<int>(g.KH * g.KW), hi, lo);
+    check_cuda(cudaGetLastError(), "pack_b launch");
+    if (!g.tap_major()) {
+        int2* tab = reinterpret_cast<int2*>(lo + g.M * kpad);
+        conv_ktab_kernel<<<static_cast<unsigned>((kpad + 255) / 256), 256, 0, dev->stream>>>(
+            tab, static_cast<int>(K), static_cast<int>(kpad), static_cast<int>(g.KH * g.KW), static_cast<int>(g.KW),
+            static_cast<int>(g.dh), static_cast<int>(g.dw), g.H * g.W, static_cast<int>(g.W));
+        check_cuda(cudaGetLastError(), "ktab launch");
+    }
+}
+
+void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* packed, float* y, const Epilogue& ep) {
+    const int64_t K = g.K(), kpad = round_up(K, 32);
+    const int64_t ohw = g.OH * g.OW;
+    const int64_t m_total = g.N * ohw;
+    if (m_total >= (1LL << 31) || g.C * g.H * g.W >= (1LL << 31) || ohw * g.M >= (1LL << 31)) {
+        fail(kStatusUnsupported, "Conv: tensor too large for 32-bit tile indexing");
+    }
+    Args a{};
+    a.M = static_cast<int>(m_total);
+    a.N = static_cast<int>(g.Mg());
+    a.K = static_cast<int>(K);
+    a.nkb = static_cast<int>(kpad / 32);
+    a.mode = g.tap_major() ? kAConvTap : kAConvGeneric;
+    a.a = x;
+    a.a_zstride = g.Cg() * g.H * g.W;
+    a.C = static_cast<int>(g.C);
+    a.H = static_cast<int>(g.H);
+    a.W = static_cast<int>(g.W);
+    a.OH = static_cast<int>(g.OH);
+    a.OW = static_cast<int>(g.OW);
+    a.KW = static_cast<int>(g.KW);
+    a.sh = static_cast<int>(g.sh);
+    a.sw = static_cast<int>(g.sw);
+    a.ph = static_cast<int>(g.ph);
+    a.pw = static_cast<int>(g.pw);
+    a.dh = static_cast<int>(g.dh);
+    a.dw = static_cast<int>(g.dw);
+    a.Cg = static_cast<int>(g.Cg());
+    a.HW = g.H * g.W;
+    a.OHW = ohw;
+    a.img_stride = g.C * g.H * g.W;
+    const float* hi = static_cast<const float*>(packed);
+    a.ktab = g.tap_major() ? nullptr : reinterpret_cast<const int2*>(hi + 2 * g.M * kpad);
+    a.b_zrows = static_cast<int>(g.Mg());
+    a.out = y;
+    a.out_zstride = g.Mg() * ohw;
+    a.out_img_stride = g.M * ohw;
+    a.conv_out = 1;
+    a.bias_zstride = static_cast<int>(g.Mg());
+    fill_epilogue(a, ep);
+    launch(dev, a, g.Mg(), g.group, hi, g.M);
+}
+
+// ---- Gemm / MatMul -----------------------------------------------------------
+
+size_t gemm_packed_bytes(const GemmGeom& g) {
+    const int64_t kpad = round_up(g.K, 32);
+    return static_cast<size_t>(2 * g.batch * g.N * kpad * 4);
+}
+
+void gemm_pack_b(nb2_device* dev, const GemmGeom& g, const float* b, void* packed) {
+    const int64_t kpad = round_up(g.K, 32);
+    float* hi = static_cast<float*>(packed);
+    float* lo = hi + g.batch * g.N * kpad;
+    // op(B) is [K,N]; packed rows are the N columns. transB=1 stores B as
+    // [N,K] (rows already K-major); transB=0 stores [K,N].
+    const int layout = g.trans_b ? kBRowsK : kBKRows;
+    const dim3 grid(static_cast<unsigned>(kpad / 32), static_cast<unsigned>((g.N + 31) / 32),
+                    static_cast<unsigned>(g.batch));
+    pack_b_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(b, layout, static_cast<int>(g.N), static_cast<int>(g.K),
+                                                        static_cast<int>(kpad), g.ldb, g.b_zstride, 1, 1, hi, lo);
+    check_cuda(cudaGetLastError(), "pack_b launch");
+}
+
+void gemm_run(nb2_device* dev, const GemmGeom& g, const float* a_ptr, const void* packed_b, float* y,
+              const Epilogue& ep) {
+    if (g.M >= (1LL << 31) || g.N >= (1LL << 31) || g.K >= (1LL << 31)) {
+        fail(kStatusUnsupported, "Gemm: dimension too large");
+    }
+    const int64_t kpad = round_up(g.K, 32);
+    Args a{};
+    a.M = static_cast<int>(g.M);
+    a.N = static_cast<int>(g.N);
+    a.K = static_cast<int>(g.K);
+    a.nkb = static_cast<int>(kpad / 32);
+    a.mode = g.trans_a ? kADenseM : kADenseK;
+    a.a = a_ptr;
+    a.a_zstride = g.a_zstride;
+    a.lda = g.lda;
+    a.vec4 = (!g.trans_a && g.K % 4 == 0 && g.lda % 4 == 0 && (reinterpret_cast<uintptr_t>(a_ptr) & 15) == 0 &&
+              (g.a_zstride % 4) == 0)
+                 ? 1
+                 : 0;
+    a.b_zrows = static_cast<int>(g.N);
+    a.out = y;
+    a.out_zstride = g.c_zstride;
+    a.ldc = g.ldc;
+    a.conv_out = 0;
+    a.bias_zstride = 0;
+    fill_epilogue(a, ep);
+    launch(dev, a, g.N, g.batch, static_cast<const float*>(packed_b), g.batch * g.N);
+}
+
+} // namespace nb2

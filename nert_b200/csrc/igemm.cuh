@@ -1,0 +1,64 @@
+// Host-facing interface of the tcgen05 contraction engine (igemm.cu).
+//
+// One kernel serves Conv (implicit GEMM on NCHW), Gemm and batched MatMul:
+//     D[z][M x N] = A[z][M x K] * B[z][N x K]^T, then a fused epilogue
+//     v = alpha*acc + bias_scale*bias[n] + res_scale*res[off]; act(v).
+// A is gathered by producer warps straight from the fp32 source (im2col
+// addressing for Conv, row- or column-major for dense operands) and split into
+// tf32 hi/lo planes in shared memory; B is a pre-packed, pre-split K-major
+// matrix [rows][Kpad] (hi plane, then lo plane) fetched by TMA.
+#pragma once
+
+#include "runtime.hpp"
+
+#include <cstdint>
+
+namespace nb2 {
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActSigmoid = 3 };
+
+struct Epilogue {
+    float alpha = 1.0f;
+    const float* bias = nullptr; // per output column n (per output channel for Conv)
+    float bias_scale = 1.0f;
+    const float* res = nullptr; // same layout as the output
+    float res_scale = 1.0f;
+    int act = kActNone;
+};
+
+// 2-D convolution geometry (1-D convolutions use H = KH = 1).
+struct ConvGeom {
+    int64_t N, C, H, W;  // input
+    int64_t M, KH, KW;   // weight [M, C/group, KH, KW]
+    int64_t OH, OW;      // output
+    int64_t sh, sw, ph, pw, dh, dw, group;
+    int64_t Cg() const { return C / group; }
+    int64_t Mg() const { return M / group; }
+    int64_t K() const { return Cg() * KH * KW; }
+    bool tap_major() const { return Cg() % 32 == 0; }
+};
+
+int64_t round_up(int64_t v, int64_t m);
+
+// Bytes of the packed weight buffer of a Conv: hi and lo planes of
+// [M][Kpad] fp32, then (generic layout only) a Kpad-entry int2 tap table.
+size_t conv_packed_bytes(const ConvGeom& g);
+void conv_pack(nb2_device* dev, const ConvGeom& g, const float* w, void* packed);
+void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* packed, float* y, const Epilogue& ep);
+
+// Dense GEMM: Y[M,N] = op(A)[M,K] * op(B)[K,N]; lda/ldb are the row strides of
+// A and B as stored. B is packed per call into `packed` (see gemm_packed_bytes).
+struct GemmGeom {
+    int64_t M, N, K;
+    int trans_a, trans_b;
+    int64_t lda, ldb, ldc;
+    int64_t batch = 1;                  // batched MatMul: z slices
+    int64_t a_zstride = 0, b_zstride = 0, c_zstride = 0;
+};
+
+size_t gemm_packed_bytes(const GemmGeom& g);
+void gemm_pack_b(nb2_device* dev, const GemmGeom& g, const float* b, void* packed);
+void gemm_run(nb2_device* dev, const GemmGeom& g, const float* a, const void* packed_b, float* y,
+              const Epilogue& ep);
+
+} // namespace nb2

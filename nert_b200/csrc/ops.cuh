@@ -1,0 +1,47 @@
+// Bandwidth-bound rows of the B200 layer (elementwise, pooling, reductions,
+// normalisation, data movement, selection). All launch on the device's
+// stream and return without synchronising.
+#pragma once
+
+#include "runtime.hpp"
+
+#include <cstdint>
+#include <vector>
+
+namespace nb2 {
+
+enum UnaryOp : int {
+    kURelu = 0,
+    kUSigmoid = 1,
+    kUErf = 2,
+    kUSqrt = 3,
+    kUNeg = 4,
+    kUAbs = 5,
+    kUExp = 6,
+    kUTanh = 7,
+    kUIdentity = 8,
+    kUSilu = 9,
+    kUGeluErf = 10, // 0.5*x*(1+erf(x/sqrt(2))) — the fused form of the Erf chain
+};
+
+enum BinaryOp : int { kBAdd = 0, kBSub = 1, kBMul = 2, kBDiv = 3, kBPow = 4 };
+
+// dtype codes shared with the C ABI
+enum Dtype : int { kF32 = 0, kI64 = 1, kBool = 2 };
+
+constexpr int kMaxRank = 8;
+
+void unary(nb2_device* dev, int op, const float* x, float* y, int64_t n);
+// y = a (op) b with NumPy broadcasting; a/b/y dims given explicitly.
+void binary(nb2_device* dev, int op, int dtype, const void* a, const std::vector<int64_t>& ad, const void* b,
+            const std::vector<int64_t>& bd, void* y, const std::vector<int64_t>& yd);
+void copy(nb2_device* dev, const void* src, void* dst, int64_t bytes);
+
+struct PoolGeom {
+    int64_t N, C, H, W, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
+};
+void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
+// mean over the trailing `inner` elements of each of `rows` rows
+void row_mean(nb2_device* dev, const float* x, float* y, int64_t rows, int64_t inner);
+
+} // namespace nb2

@@ -1,0 +1,133 @@
+// Pooling rows: MaxPool 2-D and spatial means (GlobalAveragePool / the
+// ReduceMean form of global pooling).
+//
+// Reference semantics: MaxPool takes the max over in-range taps only, -inf when
+// none is in range (src/kernels/max_pool.cpp:207-235); GlobalAveragePool sums
+// in double and divides by the spatial size (global_average_pool.cpp:59-67).
+// The reference CUDA rows use one thread per output / per row
+// (src/cuda/max_pool.cu:101-128, global_average_pool.cu:36-44).
+
+#include "ops.cuh"
+
+#include <cfloat>
+
+namespace nb2 {
+
+namespace {
+
+// One thread per output element, consecutive threads along the output row so
+// the window reads of a warp stay within a few cache lines.
+__global__ void maxpool2d_kernel(const float* __restrict__ x, float* __restrict__ y, PoolGeom g, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t ow = i % g.OW;
+        int64_t t = i / g.OW;
+        const int64_t oh = t % g.OH;
+        t /= g.OH; // n*C + c
+        const float* plane = x + t * g.H * g.W;
+        const int64_t h0 = oh * g.sh - g.ph;
+        const int64_t w0 = ow * g.sw - g.pw;
+        float best = -INFINITY;
+        for (int64_t kh = 0; kh < g.KH; ++kh) {
+            const int64_t ih = h0 + kh * g.dh;
+            if (ih < 0 || ih >= g.H) {
+                continue;
+            }
+            const float* row = plane + ih * g.W;
+            for (int64_t kw = 0; kw < g.KW; ++kw) {
+                const int64_t iw = w0 + kw * g.dw;
+                if (iw < 0 || iw >= g.W) {
+                    continue;
+                }
+                const float v = __ldg(row + iw);
+                if (v > best) {
+                    best = v;
+                }
+            }
+        }
+        y[i] = best;
+    }
+}
+
+// Warp per row, double accumulation, for short rows (e.g. 7x7 = 49).
+__global__ void row_mean_warp_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t inner) {
+    const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= rows) {
+        return;
+    }
+    const float* r = x + warp * inner;
+    double s = 0.0;
+    for (int64_t k = lane; k < inner; k += 32) {
+        s += static_cast<double>(__ldg(r + k));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    if (lane == 0) {
+        y[warp] = static_cast<float>(s / static_cast<double>(inner));
+    }
+}
+
+// Block per row for long rows.
+__global__ void row_mean_block_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t inner) {
+    __shared__ double part[32];
+    const float* r = x + blockIdx.x * inner;
+    double s = 0.0;
+    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0 && inner % 4 == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(r);
+        for (int64_t k = threadIdx.x; k < inner / 4; k += blockDim.x) {
+            const float4 v = __ldg(r4 + k);
+            s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+        }
+    } else {
+        for (int64_t k = threadIdx.x; k < inner; k += blockDim.x) {
+            s += static_cast<double>(__ldg(r + k));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        part[threadIdx.x >> 5] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < blockDim.x / 32 ? part[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+        }
+        if (threadIdx.x == 0) {
+            y[blockIdx.x] = static_cast<float>(s / static_cast<double>(inner));
+        }
+    }
+}
+
+} // namespace
+
+void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {
+    const int64_t total = g.N * g.C * g.OH * g.OW;
+    if (total <= 0) {
+        return;
+    }
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
+    maxpool2d_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
+    check_cuda(cudaGetLastError(), "maxpool launch");
+}
+
+void row_mean(nb2_device* dev, const float* x, float* y, int64_t rows, int64_t inner) {
+    if (rows <= 0 || inner <= 0) {
+        return;
+    }
+    if (inner <= 1024) {
+        const int64_t blocks = (rows * 32 + 255) / 256;
+        row_mean_warp_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, rows, inner);
+    } else {
+        row_mean_block_kernel<<<static_cast<unsigned>(rows), 256, 0, dev->stream>>>(x, y, inner);
+    }
+    check_cuda(cudaGetLastError(), "row_mean launch");
+}
+
+} // namespace nb2
