@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""ResNet-18 fp32 inference throughput on the B200 layer (images/s, bs64 per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step is one full ResNet-18 forward pass (batch 64 per GPU, 3x224x224,
+seeded synthetic input and Kaiming weights, BatchNorm folded) through the
+engine's public API. Multi-GPU runs are batch-sharded replicas (one process
+per GPU under torchrun, no collective on the data path); rank timings are
+combined as the max over ranks.
+
+* value:  device-resident input, one CUDA-graph replay per step, timed with
+          CUDA events on the engine's stream; L2 is flushed (256 MB write)
+          between steps, outside the timed events.
+* e2e:    the same through Model.run (pinned host input -> H2D -> run -> D2H
+          of the logits) per step.
+* roofline: the tensor-core Conv/Gemm kernel's algorithmic FLOP/s (from one
+          eager pass with an event between rows) against the measured TF32
+          dense peak / 3 (the 3xTF32 effective peak).
+* cpu_baseline: the reference NERT CpuDevice (oracle/_ref, compiled from the
+          reference sources) on the host cores, one image per process.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ResNet-18 fp32 images/s bs64 at 1/2/4/8 B200; Conv/GEMM % of TF32 tensor peak"
+UNIT = "images/s"
+BATCH = 64
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "1xtf32"])
+    return p.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ---- reference CPU leg (oracle/_ref, the reference's own CpuDevice) ----------
+
+_REF = None
+
+
+def _ref_worker_init(onnx_path, batch):
+    global _REF
+    from oracle import ref
+
+    _REF = ref.RefModel(onnx_path, {"input": [batch, 3, 224, 224]})
+
+
+def _ref_worker_run(seed):
+    import numpy as np
+
+    from nert_b200 import synth
+
+    x = synth.uniform((1, 3, 224, 224), -1.0, 1.0, seed)
+    t0 = time.perf_counter()
+    _REF.run({"input": x.astype(np.float32)})
+    return time.perf_counter() - t0
+
+
+class RefPool:
+    """One spawned process per core, each holding the reference Model (b1)."""
+
+    def __init__(self, cores: int):
+        import multiprocessing as mp
+
+        from nert_b200 import configs, onnx_io
+
+        self.tmp = tempfile.TemporaryDirectory()
+        path = onnx_io.save(configs.resnet18(1), os.path.join(self.tmp.name, "resnet18_b1.onnx"))
+        self.cores = cores
+        self.pool = mp.get_context("spawn").Pool(cores, initializer=_ref_worker_init, initargs=(path, 1))
+
+    def step(self) -> float:
+        """P images in parallel; returns wall seconds."""
+        t0 = time.perf_counter()
+        self.pool.map(_ref_worker_run, list(range(self.cores)), chunksize=1)
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+        self.tmp.cleanup()
+
+
+def ref_cores() -> int:
+    return max(1, min(os.cpu_count() or 1, 8))
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import ref
+
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnert_ref.so was not built"}))
+        return 0
+    cores = ref_cores()
+    pool = RefPool(cores)
+    try:
+        for _ in range(max(0, args.warmup)):
+            pool.step()
+        walls = [pool.step() for _ in range(args.steps)]
+    finally:
+        pool.close()
+    total = sum(walls)
+    value = cores * args.steps / total
+    sample = f"{cores} ResNet-18 images per step (batch 1 each, one process per core) of the bs{args.batch} workload"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 accumulation)",
+        "data": "synthetic (seeded U[-1,1] input, Kaiming weights, BN folded)",
+        "config": {"workload": "resnet18", "model": "resnet18", "per_gpu_batch": args.batch,
+                   "global_batch": args.batch * args.gpus, "image": [3, 224, 224], "device": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- clocks --------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.split(", ") for r in self.out.read().strip().splitlines() if r.strip()]
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[0]))
+                mx = float(r[1])
+                for nm, v in zip(names, r[4:8]):
+                    if v.strip() == "Active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- roofline helpers ------------------------------------------------------------
+
+def measure_tf32_peak() -> float:
+    """Dense TF32 TFLOP/s of a library GEMM (torch/cuBLAS, 8192^3, best of 10)."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        n = 8192
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        for _ in range(3):
+            torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = 1e9
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            torch.matmul(a, b)
+            e.record()
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+# ---- B200 leg ------------------------------------------------------------------------
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank, world, local = dist_env()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import ref
+
+        if ref.available():
+            cpu = {"pool": RefPool(ref_cores())}  # spawned before the first GPU call
+
+    import numpy as np
+    import torch
+
+    if args.precision == "1xtf32":
+        os.environ["NERT_B200_PRECISION"] = "1xtf32"
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+
+    from nert_b200 import configs
+    from nert_b200 import model as nbm
+
+    batch = args.batch
+    graph = configs.resnet18(batch)
+    m = nbm.Model(graph, {"input": [batch, 3, 224, 224]}, device=local)
+    stats = m.stats()
+    x = configs.resnet_input(batch)
+    h_in = nbm.HostBuffer(x.shape)
+    h_in.array[...] = x
+    out_shape = m.outputs[0]["shape"]
+    h_out = nbm.HostBuffer(out_shape)
+    m.run_into([h_in.ptr], [h_out.ptr])  # stages the input, captures the CUDA graph
+
+    stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > 126 MB L2
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def timed(fn, steps):
+        evs = []
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                fn()
+                e.record(stream)
+                evs.append((s, e))
+        torch.cuda.synchronize()
+        stream.synchronize()
+        return [s.elapsed_time(e) for s, e in evs]
+
+    def run_device():
+        m.launch()
+
+    def run_e2e():
+        m.run_async([h_in.ptr], [h_out.ptr])
+
+    # warm-up
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            m.launch()
+            m.run_async([h_in.ptr], [h_out.ptr])
+    m.synchronize()
+    torch.cuda.synchronize()
+
+    # device-resident timed region
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    dev_ms = timed(run_device, args.steps)
+    m.synchronize()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    e2e_ms = timed(run_e2e, args.steps)
+    m.synchronize()
+    barrier()
+
+    mean_dev = sum(dev_ms) / len(dev_ms)
+    mean_e2e = sum(e2e_ms) / len(e2e_ms)
+    if dist is not None:
+        t = torch.tensor([mean_dev, mean_e2e], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mean_dev, mean_e2e = float(t[0]), float(t[1])
+
+    # roofline of the tensor-core contraction kernel (one eager pass per repeat)
+    analysis = nbm.analyze(graph, {"input": [batch, 3, 224, 224]})
+    tensors = analysis["tensors"]
+    conv_flops = {}
+    for e in analysis["exec"]:
+        if e["op"] in ("Conv", "Gemm"):
+            y = tensors[e["outs"][0]]["dims"]
+            w = graph.initializers[graph_node(graph, e["name"]).inputs[1]]
+            if e["op"] == "Conv":
+                k = int(np.prod(w.shape[1:]))
+                conv_flops[e["name"]] = 2.0 * float(np.prod(y)) * k
+            else:
+                k = w.shape[1] if graph_node(graph, e["name"]).attrs.get("transB", 0) else w.shape[0]
+                conv_flops[e["name"]] = 2.0 * float(np.prod(y)) * k
+    sums = {}
+    for _ in range(3):
+        for label, ms in m.profile():
+            sums[label] = sums.get(label, 0.0) + ms / 3
+    tc_time = sum(ms for lab, ms in sums.items() if lab.split(":", 1)[1] in conv_flops)
+    tc_flop = sum(conv_flops.values())
+    total_prof = sum(sums.values())
+    achieved = tc_flop / (tc_time * 1e-3) / 1e12 if tc_time > 0 else None
+
+    line = None
+    if rank == 0:
+        tf32 = measure_tf32_peak()
+        peak = tf32 / 3.0
+        line = {
+            "metric": METRIC,
+            "value": world * batch / (mean_dev * 1e-3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": mean_dev,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32 (3xTF32 tensor-core contractions, fp32 accumulate)" if args.precision == "3xtf32"
+            else "f32 (1xTF32 contractions, opt-in)",
+            "data": "synthetic (seeded U[-1,1] input, Kaiming weights, BN folded)",
+            "config": {"workload": "resnet18", "model": "resnet18", "per_gpu_batch": batch,
+                       "global_batch": batch * world, "image": [3, 224, 224], "parallelism": f"replicas{world}",
+                       "l2": "flushed (256 MB write) between timed steps, outside the step events",
+                       "precision": args.precision, "cuda_graph": True,
+                       "fused_groups": stats["fused_groups"], "rows_per_run": stats["exec_nodes"]},
+            "e2e": {"value": world * batch / (mean_e2e * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(np.prod(out_shape) * 4),
+                    "ms_per_step": mean_e2e},
+            "roofline": {"bound": "tensor", "kernel": "igemm_kernel (tcgen05 implicit-GEMM Conv/Gemm)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved else None,
+                         "peak_note": f"measured TF32 dense {tf32:.1f} TFLOP/s (torch TF32 GEMM 8192^3) / 3 = "
+                                      f"3xTF32-effective",
+                         "frac_of_tf32_dense": (achieved / tf32) if achieved else None,
+                         "flops_per_step": tc_flop, "kernel_ms_per_step": tc_time,
+                         "share_of_step": tc_time / total_prof if total_prof else None,
+                         "traffic": None},
+            "clocks": clk,
+            "gpu_launches": int(stats["kernels_per_run"]) * args.steps,
+        }
+    del flush
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+    if rank == 0 and cpu is not None:
+        pool = cpu["pool"]
+        try:
+            pool.step()  # warm
+            walls = [pool.step() for _ in range(2)]
+        finally:
+            pool.close()
+        v = pool.cores * len(walls) / sum(walls)
+        line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": pool.cores, "kind": "reference",
+                                "sample": f"2 x {pool.cores} ResNet-18 images (batch 1, one process per core)"}
+    elif rank == 0:
+        line["cpu_baseline"] = None
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def graph_node(graph, name):
+    for n in graph.nodes:
+        if n.name == name:
+            return n
+    raise KeyError(name)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

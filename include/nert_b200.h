@@ -147,6 +147,90 @@ int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], floa
 /* Mean over the trailing `inner` elements of `rows` rows, double accumulation
  * (GlobalAveragePool, src/kernels/global_average_pool.cpp:32-68). */
 int nb2_row_mean(nb2_device* dev, const float* x, int64_t rows, int64_t inner, float* y);
+/* Softmax over the middle axis of an [outer, len, inner] view
+ * (src/kernels/softmax.cpp:47-120). */
+int nb2_softmax(nb2_device* dev, const float* x, float* y, int64_t outer, int64_t len, int64_t inner);
+/* LayerNormalization over rows of length d (src/kernels/layer_normalization.cpp:77-160);
+ * bias, mean and inv_std may be null. */
+int nb2_layernorm(nb2_device* dev, const float* x, const float* scale, const float* bias, float* y, float* mean,
+                  float* inv_std, int64_t rows, int64_t d, float epsilon);
+/* Transpose (src/kernels/transpose.cpp:54): y = permute(x, perm); elem_bytes 1, 4 or 8. */
+int nb2_transpose(nb2_device* dev, const void* x, void* y, const int64_t* dims, const int64_t* perm, int rank,
+                  int elem_bytes);
+/* Concat / Split (src/kernels/concat.cpp:64, split.cpp:65) as one launch:
+ * `parts` blocks of parts_len[i]*inner elements per outer row. concat=1
+ * gathers parts[] into whole, concat=0 scatters whole into parts[]. */
+int nb2_concat_split(nb2_device* dev, int concat, void* whole, void* const* parts, const int64_t* parts_len,
+                     int n_parts, int64_t outer, int64_t inner, int elem_bytes);
+/* Slice (src/kernels/slice.cpp) with resolved per-axis starts and steps. */
+int nb2_slice(nb2_device* dev, const void* x, void* y, const int64_t* in_dims, const int64_t* out_dims,
+              const int64_t* starts, const int64_t* steps, int rank, int elem_bytes);
+/* Gather (src/kernels/gather.cpp:49-129) on an [outer, axis_len, inner] view
+ * with int64 indices; out-of-range indices surface as NB2_ERR_DEVICE at the
+ * next synchronisation (no device trap). */
+int nb2_gather(nb2_device* dev, const void* x, const int64_t* indices, void* y, int64_t outer, int64_t axis_len,
+               int64_t inner, int64_t n_indices, int elem_bytes);
+/* TopK largest/sorted along the last axis of [rows, len] (src/kernels/top_k.cpp:53-142):
+ * values and int64 indices ordered by (value desc, index asc); k <= 1024. */
+int nb2_topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t len, int64_t k);
+/* Resize nearest/linear (src/kernels/resize.cpp:162-): mode 0 nearest, 1 linear;
+ * transform 0 half_pixel, 1 pytorch_half_pixel, 2 align_corners, 3 asymmetric;
+ * nearest_mode 0 round_prefer_floor, 1 round_prefer_ceil, 2 floor, 3 ceil.
+ * `scales` are the per-axis factors of the coordinate transform. */
+int nb2_resize(nb2_device* dev, const void* x, void* y, const int64_t* in_dims, const int64_t* out_dims,
+               const double* scales, int rank, int mode, int transform, int nearest_mode, int dtype);
+/* Cast between NB2_F32 / NB2_I64 / NB2_BOOL (float -> int64 truncates). */
+int nb2_cast(nb2_device* dev, const void* x, int from_dtype, void* y, int to_dtype, int64_t count);
+
+/* ---- engine: whole graphs ------------------------------------------------ */
+
+/* One ONNX graph bound to one GPU and one concrete input shape: the B200
+ * counterpart of nert::Model (include/nert/executor.hpp:57-122,
+ * src/executor.cpp:202-560). Construction parses the ONNX bytes, infers
+ * shapes, fuses Conv/Gemm/MatMul epilogues (Relu, residual Add, SiLU, bias),
+ * plans one arena, uploads weights once (Conv/Gemm weights pre-split for the
+ * tensor cores) and allocates every device buffer; a run allocates nothing.
+ * Errors: NB2_ERR_INVALID for a graph the engine cannot run (unknown op,
+ * unsupported form), NB2_ERR_DEVICE for a device-recorded run-time error. */
+typedef struct nb2_model nb2_model;
+
+#define NB2_MODEL_NO_FUSION 1 /* run every node as its own row */
+#define NB2_MODEL_NO_GRAPH 2  /* launch rows one by one instead of a CUDA-graph replay */
+
+int nb2_model_create(const void* onnx, int64_t size, int n_inputs, const char* const* input_names,
+                     const int64_t* dims_flat, const int* ranks, int ordinal, int flags, nb2_model** out);
+int nb2_model_destroy(nb2_model* m);
+int nb2_model_num_io(const nb2_model* m, int* n_inputs, int* n_outputs);
+/* name / dtype (NB2_F32, NB2_I64, NB2_BOOL) / dims (up to 8) / device buffer
+ * of input or output i. */
+int nb2_model_io(const nb2_model* m, int is_output, int i, const char** name, int* dtype, int* rank, int64_t* dims8,
+                 void** device_ptr);
+/* End to end (Model::Run): copy every input from host memory (pinned memory
+ * from nb2_host_alloc makes the copies asynchronous), run, copy every output
+ * back, synchronise. Inputs/outputs in declaration order. */
+int nb2_model_run(nb2_model* m, const void* const* host_inputs, void* const* host_outputs);
+/* nb2_model_run without the final synchronise (host buffers must stay valid
+ * until nb2_model_synchronize returns). */
+int nb2_model_run_async(nb2_model* m, const void* const* host_inputs, void* const* host_outputs);
+/* Device-resident run: the inputs are already in the model's input buffers
+ * (nb2_model_io); returns once the work is queued. */
+int nb2_model_launch(nb2_model* m);
+int nb2_model_synchronize(nb2_model* m);
+int nb2_model_stats(const nb2_model* m, int64_t* kernels_per_run, int64_t* arena_bytes, int64_t* weight_bytes,
+                    int64_t* fused_groups, int64_t* exec_nodes);
+/* One eager pass with a CUDA event between rows: per-row labels
+ * (label_len bytes each) and milliseconds; *count = number of rows. */
+int nb2_model_profile(nb2_model* m, int max_steps, char* labels, int label_len, float* ms, int* count);
+int nb2_model_stream(const nb2_model* m, void** stream);
+
+/* Host-only planning (no GPU needed): shapes, fused row list and arena plan
+ * of a graph as JSON; *needed is the byte size including the terminator. */
+int nb2_graph_analyze(const void* onnx, int64_t size, int n_inputs, const char* const* input_names,
+                      const int64_t* dims_flat, const int* ranks, int flags, char* buf, int64_t cap, int64_t* needed);
+
+/* Pinned host memory for inputs/outputs that cross PCIe every run. */
+int nb2_host_alloc(int64_t bytes, void** out);
+int nb2_host_free(void* p);
 
 #ifdef __cplusplus
 }

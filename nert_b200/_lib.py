@@ -61,6 +61,18 @@ _SIGS = {
                                   vp, c_i64p, ctypes.c_int]),
     "nb2_maxpool2d": (ctypes.c_int, [vp, vp, c_i64p, vp, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p]),
     "nb2_row_mean": (ctypes.c_int, [vp, vp, ctypes.c_int64, ctypes.c_int64, vp]),
+    "nb2_softmax": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+    "nb2_layernorm": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_float]),
+    "nb2_transpose": (ctypes.c_int, [vp, vp, vp, c_i64p, c_i64p, ctypes.c_int, ctypes.c_int]),
+    "nb2_concat_split": (ctypes.c_int, [vp, ctypes.c_int, vp, ctypes.POINTER(vp), c_i64p, ctypes.c_int,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int]),
+    "nb2_slice": (ctypes.c_int, [vp, vp, vp, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_int, ctypes.c_int]),
+    "nb2_gather": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_int]),
+    "nb2_topk": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
+    "nb2_resize": (ctypes.c_int, [vp, vp, vp, c_i64p, c_i64p, ctypes.POINTER(ctypes.c_double), ctypes.c_int,
+                                  ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "nb2_cast": (ctypes.c_int, [vp, vp, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int64]),
 }
 
 _lib = None

@@ -4,6 +4,8 @@
 #include "../../include/nert_b200.h"
 #include "igemm.cuh"
 #include "ops.cuh"
+#include "ops_move.cuh"
+#include "ops_norm.cuh"
 #include "runtime.hpp"
 
 #include <algorithm>
@@ -410,6 +412,120 @@ int nb2_row_mean(nb2_device* dev, const float* x, int64_t rows, int64_t inner, f
         need(rows == 0 || (x != nullptr && y != nullptr), "mean: null buffer");
         bind(dev);
         row_mean(dev, x, y, rows, inner);
+    });
+}
+
+int nb2_softmax(nb2_device* dev, const float* x, float* y, int64_t outer, int64_t len, int64_t inner) {
+    return guard([&] {
+        need(outer >= 0 && len >= 0 && inner >= 0, "Softmax: negative extent");
+        need(outer * len * inner == 0 || (x != nullptr && y != nullptr), "Softmax: null buffer");
+        bind(dev);
+        softmax(dev, x, y, outer, len, inner);
+    });
+}
+
+int nb2_layernorm(nb2_device* dev, const float* x, const float* scale, const float* bias, float* y, float* mean,
+                  float* inv_std, int64_t rows, int64_t d, float epsilon) {
+    return guard([&] {
+        need(rows >= 0 && d > 0, "LayerNormalization: bad extents");
+        need(rows == 0 || (x != nullptr && scale != nullptr && y != nullptr), "LayerNormalization: null buffer");
+        bind(dev);
+        layernorm(dev, x, scale, bias, y, mean, inv_std, rows, d, epsilon);
+    });
+}
+
+int nb2_transpose(nb2_device* dev, const void* x, void* y, const int64_t* dims, const int64_t* perm, int rank,
+                  int elem_bytes) {
+    return guard([&] {
+        need(rank >= 0 && rank <= 8, "Transpose: rank must be 0..8");
+        need(elem_bytes == 1 || elem_bytes == 4 || elem_bytes == 8, "Transpose: element size must be 1, 4 or 8");
+        std::vector<int64_t> d(dims, dims + rank), p(perm, perm + rank);
+        std::vector<bool> seen(static_cast<size_t>(rank), false);
+        for (int64_t a : p) {
+            need(a >= 0 && a < rank && !seen[static_cast<size_t>(a)], "Transpose: perm is not a permutation");
+            seen[static_cast<size_t>(a)] = true;
+        }
+        bind(dev);
+        transpose(dev, x, y, d, p, elem_bytes);
+    });
+}
+
+int nb2_concat_split(nb2_device* dev, int concat, void* whole, void* const* parts, const int64_t* parts_len,
+                     int n_parts, int64_t outer, int64_t inner, int elem_bytes) {
+    return guard([&] {
+        need(n_parts > 0 && outer >= 0 && inner >= 0 && elem_bytes > 0, "Concat/Split: bad extents");
+        int64_t total = 0;
+        for (int i = 0; i < n_parts; ++i) {
+            need(parts_len[i] >= 0, "Concat/Split: negative part length");
+            total += parts_len[i];
+        }
+        const int64_t pitch = total * inner * elem_bytes;
+        std::vector<CopySeg> segs;
+        int64_t at = 0;
+        for (int i = 0; i < n_parts; ++i) {
+            const int64_t rb = parts_len[i] * inner * elem_bytes;
+            auto* w = static_cast<uint8_t*>(whole) + at;
+            auto* p = static_cast<uint8_t*>(parts[i]);
+            segs.push_back(concat ? CopySeg{p, w, rb, pitch, rb, outer} : CopySeg{w, p, pitch, rb, rb, outer});
+            at += rb;
+        }
+        bind(dev);
+        segment_copy(dev, segs);
+    });
+}
+
+int nb2_slice(nb2_device* dev, const void* x, void* y, const int64_t* in_dims, const int64_t* out_dims,
+              const int64_t* starts, const int64_t* steps, int rank, int elem_bytes) {
+    return guard([&] {
+        need(rank >= 1 && rank <= 8, "Slice: rank must be 1..8");
+        bind(dev);
+        slice(dev, x, y, std::vector<int64_t>(in_dims, in_dims + rank), std::vector<int64_t>(out_dims, out_dims + rank),
+              std::vector<int64_t>(starts, starts + rank), std::vector<int64_t>(steps, steps + rank), elem_bytes);
+    });
+}
+
+int nb2_gather(nb2_device* dev, const void* x, const int64_t* indices, void* y, int64_t outer, int64_t axis_len,
+               int64_t inner, int64_t n_indices, int elem_bytes) {
+    return guard([&] {
+        need(outer >= 0 && axis_len >= 0 && inner >= 0 && n_indices >= 0, "Gather: negative extent");
+        bind(dev);
+        gather(dev, x, indices, y, outer, axis_len, inner, n_indices, elem_bytes);
+    });
+}
+
+int nb2_topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t len, int64_t k) {
+    return guard([&] {
+        need(rows >= 0 && len >= 0 && k >= 0, "TopK: negative extent");
+        need(k <= len, "TopK: K is larger than the axis");
+        bind(dev);
+        topk(dev, x, values, indices, rows, len, k);
+    });
+}
+
+int nb2_resize(nb2_device* dev, const void* x, void* y, const int64_t* in_dims, const int64_t* out_dims,
+               const double* scales, int rank, int mode, int transform, int nearest_mode, int dtype) {
+    return guard([&] {
+        need(rank >= 1 && rank <= 8, "Resize: rank must be 1..8");
+        need(mode == 0 || mode == 1, "Resize: mode must be nearest (0) or linear (1)");
+        need(transform >= 0 && transform <= 3 && nearest_mode >= 0 && nearest_mode <= 3, "Resize: unknown mode");
+        need(dtype == NB2_F32 || (dtype == NB2_I64 && mode == 0), "Resize: tensors must be float32 (or int64 for nearest)");
+        std::vector<int64_t> in(in_dims, in_dims + rank), out(out_dims, out_dims + rank);
+        for (int d = 0; d < rank; ++d) {
+            need(in[d] > 0 && out[d] > 0, "Resize: non-positive dimension");
+        }
+        bind(dev);
+        void* tables = dev->scratch(resize_table_bytes(out));
+        resize_on_device_tables(dev, x, y, in, out, std::vector<double>(scales, scales + rank), mode, transform,
+                                nearest_mode, dtype == NB2_F32, tables);
+    });
+}
+
+int nb2_cast(nb2_device* dev, const void* x, int from_dtype, void* y, int to_dtype, int64_t count) {
+    return guard([&] {
+        need(from_dtype >= 0 && from_dtype <= 2 && to_dtype >= 0 && to_dtype <= 2, "Cast: unknown dtype");
+        need(count >= 0, "Cast: negative count");
+        bind(dev);
+        cast(dev, x, from_dtype, y, to_dtype, count);
     });
 }
 

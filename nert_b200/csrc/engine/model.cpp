@@ -1,0 +1,920 @@
+// B200 engine Model: fusion peephole, arena planning, weight residency and
+// packing, and CUDA-graph execution (see model.hpp).
+
+#include "model.hpp"
+
+#include "../igemm.cuh"
+#include "../ops.cuh"
+#include "../ops_move.cuh"
+#include "../ops_norm.cuh"
+
+#include <algorithm>
+#include <cstring>
+#include <list>
+#include <set>
+
+namespace nb2 {
+namespace eng {
+
+namespace {
+
+constexpr int64_t kAlign = 256;
+
+int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// One executable unit after fusion: a node, or a Conv/Gemm/MatMul that
+// absorbed its epilogue consumers.
+struct ExecNode {
+    const Node* node = nullptr;
+    std::string op;
+    std::vector<std::string> ins;  // every tensor read (for liveness)
+    std::vector<std::string> outs; // tensors produced
+    std::string out;               // the fused group's visible output (outs[0] for plain nodes)
+    std::string residual;          // fused residual Add operand
+    std::string bias;              // fused MatMul bias (Add of a constant [N])
+    int act = kActNone;
+    int pos = 0;
+    bool alias = false; // output is a view of input 0
+    int group = 1;      // nodes in the group
+};
+
+bool is_alias_op(const std::string& op) {
+    return op == "Flatten" || op == "Reshape" || op == "Squeeze" || op == "Unsqueeze" || op == "Identity";
+}
+
+std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInfo>& shapes, bool enable,
+                           int64_t& fused_groups) {
+    std::map<std::string, std::vector<int>> consumers;
+    for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+        for (const auto& in : g.nodes[i].inputs) {
+            if (!in.empty()) {
+                consumers[in].push_back(i);
+            }
+        }
+    }
+    std::set<std::string> outputs;
+    for (const auto& o : g.outputs) {
+        outputs.insert(o.first);
+    }
+    std::vector<bool> absorbed(g.nodes.size(), false);
+    // the single, not yet fused consumer of `t` (t not a graph output), else -1
+    auto single = [&](const std::string& t) -> int {
+        if (outputs.count(t)) {
+            return -1;
+        }
+        auto it = consumers.find(t);
+        if (it == consumers.end() || it->second.size() != 1 || absorbed[it->second[0]]) {
+            return -1;
+        }
+        return it->second[0];
+    };
+    std::vector<ExecNode> list;
+    fused_groups = 0;
+    for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+        if (absorbed[i]) {
+            continue;
+        }
+        const Node& n = g.nodes[i];
+        ExecNode e;
+        e.node = &n;
+        e.op = n.op;
+        e.pos = i;
+        for (const auto& in : n.inputs) {
+            if (!in.empty()) {
+                e.ins.push_back(in);
+            }
+        }
+        e.outs = n.outputs;
+        e.out = n.outputs.empty() ? "" : n.outputs[0];
+        e.alias = is_alias_op(n.op);
+        const bool mm_const_b = n.op == "MatMul" && g.constants.count(n.inputs[1]) &&
+                                g.constants.at(n.inputs[1]).dims.size() == 2 &&
+                                shapes.at(n.inputs[0]).dims.size() >= 2;
+        if (enable && (n.op == "Conv" || n.op == "Gemm" || mm_const_b)) {
+            std::string cur = e.out;
+            if (mm_const_b) {
+                const int j = single(cur);
+                if (j >= 0 && g.nodes[j].op == "Add") {
+                    const Node& a = g.nodes[j];
+                    const std::string other = a.inputs[0] == cur ? a.inputs[1] : a.inputs[0];
+                    const int64_t N = g.constants.at(n.inputs[1]).dims[1];
+                    auto c = g.constants.find(other);
+                    if (c != g.constants.end() && c->second.dtype == DType::F32 && c->second.count() == N &&
+                        shapes.at(a.outputs[0]).dims == shapes.at(cur).dims) {
+                        e.bias = other;
+                        e.ins.push_back(other);
+                        absorbed[j] = true;
+                        e.pos = j;
+                        e.group++;
+                        cur = a.outputs[0];
+                    }
+                }
+            }
+            int j = single(cur);
+            if (j >= 0 && g.nodes[j].op == "Add") {
+                const Node& a = g.nodes[j];
+                const std::string other = a.inputs[0] == cur ? a.inputs[1] : a.inputs[0];
+                if (other != cur && shapes.at(other).dims == shapes.at(cur).dims &&
+                    shapes.at(other).dtype == DType::F32) {
+                    e.residual = other;
+                    e.ins.push_back(other);
+                    absorbed[j] = true;
+                    e.pos = j;
+                    e.group++;
+                    cur = a.outputs[0];
+                    j = single(cur);
+                }
+            }
+            if (j >= 0 && g.nodes[j].op == "Relu") {
+                e.act = kActRelu;
+                absorbed[j] = true;
+                e.pos = j;
+                e.group++;
+                cur = g.nodes[j].outputs[0];
+            } else if (!outputs.count(cur) && consumers.count(cur) && consumers[cur].size() == 2) {
+                // SiLU: Sigmoid(cur) feeding only Mul(cur, sigmoid)
+                const int c0 = consumers[cur][0], c1 = consumers[cur][1];
+                const int s = g.nodes[c0].op == "Sigmoid" ? c0 : g.nodes[c1].op == "Sigmoid" ? c1 : -1;
+                const int m = s == c0 ? c1 : c0;
+                if (s >= 0 && g.nodes[m].op == "Mul" && !absorbed[s] && !absorbed[m]) {
+                    const std::string sig = g.nodes[s].outputs[0];
+                    const Node& mul = g.nodes[m];
+                    const bool pair = (mul.inputs[0] == cur && mul.inputs[1] == sig) ||
+                                      (mul.inputs[1] == cur && mul.inputs[0] == sig);
+                    if (pair && single(sig) == m && m > s) {
+                        e.act = kActSilu;
+                        absorbed[s] = absorbed[m] = true;
+                        e.pos = m;
+                        e.group += 2;
+                        cur = mul.outputs[0];
+                    }
+                }
+            }
+            if (e.group > 1) {
+                ++fused_groups;
+                e.out = cur;
+                e.outs = {cur};
+            }
+        }
+        list.push_back(std::move(e));
+    }
+    std::stable_sort(list.begin(), list.end(), [](const ExecNode& a, const ExecNode& b) { return a.pos < b.pos; });
+    return list;
+}
+
+ConvGeom conv_geom(const Node& n, const TensorInfo& x, const TensorInfo& w, const TensorInfo& y) {
+    const bool one_d = x.dims.size() == 3;
+    ConvGeom g{};
+    g.N = x.dims[0];
+    g.C = x.dims[1];
+    g.H = one_d ? 1 : x.dims[2];
+    g.W = one_d ? x.dims[2] : x.dims[3];
+    g.M = w.dims[0];
+    g.KH = one_d ? 1 : w.dims[2];
+    g.KW = one_d ? w.dims[2] : w.dims[3];
+    g.OH = one_d ? 1 : y.dims[2];
+    g.OW = one_d ? y.dims[2] : y.dims[3];
+    const size_t r = x.dims.size() - 2;
+    std::vector<int64_t> s = n.getints("strides"), d = n.getints("dilations"), pads = n.getints("pads");
+    if (s.empty()) {
+        s.assign(r, 1);
+    }
+    if (d.empty()) {
+        d.assign(r, 1);
+    }
+    std::vector<int64_t> pb(r, 0);
+    const std::string ap = n.gets("auto_pad", "NOTSET");
+    std::vector<int64_t> in_sp(x.dims.begin() + 2, x.dims.end()), k(w.dims.begin() + 2, w.dims.end());
+    for (size_t i = 0; i < r; ++i) {
+        if (ap == "SAME_UPPER" || ap == "SAME_LOWER") {
+            const int64_t out = (in_sp[i] + s[i] - 1) / s[i];
+            const int64_t total = std::max<int64_t>(0, (out - 1) * s[i] + d[i] * (k[i] - 1) + 1 - in_sp[i]);
+            pb[i] = ap == "SAME_UPPER" ? total / 2 : total - total / 2;
+        } else if (ap != "VALID" && !pads.empty()) {
+            pb[i] = pads[i];
+        }
+    }
+    g.sh = one_d ? 1 : s[0];
+    g.sw = one_d ? s[0] : s[1];
+    g.dh = one_d ? 1 : d[0];
+    g.dw = one_d ? d[0] : d[1];
+    g.ph = one_d ? 0 : pb[0];
+    g.pw = one_d ? pb[0] : pb[1];
+    g.group = n.geti("group", 1);
+    if (g.group <= 0 || g.C % g.group != 0 || g.M % g.group != 0 || w.dims[1] != g.C / g.group) {
+        throw LoadError(n.where() + ": weight channel dimension does not match input/group");
+    }
+    return g;
+}
+
+} // namespace
+
+Model::Model(const uint8_t* onnx, size_t size, const std::map<std::string, std::vector<int64_t>>& input_dims,
+             int ordinal, int flags)
+    : dev_(nb2::device(ordinal)), g_(parse_onnx(onnx, size)) {
+    dev_->make_current();
+    try {
+        build(input_dims, flags);
+    } catch (...) {
+        if (exec_) {
+            cudaGraphExecDestroy(exec_);
+            exec_ = nullptr;
+        }
+        cudaStreamSynchronize(dev_->stream);
+        for (void* p : allocations_) {
+            cudaFree(p);
+        }
+        allocations_.clear();
+        throw;
+    }
+}
+
+Model::~Model() {
+    cudaSetDevice(dev_->ordinal);
+    if (exec_) {
+        cudaGraphExecDestroy(exec_);
+    }
+    cudaStreamSynchronize(dev_->stream);
+    for (void* p : allocations_) {
+        cudaFree(p);
+    }
+}
+
+namespace {
+
+// Host-only half of Model construction: shapes, fusion, liveness and the
+// arena plan. Needs no GPU (nb2_graph_analyze exposes it for tests).
+struct PlanResult {
+    std::map<std::string, TensorInfo> shapes;
+    std::vector<ExecNode> ex;
+    std::map<std::string, std::string> root;
+    std::map<std::string, int64_t> offset;
+    std::map<std::string, int> last_use;
+    int64_t arena = 0;
+    int64_t fused_groups = 0;
+};
+
+PlanResult plan_graph(const Graph& g_, const std::map<std::string, std::vector<int64_t>>& input_dims, int flags) {
+    PlanResult pr;
+    pr.shapes = infer_shapes(g_, input_dims);
+    const auto& shapes_ = pr.shapes;
+    std::vector<ExecNode>& ex = pr.ex;
+    ex = fuse(g_, shapes_, (flags & kNoFusion) == 0, pr.fused_groups);
+
+    // ---- liveness over the fused list (aliases share their root's buffer)
+    std::map<std::string, std::string> root;
+    auto root_of = [&](const std::string& t) -> std::string {
+        auto it = root.find(t);
+        return it == root.end() ? t : it->second;
+    };
+    std::set<std::string> graph_inputs, graph_outputs;
+    for (const auto& in : g_.inputs) {
+        graph_inputs.insert(in.first);
+    }
+    for (const auto& o : g_.outputs) {
+        graph_outputs.insert(o.first);
+    }
+    const int n_exec = static_cast<int>(ex.size());
+    std::map<std::string, int> last_use;
+    for (int i = 0; i < n_exec; ++i) {
+        if (ex[i].alias) {
+            root[ex[i].out] = root_of(ex[i].ins[0]);
+        }
+        for (const auto& in : ex[i].ins) {
+            last_use[root_of(in)] = i;
+        }
+    }
+    for (const auto& o : graph_outputs) {
+        last_use[root_of(o)] = n_exec + 1;
+    }
+
+    // ---- arena plan: first fit over live blocks, outputs placed before the
+    // node's dying inputs are released (an output never aliases its inputs).
+    std::map<std::string, int64_t> offset;
+    std::list<std::pair<int64_t, std::pair<int64_t, std::string>>> live; // offset -> (size, root)
+    int64_t arena = 0;
+    auto place = [&](const std::string& t, int64_t bytes) {
+        bytes = align_up(std::max<int64_t>(bytes, 1));
+        int64_t at = 0;
+        auto it = live.begin();
+        for (; it != live.end(); ++it) {
+            if (it->first - at >= bytes) {
+                break;
+            }
+            at = std::max(at, it->first + it->second.first);
+        }
+        live.insert(it, {at, {bytes, t}});
+        offset[t] = at;
+        arena = std::max(arena, at + bytes);
+    };
+    for (int i = 0; i < n_exec; ++i) {
+        if (!ex[i].alias) {
+            for (const auto& o : ex[i].outs) {
+                if (o.empty() || graph_inputs.count(o) || g_.constants.count(o)) {
+                    continue;
+                }
+                const TensorInfo& ti = shapes_.at(o);
+                place(o, numel(ti.dims) * dtype_size(ti.dtype));
+            }
+        }
+        for (auto it = live.begin(); it != live.end();) {
+            const std::string& r = it->second.second;
+            auto lu = last_use.find(r);
+            const int until = lu == last_use.end() ? i : lu->second;
+            if (until <= i) {
+                it = live.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
+    pr.root = root;
+    pr.offset = offset;
+    pr.last_use = last_use;
+    pr.arena = arena;
+    return pr;
+}
+
+} // namespace
+
+void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims, int flags) {
+    use_graph_ = (flags & kNoGraph) == 0;
+    PlanResult pr = plan_graph(g_, input_dims, flags);
+    shapes_ = pr.shapes;
+    fused_groups_ = pr.fused_groups;
+    const std::vector<ExecNode>& ex = pr.ex;
+    const std::map<std::string, std::string>& root = pr.root;
+    auto root_of = [&](const std::string& t) -> std::string {
+        auto it = root.find(t);
+        return it == root.end() ? t : it->second;
+    };
+    const std::map<std::string, int64_t>& offset = pr.offset;
+    arena_bytes_ = pr.arena;
+
+    // ---- device buffers: arena, graph inputs, constants, packed weights
+    auto dmalloc = [&](int64_t bytes) -> uint8_t* {
+        if (bytes <= 0) {
+            return nullptr;
+        }
+        void* p = nullptr;
+        if (cudaMalloc(&p, static_cast<size_t>(bytes)) != cudaSuccess) {
+            cudaGetLastError();
+            throw RunError("executor: could not allocate " + std::to_string(bytes) + " bytes on the device");
+        }
+        allocations_.push_back(p);
+        return static_cast<uint8_t*>(p);
+    };
+    uint8_t* arena_ptr = dmalloc(arena_bytes_);
+    std::map<std::string, void*> ptr;
+    for (const auto& in : g_.inputs) {
+        const TensorInfo& ti = shapes_.at(in.first);
+        IOInfo io{in.first, ti.dtype, ti.dims, nullptr, numel(ti.dims) * dtype_size(ti.dtype)};
+        io.dev = dmalloc(align_up(io.bytes));
+        ptr[in.first] = io.dev;
+        inputs_.push_back(io);
+    }
+    // constants read by kernels as data (not shape operands, not packed weights)
+    std::set<std::string> packed_conv, packed_gemm, raw_needed;
+    for (const auto& e : ex) {
+        const Node& n = *e.node;
+        auto data_in = [&](size_t i) {
+            if (i < n.inputs.size() && g_.constants.count(n.inputs[i])) {
+                raw_needed.insert(n.inputs[i]);
+            }
+        };
+        if (e.op == "Conv") {
+            if (g_.constants.count(n.inputs[1])) {
+                packed_conv.insert(n.inputs[1]);
+            } else {
+                data_in(1);
+            }
+            data_in(0);
+            data_in(2);
+        } else if (e.op == "Gemm" || e.op == "MatMul") {
+            data_in(0);
+            if (g_.constants.count(n.inputs[1])) {
+                packed_gemm.insert(n.inputs[1]);
+            }
+            data_in(2);
+            data_in(1); // raw copy also kept (simple; weights are small next to 180 GB)
+        } else if (e.op == "Reshape" || e.op == "Squeeze" || e.op == "Unsqueeze" || e.op == "Split" ||
+                   e.op == "Slice" || e.op == "TopK" || e.op == "Resize" || e.op == "ReduceMean") {
+            data_in(0);
+        } else {
+            for (size_t i = 0; i < n.inputs.size(); ++i) {
+                data_in(i);
+            }
+        }
+        if (!e.residual.empty()) {
+            data_in(0);
+            if (g_.constants.count(e.residual)) {
+                raw_needed.insert(e.residual);
+            }
+        }
+        if (!e.bias.empty()) {
+            raw_needed.insert(e.bias);
+        }
+    }
+    int64_t wbytes = 0;
+    std::map<std::string, int64_t> woff;
+    for (const auto& name : raw_needed) {
+        woff[name] = wbytes;
+        wbytes += align_up(static_cast<int64_t>(g_.constants.at(name).bytes.size()));
+    }
+    uint8_t* wptr = dmalloc(wbytes);
+    for (const auto& name : raw_needed) {
+        const Constant& c = g_.constants.at(name);
+        if (!c.bytes.empty()) {
+            // Ordered on the device stream: a plain cudaMemcpy from pageable
+            // memory may return before its DMA lands, and the packing kernels
+            // below run on the (non-blocking) device stream.
+            check_cuda(cudaMemcpyAsync(wptr + woff[name], c.bytes.data(), c.bytes.size(), cudaMemcpyHostToDevice,
+                                       dev_->stream),
+                       "cudaMemcpyAsync(weights)");
+        }
+        ptr[name] = wptr + woff[name];
+    }
+    weight_bytes_ = wbytes;
+    for (const auto& kv : offset) {
+        ptr[kv.first] = arena_ptr + kv.second;
+    }
+    auto P = [&](const std::string& t) -> void* {
+        if (t.empty()) {
+            return nullptr;
+        }
+        auto it = ptr.find(root_of(t));
+        if (it == ptr.end()) {
+            throw RunError("executor: tensor '" + t + "' has no device buffer");
+        }
+        return it->second;
+    };
+    auto F = [&](const std::string& t) { return static_cast<float*>(P(t)); };
+    auto dims = [&](const std::string& t) -> const std::vector<int64_t>& { return shapes_.at(t).dims; };
+
+    // ---- steps
+    int64_t scratch_need = 0;
+    std::vector<std::function<void(void*)>> pending; // steps needing the scratch pointer
+    for (const auto& e : ex) {
+        const Node& n = *e.node;
+        if (e.alias) {
+            continue;
+        }
+        Step st;
+        st.label = n.op + (e.group > 1 ? "+fused" : "") + ":" + n.name;
+        if (e.op == "Conv") {
+            ConvGeom geom = conv_geom(n, shapes_.at(n.inputs[0]), shapes_.at(n.inputs[1]), shapes_.at(n.outputs[0]));
+            Epilogue ep;
+            ep.bias = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;
+            ep.res = e.residual.empty() ? nullptr : F(e.residual);
+            ep.act = e.act;
+            const float* x = F(n.inputs[0]);
+            float* y = F(e.out);
+            const int64_t pbytes = static_cast<int64_t>(conv_packed_bytes(geom));
+            if (packed_conv.count(n.inputs[1])) {
+                // pack once at load from a temporary upload of the raw weight
+                uint8_t* packed = dmalloc(align_up(pbytes));
+                const Constant& wc = g_.constants.at(n.inputs[1]);
+                void* tmp = nullptr;
+                check_cuda(cudaMalloc(&tmp, wc.bytes.size()), "cudaMalloc(weight staging)");
+                check_cuda(cudaMemcpyAsync(tmp, wc.bytes.data(), wc.bytes.size(), cudaMemcpyHostToDevice,
+                                           dev_->stream),
+                           "cudaMemcpyAsync(weight)");
+                conv_pack(dev_, geom, static_cast<const float*>(tmp), packed);
+                check_cuda(cudaStreamSynchronize(dev_->stream), "pack sync");
+                cudaFree(tmp);
+                weight_bytes_ += pbytes;
+                nb2_device* dev = dev_;
+                st.run = [=] { conv_run(dev, geom, x, packed, y, ep); };
+            } else {
+                const float* w = F(n.inputs[1]);
+                scratch_need = std::max(scratch_need, pbytes);
+                nb2_device* dev = dev_;
+                void** sp = &scratch_;
+                st.launches = geom.tap_major() ? 2 : 3;
+                st.run = [=] {
+                    conv_pack(dev, geom, w, *sp);
+                    conv_run(dev, geom, x, *sp, y, ep);
+                };
+            }
+        } else if (e.op == "Gemm" || e.op == "MatMul") {
+            GemmGeom gg{};
+            Epilogue ep;
+            const auto& ad = dims(n.inputs[0]);
+            const auto& bd = dims(n.inputs[1]);
+            if (e.op == "Gemm") {
+                gg.trans_a = static_cast<int>(n.geti("transA", 0));
+                gg.trans_b = static_cast<int>(n.geti("transB", 0));
+                gg.M = gg.trans_a ? ad[1] : ad[0];
+                gg.K = gg.trans_a ? ad[0] : ad[1];
+                gg.N = gg.trans_b ? bd[0] : bd[1];
+                gg.lda = ad[1];
+                gg.ldb = bd[1];
+                gg.ldc = gg.N;
+                ep.alpha = n.getf("alpha", 1.0f);
+                const float beta = n.getf("beta", 1.0f);
+                if (n.inputs.size() > 2 && !n.inputs[2].empty()) {
+                    const auto& cd = dims(n.inputs[2]);
+                    if (cd.size() == 1 && cd[0] == gg.N) {
+                        ep.bias = F(n.inputs[2]);
+                        ep.bias_scale = beta;
+                    } else if (cd.size() == 2 && cd[0] == gg.M && cd[1] == gg.N) {
+                        ep.res = F(n.inputs[2]);
+                        ep.res_scale = beta;
+                    } else {
+                        throw LoadError(n.where() + ": bias shape must be [N] or [M,N]");
+                    }
+                }
+                if (!e.residual.empty()) {
+                    if (ep.res) {
+                        throw LoadError(n.where() + ": cannot fuse a residual into a Gemm with an [M,N] bias");
+                    }
+                    ep.res = F(e.residual);
+                }
+            } else {
+                // MatMul (src/kernels/mat_mul.cpp:79-169)
+                std::vector<int64_t> a = ad, b = bd;
+                if (a.size() == 1) {
+                    a.insert(a.begin(), 1);
+                }
+                if (b.size() == 1) {
+                    b.push_back(1);
+                }
+                const int64_t M = a[a.size() - 2], K = a.back(), N = b.back();
+                int64_t batch = 1, a_count = 1, b_count = 1;
+                const auto& yd = dims(n.outputs[0]);
+                (void)yd;
+                std::vector<int64_t> ab(a.begin(), a.end() - 2), bb(b.begin(), b.end() - 2);
+                const size_t r = std::max(ab.size(), bb.size());
+                ab.insert(ab.begin(), r - ab.size(), 1);
+                bb.insert(bb.begin(), r - bb.size(), 1);
+                for (size_t i = 0; i < r; ++i) {
+                    batch *= std::max(ab[i], bb[i]);
+                    a_count *= ab[i];
+                    b_count *= bb[i];
+                }
+                if ((a_count != batch && a_count != 1) || (b_count != batch && b_count != 1)) {
+                    throw LoadError(n.where() + ": partial batch broadcasting is not supported");
+                }
+                gg.N = N;
+                gg.K = K;
+                gg.lda = K;
+                gg.ldb = N;
+                gg.ldc = N;
+                if (b_count == 1) {
+                    gg.M = M * batch;
+                } else {
+                    gg.M = M;
+                    gg.batch = batch;
+                    gg.a_zstride = a_count == 1 ? 0 : M * K;
+                    gg.b_zstride = K * N;
+                    gg.c_zstride = M * N;
+                }
+                if (!e.bias.empty()) {
+                    ep.bias = F(e.bias);
+                }
+                if (!e.residual.empty()) {
+                    ep.res = F(e.residual);
+                }
+            }
+            ep.act = e.act;
+            const float* A = F(n.inputs[0]);
+            float* y = F(e.out);
+            const int64_t pbytes = static_cast<int64_t>(gemm_packed_bytes(gg));
+            nb2_device* dev = dev_;
+            if (packed_gemm.count(n.inputs[1])) {
+                uint8_t* packed = dmalloc(align_up(pbytes));
+                gemm_pack_b(dev_, gg, F(n.inputs[1]), packed);
+                check_cuda(cudaStreamSynchronize(dev_->stream), "pack sync");
+                weight_bytes_ += pbytes;
+                st.run = [=] { gemm_run(dev, gg, A, packed, y, ep); };
+            } else {
+                const float* B = F(n.inputs[1]);
+                scratch_need = std::max(scratch_need, pbytes);
+                void** sp = &scratch_;
+                st.launches = 2;
+                st.run = [=] {
+                    gemm_pack_b(dev, gg, B, *sp);
+                    gemm_run(dev, gg, A, *sp, y, ep);
+                };
+            }
+        } else if (e.op == "Relu" || e.op == "Sigmoid" || e.op == "Erf" || e.op == "Sqrt" || e.op == "Neg" ||
+                   e.op == "Abs" || e.op == "Exp" || e.op == "Tanh") {
+            static const std::map<std::string, int> codes = {{"Relu", kURelu}, {"Sigmoid", kUSigmoid},
+                                                             {"Erf", kUErf},   {"Sqrt", kUSqrt},
+                                                             {"Neg", kUNeg},   {"Abs", kUAbs},
+                                                             {"Exp", kUExp},   {"Tanh", kUTanh}};
+            const int code = codes.at(e.op);
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            const int64_t cnt = numel(dims(n.outputs[0]));
+            nb2_device* dev = dev_;
+            st.run = [=] { unary(dev, code, x, y, cnt); };
+        } else if (e.op == "Add" || e.op == "Sub" || e.op == "Mul" || e.op == "Div" || e.op == "Pow") {
+            static const std::map<std::string, int> codes = {
+                {"Add", kBAdd}, {"Sub", kBSub}, {"Mul", kBMul}, {"Div", kBDiv}, {"Pow", kBPow}};
+            const int code = codes.at(e.op);
+            const TensorInfo& ta = shapes_.at(n.inputs[0]);
+            const int dt = ta.dtype == DType::I64 ? kI64 : kF32;
+            const void* a = P(n.inputs[0]);
+            const void* b = P(n.inputs[1]);
+            void* y = P(n.outputs[0]);
+            const auto ad = dims(n.inputs[0]), bd = dims(n.inputs[1]), yd = dims(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { binary(dev, code, dt, a, ad, b, bd, y, yd); };
+        } else if (e.op == "MaxPool") {
+            const auto& xd = dims(n.inputs[0]);
+            const auto& yd = dims(n.outputs[0]);
+            std::vector<int64_t> k = n.getints("kernel_shape"), s = n.getints("strides"), d = n.getints("dilations"),
+                                 pads = n.getints("pads");
+            if (s.empty()) {
+                s = {1, 1};
+            }
+            if (d.empty()) {
+                d = {1, 1};
+            }
+            if (pads.empty()) {
+                pads = {0, 0, 0, 0};
+            }
+            if (n.gets("auto_pad", "NOTSET") != "NOTSET" || n.outputs.size() > 1) {
+                throw LoadError(n.where() + ": auto_pad and the Indices output are not supported on B200");
+            }
+            PoolGeom pg{xd[0], xd[1], xd[2], xd[3], yd[2], yd[3], k[0], k[1], s[0], s[1], pads[0], pads[1], d[0], d[1]};
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { maxpool2d(dev, pg, x, y); };
+        } else if (e.op == "GlobalAveragePool" || e.op == "ReduceMean") {
+            const auto& xd = dims(n.inputs[0]);
+            int64_t rows = 1, inner = 1;
+            if (e.op == "GlobalAveragePool") {
+                rows = xd[0] * xd[1];
+                inner = numel(xd) / rows;
+            } else {
+                std::vector<int64_t> axes = g_.opset >= 18
+                                                ? (n.inputs.size() > 1 && !n.inputs[1].empty()
+                                                       ? g_.constants.at(n.inputs[1]).as_i64()
+                                                       : std::vector<int64_t>{})
+                                                : n.getints("axes");
+                const int64_t r = static_cast<int64_t>(xd.size());
+                std::set<int64_t> ax;
+                for (int64_t a : axes) {
+                    ax.insert(a < 0 ? a + r : a);
+                }
+                if (axes.empty()) {
+                    for (int64_t i = 0; i < r; ++i) {
+                        ax.insert(i);
+                    }
+                }
+                const int64_t first = *ax.begin();
+                if (*ax.rbegin() != r - 1 || static_cast<int64_t>(ax.size()) != r - first) {
+                    throw LoadError(n.where() + ": only trailing-axis means are implemented on B200");
+                }
+                for (int64_t i = 0; i < r; ++i) {
+                    (i < first ? rows : inner) *= xd[i];
+                }
+            }
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { row_mean(dev, x, y, rows, inner); };
+        } else if (e.op == "Softmax") {
+            const auto& xd = dims(n.inputs[0]);
+            const int64_t r = static_cast<int64_t>(xd.size());
+            int64_t axis = n.geti("axis", g_.opset >= 13 ? -1 : 1);
+            if (axis < 0) {
+                axis += r;
+            }
+            int64_t outer = 1, L = 1, inner = 1;
+            if (g_.opset >= 13) {
+                for (int64_t i = 0; i < r; ++i) {
+                    (i < axis ? outer : i == axis ? L : inner) *= xd[i];
+                }
+            } else { // legacy 2-D coercion (src/softmax_form.hpp)
+                for (int64_t i = 0; i < r; ++i) {
+                    (i < axis ? outer : L) *= xd[i];
+                }
+            }
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { softmax(dev, x, y, outer, L, inner); };
+        } else if (e.op == "LayerNormalization") {
+            const auto& xd = dims(n.inputs[0]);
+            const int64_t r = static_cast<int64_t>(xd.size());
+            int64_t axis = n.geti("axis", -1);
+            if (axis < 0) {
+                axis += r;
+            }
+            int64_t rows = 1, D = 1;
+            for (int64_t i = 0; i < r; ++i) {
+                (i < axis ? rows : D) *= xd[i];
+            }
+            const float eps = n.getf("epsilon", 1e-5f);
+            const float* x = F(n.inputs[0]);
+            const float* sc = F(n.inputs[1]);
+            const float* bi = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;
+            float* y = F(n.outputs[0]);
+            float* mo = n.outputs.size() > 1 && !n.outputs[1].empty() ? F(n.outputs[1]) : nullptr;
+            float* io = n.outputs.size() > 2 && !n.outputs[2].empty() ? F(n.outputs[2]) : nullptr;
+            nb2_device* dev = dev_;
+            st.run = [=] { layernorm(dev, x, sc, bi, y, mo, io, rows, D, eps); };
+        } else {
+            MoveStep ms = build_move_step(n, g_, shapes_, P, dmalloc);
+            if (!ms.run) {
+                throw LoadError(n.where() + ": op '" + n.op + "' has no row on the B200 device");
+            }
+            nb2_device* dev = dev_;
+            auto run = ms.run;
+            st.launches = ms.launches;
+            st.run = [=] { run(dev); };
+        }
+        launches_ += st.launches;
+        steps_.push_back(std::move(st));
+    }
+    if (scratch_need > 0) {
+        scratch_ = dmalloc(align_up(scratch_need));
+    }
+    for (const auto& o : g_.outputs) {
+        const TensorInfo& ti = shapes_.at(o.first);
+        IOInfo io{o.first, ti.dtype, ti.dims, P(o.first), numel(ti.dims) * dtype_size(ti.dtype)};
+        outputs_.push_back(io);
+    }
+    check_cuda(cudaStreamSynchronize(dev_->stream), "model build sync");
+}
+
+void Model::run_steps() {
+    for (auto& s : steps_) {
+        s.run();
+    }
+}
+
+void Model::launch() {
+    dev_->make_current();
+    if (!use_graph_) {
+        run_steps();
+        return;
+    }
+    if (exec_ == nullptr || exec_precision_ != dev_->precision) {
+        if (exec_) {
+            check_cuda(cudaGraphExecDestroy(exec_), "cudaGraphExecDestroy");
+            exec_ = nullptr;
+        }
+        // eager warm-up pass (sets kernel attributes, builds tensor maps)
+        run_steps();
+        check_cuda(cudaStreamSynchronize(dev_->stream), "warm-up sync");
+        cudaGraph_t graph = nullptr;
+        dev_->capturing = 1;
+        check_cuda(cudaStreamBeginCapture(dev_->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+        try {
+            run_steps();
+        } catch (...) {
+            cudaStreamEndCapture(dev_->stream, &graph);
+            if (graph) {
+                cudaGraphDestroy(graph);
+            }
+            dev_->capturing = 0;
+            throw;
+        }
+        check_cuda(cudaStreamEndCapture(dev_->stream, &graph), "cudaStreamEndCapture");
+        dev_->capturing = 0;
+        check_cuda(cudaGraphInstantiate(&exec_, graph, 0), "cudaGraphInstantiate");
+        cudaGraphDestroy(graph);
+        exec_precision_ = dev_->precision;
+    }
+    check_cuda(cudaGraphLaunch(exec_, dev_->stream), "cudaGraphLaunch");
+}
+
+void Model::synchronize() {
+    dev_->make_current();
+    const int code = dev_->take_device_error();
+    if (code != 0) {
+        throw RunError("a kernel reported device error " + std::to_string(code) +
+                       (code == 2 ? " (index out of range)" : code == 1 ? " (bounded wait expired)" : ""));
+    }
+}
+
+void Model::run_host(const std::vector<const void*>& in, const std::vector<void*>& out) {
+    enqueue_host(in, out);
+    synchronize();
+}
+
+void Model::enqueue_host(const std::vector<const void*>& in, const std::vector<void*>& out) {
+    if (in.size() != inputs_.size() || out.size() != outputs_.size()) {
+        throw RunError("executor: expected " + std::to_string(inputs_.size()) + " inputs and " +
+                       std::to_string(outputs_.size()) + " outputs");
+    }
+    dev_->make_current();
+    for (size_t i = 0; i < in.size(); ++i) {
+        if (inputs_[i].bytes > 0) {
+            check_cuda(cudaMemcpyAsync(inputs_[i].dev, in[i], static_cast<size_t>(inputs_[i].bytes),
+                                       cudaMemcpyHostToDevice, dev_->stream),
+                       "cudaMemcpyAsync(input)");
+        }
+    }
+    launch();
+    for (size_t i = 0; i < out.size(); ++i) {
+        if (outputs_[i].bytes > 0) {
+            check_cuda(cudaMemcpyAsync(out[i], outputs_[i].dev, static_cast<size_t>(outputs_[i].bytes),
+                                       cudaMemcpyDeviceToHost, dev_->stream),
+                       "cudaMemcpyAsync(output)");
+        }
+    }
+}
+
+std::vector<std::pair<std::string, float>> Model::profile() {
+    dev_->make_current();
+    std::vector<std::pair<std::string, float>> out;
+    std::vector<cudaEvent_t> ev(steps_.size() + 1);
+    for (auto& e : ev) {
+        check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+    }
+    run_steps(); // warm
+    check_cuda(cudaEventRecord(ev[0], dev_->stream), "cudaEventRecord");
+    for (size_t i = 0; i < steps_.size(); ++i) {
+        steps_[i].run();
+        check_cuda(cudaEventRecord(ev[i + 1], dev_->stream), "cudaEventRecord");
+    }
+    check_cuda(cudaStreamSynchronize(dev_->stream), "profile sync");
+    for (size_t i = 0; i < steps_.size(); ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+        out.emplace_back(steps_[i].label, ms);
+    }
+    for (auto& e : ev) {
+        cudaEventDestroy(e);
+    }
+    return out;
+}
+
+} // namespace eng
+} // namespace nb2
+
+namespace nb2 {
+namespace eng {
+
+namespace {
+std::string jstr(const std::string& s) {
+    std::string o = "\"";
+    for (char c : s) {
+        if (c == '"' || c == '\\') {
+            o += '\\';
+        }
+        o += c;
+    }
+    return o + "\"";
+}
+std::string jdims(const std::vector<int64_t>& d) {
+    std::string o = "[";
+    for (size_t i = 0; i < d.size(); ++i) {
+        o += (i ? "," : "") + std::to_string(d[i]);
+    }
+    return o + "]";
+}
+} // namespace
+
+std::string analyze_json(const uint8_t* onnx, size_t size, const std::map<std::string, std::vector<int64_t>>& dims,
+                         int flags) {
+    const Graph g = parse_onnx(onnx, size);
+    const PlanResult pr = plan_graph(g, dims, flags);
+    auto root_of = [&](const std::string& t) {
+        auto it = pr.root.find(t);
+        return it == pr.root.end() ? t : it->second;
+    };
+    std::string o = "{\"arena\":" + std::to_string(pr.arena) + ",\"fused_groups\":" +
+                    std::to_string(pr.fused_groups) + ",\"opset\":" + std::to_string(g.opset) + ",\"exec\":[";
+    for (size_t i = 0; i < pr.ex.size(); ++i) {
+        const ExecNode& e = pr.ex[i];
+        o += (i ? "," : "") + std::string("{\"op\":") + jstr(e.op) + ",\"name\":" + jstr(e.node->name) +
+             ",\"act\":" + std::to_string(e.act) + ",\"group\":" + std::to_string(e.group) +
+             ",\"alias\":" + (e.alias ? "true" : "false") + ",\"residual\":" + jstr(e.residual) +
+             ",\"bias\":" + jstr(e.bias) + ",\"ins\":[";
+        for (size_t j = 0; j < e.ins.size(); ++j) {
+            o += (j ? "," : "") + jstr(e.ins[j]);
+        }
+        o += "],\"outs\":[";
+        for (size_t j = 0; j < e.outs.size(); ++j) {
+            o += (j ? "," : "") + jstr(e.outs[j]);
+        }
+        o += "]}";
+    }
+    o += "],\"tensors\":{";
+    bool first = true;
+    for (const auto& kv : pr.shapes) {
+        if (g.constants.count(kv.first)) {
+            continue;
+        }
+        const std::string r = root_of(kv.first);
+        auto off = pr.offset.find(r);
+        auto lu = pr.last_use.find(r);
+        o += std::string(first ? "" : ",") + jstr(kv.first) + ":{\"dims\":" + jdims(kv.second.dims) +
+             ",\"dtype\":" + std::to_string(static_cast<int>(kv.second.dtype)) + ",\"root\":" + jstr(r) +
+             ",\"offset\":" + (off == pr.offset.end() ? std::string("-1") : std::to_string(off->second)) +
+             ",\"bytes\":" + std::to_string(numel(kv.second.dims) * dtype_size(kv.second.dtype)) +
+             ",\"last_use\":" + (lu == pr.last_use.end() ? std::string("-1") : std::to_string(lu->second)) + "}";
+        first = false;
+    }
+    return o + "}}";
+}
+
+} // namespace eng
+} // namespace nb2

@@ -64,7 +64,8 @@ nb2_device* device(int ordinal) {
         check_cuda(cudaSetDevice(ordinal), "cudaSetDevice");
         check_cuda(cudaStreamCreateWithFlags(&dev->stream, cudaStreamNonBlocking), "cudaStreamCreate");
         check_cuda(cudaMalloc(&dev->err_word, 256), "cudaMalloc(error word)");
-        check_cuda(cudaMemset(dev->err_word, 0, 256), "cudaMemset(error word)");
+        check_cuda(cudaMemsetAsync(dev->err_word, 0, 256, dev->stream), "cudaMemsetAsync(error word)");
+        check_cuda(cudaStreamSynchronize(dev->stream), "cudaStreamSynchronize");
         if (const char* env = std::getenv("NERT_B200_PRECISION")) {
             if (std::strcmp(env, "1xtf32") == 0 || std::strcmp(env, "1") == 0) {
                 dev->precision = kPrec1xTF32;

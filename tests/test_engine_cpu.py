@@ -1,0 +1,151 @@
+"""Host-side checks of the B200 engine that need no GPU.
+
+* libnert_b200.so loads and exports every entry point include/nert_b200.h
+  declares (no compute call is made without a GPU);
+* the C++ ONNX reader + shape inference agree with the reference's output
+  shapes, and the fusion peephole groups exactly the expected epilogues;
+* the arena plan never lets two simultaneously-live tensors overlap and
+  never places a row's output over one of its inputs (the reference
+  planner's guarantee, src/memory_planner.cpp:5-16, test
+  memory_planner_test.cpp:415 OutputNeverAliasesItsInput);
+* malformed graphs are rejected with the node named.
+"""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from nert_b200 import _lib, configs, onnx_io
+from nert_b200 import model as nbm
+from nert_b200.onnx_io import FLOAT, Graph
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "nert_b200.h")).read()
+    return sorted(set(re.findall(r"\b(nb2_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) >= 30
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    bound = set(_lib._SIGS)
+    assert set(header_symbols()) <= bound
+
+
+def test_error_reporting_without_gpu():
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    # no CUDA device in this container: a clean error status, not a crash
+    st = lib.nb2_device_open(0, ctypes.byref(h))
+    if st != 0:
+        assert lib.nb2_last_error().decode()
+
+
+def _intervals(a):
+    t = a["tensors"]
+    defs = {}
+    for i, e in enumerate(a["exec"]):
+        if e["alias"]:
+            continue
+        for o in e["outs"]:
+            defs.setdefault(t[o]["root"], i)
+    iv = {}
+    for name, info in t.items():
+        r = info["root"]
+        if info["offset"] < 0 or r in iv or r not in defs:
+            continue
+        start = defs[r]
+        end = max(start, info["last_use"]) if info["last_use"] >= 0 else start
+        size = (t[r]["bytes"] + 255) // 256 * 256 or 256
+        iv[r] = (start, end, t[r]["offset"], size)
+    return iv
+
+
+@pytest.mark.parametrize("builder,batch,fused", [(configs.resnet18, 64, 17), (configs.resnet50, 32, 49)],
+                         ids=["resnet18_b64", "resnet50_b32"])
+def test_plan_has_no_live_overlap(builder, batch, fused):
+    g = builder(batch)
+    a = nbm.analyze(g, {"input": [batch, 3, 224, 224]})
+    assert a["fused_groups"] == fused
+    iv = _intervals(a)
+    roots = list(iv)
+    for i in range(len(roots)):
+        s1, e1, o1, b1 = iv[roots[i]]
+        for j in range(i + 1, len(roots)):
+            s2, e2, o2, b2 = iv[roots[j]]
+            if s1 <= e2 and s2 <= e1:  # live at the same time
+                assert o1 + b1 <= o2 or o2 + b2 <= o1, (roots[i], roots[j])
+    assert a["arena"] <= nbm.analyze(g, {"input": [batch, 3, 224, 224]}, flags=nbm.NO_FUSION)["arena"]
+
+
+def test_output_shape_matches_reference_and_order():
+    g = configs.resnet18(8)
+    a = nbm.analyze(g, {"input": [8, 3, 224, 224]})
+    assert a["tensors"]["fc_out"]["dims"] == [8, 1000]
+    names = [e["name"] for e in a["exec"]]
+    # a downsample conv must run before the conv that fuses the residual it feeds
+    assert names.index("layer2.0.downsample") < names.index("layer2.0.conv2")
+    fused = {e["name"]: e for e in a["exec"]}
+    assert fused["layer2.0.conv2"]["residual"] == "layer2.0.downsample_out"
+    assert fused["layer2.0.conv2"]["act"] == 1
+    assert fused["conv1"]["act"] == 1 and fused["conv1"]["group"] == 2
+
+
+def test_silu_and_matmul_bias_fusion():
+    g = Graph(opset=13)
+    x = g.add_input("x", [2, 8, 6, 6])
+    w = g.const("w", np.ones((4, 8, 1, 1), np.float32))
+    c = g.op("Conv", [x, w], name="c")
+    s = g.op("Sigmoid", [c], name="s")
+    m = g.op("Mul", [c, s], name="m")
+    f = g.op("Reshape", [m, g.const("shape", np.array([2, -1], np.int64))], name="r")
+    mm = g.op("MatMul", [f, g.const("wm", np.ones((144, 5), np.float32))], name="mm")
+    y = g.op("Add", [mm, g.const("b", np.ones((5,), np.float32))], name="add")
+    g.add_output(y, None, FLOAT)
+    a = nbm.analyze(g, {"x": [2, 8, 6, 6]})
+    ops = {e["name"]: e for e in a["exec"]}
+    assert ops["c"]["act"] == 2 and ops["c"]["group"] == 3
+    assert ops["mm"]["bias"] == "b"
+    assert a["fused_groups"] == 2
+    assert ops["r"]["alias"]
+
+
+def test_unknown_op_is_rejected_naming_the_node():
+    g = Graph(opset=13)
+    x = g.add_input("x", [2, 3])
+    y = g.op("HardSwish", [x], name="mystery")
+    g.add_output(y, None, FLOAT)
+    with pytest.raises(_lib.NB2Error) as e:
+        nbm.analyze(g, {"x": [2, 3]})
+    assert "mystery" in str(e.value) and "HardSwish" in str(e.value)
+    assert e.value.status == _lib.ERR_INVALID
+
+
+def test_malformed_onnx_is_rejected():
+    with pytest.raises(_lib.NB2Error):
+        nbm.analyze(b"\x0a\x05garbage-not-protobuf", {"x": [1]})
+
+
+def test_missing_input_shape_is_rejected():
+    g = configs.resnet18(1)
+    with pytest.raises(_lib.NB2Error) as e:
+        nbm.analyze(g, {})
+    assert "input" in str(e.value)
+
+
+def test_onnx_file_roundtrip_through_engine_reader(tmp_path):
+    g = configs.resnet18(2)
+    p = onnx_io.save(g, str(tmp_path / "r18.onnx"))
+    a = nbm.analyze(p, {"input": [2, 3, 224, 224]})
+    assert a["opset"] == 13 and a["tensors"]["fc_out"]["dims"] == [2, 1000]

@@ -1,0 +1,116 @@
+"""Pinning the oracle (CPU only).
+
+The numpy restatement (oracle/np_ref.py) is checked against
+* the known answers of the reference's own tests (tests/golden/known_answers.py);
+* the reference library itself (oracle/_ref/libnert_ref.so, compiled from the
+  reference sources by oracle/Makefile) on seeded graphs;
+and the reference library is checked against the same known answers, so the
+two oracles and the golden values agree with one another.
+"""
+
+import numpy as np
+import pytest
+
+from golden.known_answers import CASES
+from nert_b200 import configs, onnx_io, synth
+from nert_b200.onnx_io import FLOAT, Graph
+from oracle import np_ref, ref
+
+needs_ref = pytest.mark.skipif(not ref.available(), reason="oracle/_ref not built (no reference sources here)")
+
+
+def single_op_graph(op, attrs, in_shapes, opset=13, n_out=1):
+    g = Graph(name="single", opset=opset)
+    names = [g.add_input(f"in{i}", list(s)) for i, s in enumerate(in_shapes)]
+    outs = g.op(op, names, n_out=n_out, name="node", **attrs)
+    for o in (outs if isinstance(outs, list) else [outs]):
+        g.add_output(o, None, FLOAT)
+    return g
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c[0].split()[1])
+def test_np_ref_known_answers(case):
+    cite, op, attrs, ins, exp, edims = case
+    arrs = [np.array(v, np.float32).reshape(d) for v, d in ins]
+    got = np_ref.run_op(op, attrs, arrs)
+    assert list(got.shape) == edims, cite
+    np.testing.assert_array_equal(got.ravel(), np.array(exp, np.float32), err_msg=cite)
+
+
+@needs_ref
+@pytest.mark.parametrize("case", CASES, ids=lambda c: c[0].split()[1])
+def test_reference_library_known_answers(case):
+    cite, op, attrs, ins, exp, edims = case
+    arrs = [np.array(v, np.float32).reshape(d) for v, d in ins]
+    g = single_op_graph(op, attrs, [a.shape for a in arrs])
+    out = ref.run_graph(g, {f"in{i}": a for i, a in enumerate(arrs)})
+    got = list(out.values())[0]
+    assert list(got.shape) == edims, cite
+    np.testing.assert_array_equal(got.ravel(), np.array(exp, np.float32), err_msg=cite)
+
+
+@needs_ref
+def test_np_ref_matches_reference_resnet18():
+    g = configs.resnet18(1)
+    x = configs.resnet_input(1)
+    a = np_ref.run(g, {"input": x})["fc_out"]
+    b = ref.run_graph(g, {"input": x})["fc_out"]
+    # float64 accumulation in both; only the summation order differs
+    assert np.abs(a - b).max() <= 1e-6 * np.abs(b).max()
+
+
+RANDOM_CASES = [
+    ("Conv", {"strides": [2, 2], "pads": [1, 0, 2, 1], "dilations": [1, 2], "group": 2}, [(2, 4, 9, 11), (6, 2, 3, 3),
+                                                                                      (6,)]),
+    ("Conv", {"pads": [3, 3, 3, 3], "strides": [2, 2]}, [(1, 3, 20, 20), (8, 3, 7, 7)]),
+    ("Gemm", {"transA": 1, "transB": 1, "alpha": 0.5, "beta": 2.0}, [(7, 5), (9, 7), (5, 9)]),
+    ("MatMul", {}, [(2, 3, 5, 4), (2, 3, 4, 6)]),
+    ("MaxPool", {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1], "ceil_mode": 1}, [(1, 2, 10, 9)]),
+    ("MaxPool", {"kernel_shape": [5, 5], "strides": [1, 1], "pads": [2, 2, 2, 2]}, [(1, 3, 8, 8)]),
+    ("GlobalAveragePool", {}, [(2, 3, 7, 7)]),
+    ("Softmax", {"axis": -1}, [(3, 4, 17)]),
+    ("Softmax", {"axis": 1}, [(2, 16, 5)]),
+    ("Sigmoid", {}, [(4, 33)]),
+    ("Add", {}, [(2, 3, 4), (3, 1)]),
+    ("Div", {}, [(2, 5), (5,)]),
+]
+
+
+@needs_ref
+@pytest.mark.parametrize("case", RANDOM_CASES, ids=lambda c: c[0] + "_" + "x".join(map(str, c[2][0])))
+def test_np_ref_matches_reference_random(case):
+    op, attrs, shapes = case
+    arrs = [synth.normal(s, 1.0, synth.seed_of("oracle", f"{op}{i}{s}")) for i, s in enumerate(shapes)]
+    if op == "Div":
+        arrs[1] = arrs[1] + np.float32(3.0)
+    g = single_op_graph(op, attrs, shapes)
+    b = list(ref.run_graph(g, {f"in{i}": a for i, a in enumerate(arrs)}).values())[0]
+    a = np_ref.run_op(op, attrs, arrs)
+    assert a.shape == b.shape
+    assert np.abs(a.astype(np.float64) - b).max() <= 1e-6 * max(1.0, np.abs(b).max())
+
+
+def test_synth_is_pinned():
+    """The generator must give the same bits on every host (GPU box included)."""
+    assert synth.seed_of("resnet18", "input") == 0xC0C0D5BDA8973F9A
+    u = synth.uniform((4,), -1.0, 1.0, 12345)
+    n = synth.normal((3,), 1.0, 12345)
+    np.testing.assert_array_equal(u, np.array([-0.7338407039642334, -0.5903668403625488, -0.7609149217605591,
+                                               -0.6477644443511963], np.float32))
+    np.testing.assert_allclose(n, np.array([1.1712841987609863, -1.6346750259399414, -2.0264062881469727],
+                                           np.float32), rtol=2e-7)
+    assert u.dtype == np.float32 and n.dtype == np.float32
+    # 2**-24 lattice: every uniform value is exactly representable
+    v = (synth.uniform((1000,), 0.0, 1.0, 7).astype(np.float64) * (1 << 24))
+    np.testing.assert_array_equal(v, np.round(v))
+
+
+def test_onnx_roundtrip():
+    g = configs.resnet18(1)
+    b = onnx_io.to_onnx_bytes(g)
+    g2 = onnx_io.from_onnx_bytes(b)
+    assert [n.op_type for n in g2.nodes] == [n.op_type for n in g.nodes]
+    assert g2.nodes[0].attrs == g.nodes[0].attrs
+    for k, v in g.initializers.items():
+        np.testing.assert_array_equal(g2.initializers[k], v)
+    assert onnx_io.to_onnx_bytes(g2) == b
