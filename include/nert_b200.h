@@ -122,6 +122,20 @@ int nb2_conv2d_pack(nb2_device* dev, const nb2_conv_geom* g, const float* w, voi
 int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* x, const void* packed,
                           const float* bias, const float* residual, int act, float* y);
 
+/* Conv for callers that cannot allocate device memory (no counterpart in the
+ * reference). Same semantics and validation as nb2_conv2d, but the weight is
+ * packed into a fixed 8 MiB static device array (per GPU, held until exit)
+ * instead of the growable workspace, so the call performs no cudaMalloc,
+ * cudaFree or other allocation: for code recording a CUDA graph, or running
+ * inside a framework that owns all device memory. Weights whose packed form
+ * exceeds nb2_conv2d_noalloc_capacity() bytes are rejected (NB2_ERR_INVALID).
+ * The first call on a device resolves the array's device address, so make it
+ * before any stream capture. All calls share the array and leave their data
+ * in it; calls whose kernels overlap on one GPU would race on it. */
+int nb2_conv2d_noalloc(nb2_device* dev, const nb2_conv_geom* g, const float* x, const float* w, const float* bias,
+                       const float* residual, int act, float* y);
+int64_t nb2_conv2d_noalloc_capacity(void);
+
 /* Gemm row: src/kernels/gemm.cpp:59-137 — Y[m,n] = alpha*op(A)op(B) +
  * beta*C with C absent (c_rank 0), [n] (c_rank 1) or [m,n] (c_rank 2), then
  * an optional activation. A is [m,k] ([k,m] if trans_a), B is [k,n]

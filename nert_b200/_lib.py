@@ -50,6 +50,8 @@ _SIGS = {
     "nb2_memcpy_d2h": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64]),
     "nb2_memcpy_d2d": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64]),
     "nb2_conv2d": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp, vp, vp, ctypes.c_int, vp]),
+    "nb2_conv2d_noalloc": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp, vp, vp, ctypes.c_int, vp]),
+    "nb2_conv2d_noalloc_capacity": (ctypes.c_int64, []),
     "nb2_conv2d_packed_size": (ctypes.c_int, [ctypes.POINTER(ConvGeom), c_i64p]),
     "nb2_conv2d_pack": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp]),
     "nb2_conv2d_run_packed": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp, vp, vp, ctypes.c_int, vp]),

@@ -111,6 +111,12 @@ struct HostStage {
 
 } // namespace
 
+namespace nb2 {
+// The validated geometry of a C-ABI Conv description (shared by every Conv
+// entry point).
+ConvGeom conv_geom_from_c(const nb2_conv_geom* c) { return to_geom(c); }
+} // namespace nb2
+
 extern "C" {
 
 const char* nb2_last_error(void) { return nb2::last_error(); }
