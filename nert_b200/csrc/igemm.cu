@@ -34,6 +34,7 @@ enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3 
 
 struct Args {
     int M, N, K, nkb;
+    int zcount; // batch / group slices
     int mode;
     const float* a;
     int64_t a_zstride;
@@ -43,6 +44,7 @@ struct Args {
     int C, H, W, OH, OW, KW, sh, sw, ph, pw, dh, dw, Cg;
     int64_t HW, OHW, img_stride;
     const int2* ktab;
+    int ktab_smem; // copy the tap table into shared memory
     // B
     int b_zrows;
     // epilogue
@@ -67,9 +69,15 @@ struct Cfg {
     static constexpr int kStageBytes = (kAPlane + kBPlane) * kPlanes;
     static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-    static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
-    static constexpr int kThreads = 320;
+    // two accumulators per tile (even / odd K blocks) x two tiles in flight
+    static constexpr int kAccs = 2;
+    static constexpr int kTmemCols = 2 * kAccs * BN;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 512;
+    static constexpr int kEpiWarps = 4;  // warps 0-3: epilogue (TMEM lane quarters 0-3)
+    static constexpr int kProdWarps = 8; // warps 4-11: A producers
+    static constexpr int kTmaWarp = 12;
+    static constexpr int kMmaWarp = 13;
+    static constexpr int kThreads = 14 * 32;
 };
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -96,8 +104,10 @@ struct RowState {
     int cin, kh, kw;
 };
 
-__device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, int half, float (&v)[16]) {
-    if (p.mode == kAConvTap) {
+template <int MODE>
+__device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, int half, const int2* ktab,
+                                         float (&v)[16]) {
+    if constexpr (MODE == kAConvTap) {
         // K ordered (kh, kw, cin) with Cg % 32 == 0: the whole 32-wide block
         // sits on one filter tap, so validity is one test per block.
         const int ih = rs.ih0 + rs.kh * p.dh;
@@ -117,18 +127,21 @@ __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, in
                 ++rs.kh;
             }
         }
-    } else if (p.mode == kAConvGeneric) {
+    } else if constexpr (MODE == kAConvGeneric) {
+        // per-k tap table (shared memory when it fits); branch-free: an
+        // out-of-window tap loads from a valid address and is zeroed after
         const int k0 = kb * 32 + half * 16;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const int2 e = __ldg(p.ktab + k0 + i);
+            const int2 e = ktab[k0 + i];
             const int dhk = e.y >> 16;
             const int dwk = e.y & 0xFFFF;
-            const bool ok = rs.ok && e.y >= 0 && (unsigned)(rs.ih0 + dhk) < (unsigned)p.H &&
-                            (unsigned)(rs.iw0 + dwk) < (unsigned)p.W;
-            v[i] = ok ? __ldg(rs.base + e.x) : 0.0f;
+            const bool ok = rs.ok & (e.y >= 0) & ((unsigned)(rs.ih0 + dhk) < (unsigned)p.H) &
+                            ((unsigned)(rs.iw0 + dwk) < (unsigned)p.W);
+            const float t = __ldg(ok ? rs.base + e.x : p.a);
+            v[i] = ok ? t : 0.0f;
         }
-    } else if (p.mode == kADenseK) {
+    } else if constexpr (MODE == kADenseK) {
         const int k0 = kb * 32 + half * 16;
         if (p.vec4) {
 #pragma unroll
@@ -189,8 +202,30 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int BN, bool THREE>
-__global__ void __launch_bounds__(320, 1)
+template <bool THREE>
+__device__ __forceinline__ bool produce_block(uint8_t* a_hi, uint8_t* a_lo, uint64_t* empty, uint64_t* full_a,
+                                              uint32_t g, int S, int r, int half, int lane, const float (&v)[16],
+                                              volatile int* abort_flag, int* err) {
+    const int s = static_cast<int>(g % static_cast<uint32_t>(S));
+    const uint32_t ph = (g / static_cast<uint32_t>(S)) & 1u;
+    if (!warp_wait(&empty[s], ph ^ 1u, abort_flag, err)) {
+        return false;
+    }
+    store16<THREE>(a_hi, a_lo, r, half, v);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(&full_a[s]);
+    }
+    return true;
+}
+
+// Persistent, warp-specialised contraction kernel: one CTA per SM walks the
+// output tiles (m fastest, so concurrent CTAs share the B tile in L2); the
+// TMEM accumulators are double buffered so the epilogue of one tile overlaps
+// the main loop of the next.
+template <int BN, bool THREE, int MODE>
+__global__ void __launch_bounds__(448, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
                  const __grid_constant__ CUtensorMap tm_lo) {
     using C = Cfg<BN, THREE>;
@@ -200,8 +235,10 @@ __global__ void __launch_bounds__(320, 1)
     uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
     uint64_t* full_b = full_a + S;
     uint64_t* empty = full_b + S;
-    uint64_t* acc_full = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* acc_full = empty + S;  // [2]
+    uint64_t* acc_empty = acc_full + 2; // [2]
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     auto a_hi = [&](int s) { return smem + s * C::kStageBytes; };
@@ -211,26 +248,42 @@ __global__ void __launch_bounds__(320, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int z = blockIdx.z;
-    const int m0 = blockIdx.x * 128;
-    const int n0 = blockIdx.y * BN;
     const int nkb = p.nkb;
+    const int num_m = (p.M + 127) / 128;
+    const int num_n = (p.N + BN - 1) / BN;
+    const int tiles_per_z = num_m * num_n;
+    const int num_tiles = tiles_per_z * p.zcount;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full_a[s], 8);
+            mbar_init(&full_a[s], C::kProdWarps);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], C::kEpiWarps);
+        }
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
+    }
+    // generic conv gather: tap table into shared memory when it fits
+    const int2* ktab = p.ktab;
+    if constexpr (MODE == kAConvGeneric) {
+        if (p.ktab_smem) {
+            int2* t = reinterpret_cast<int2*>(smem + S * C::kStageBytes + 512);
+            for (int k = threadIdx.x; k < nkb * 32; k += blockDim.x) {
+                t[k] = p.ktab[k];
+            }
+            ktab = t;
+        }
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::kTmemCols);
         tmem_relinquish();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == C::kTmaWarp && lane == 0) {
         prefetch_tmap(&tm_hi);
         if (THREE) {
             prefetch_tmap(&tm_lo);
@@ -241,161 +294,237 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 8) {
-        // ---------------- producers ----------------
-        const int r = (warp & 3) * 32 + lane;
-        const int half = warp >> 2;
-        RowState rs;
-        rs.m = m0 + r;
-        rs.ok = rs.m < p.M;
-        rs.cin = 0;
-        rs.kh = 0;
-        rs.kw = 0;
-        const float* az = p.a + (int64_t)z * p.a_zstride;
-        if (p.mode == kAConvTap || p.mode == kAConvGeneric) {
-            const int mm = rs.ok ? rs.m : 0;
-            const int n_img = mm / (int)p.OHW;
-            const int pix = mm - n_img * (int)p.OHW;
-            const int oh = pix / p.OW;
-            const int ow = pix - oh * p.OW;
-            rs.ih0 = oh * p.sh - p.ph;
-            rs.iw0 = ow * p.sw - p.pw;
-            const float* img = az + (int64_t)n_img * p.img_stride;
-            rs.base = (p.mode == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
-        } else if (p.mode == kADenseK) {
-            rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
-        } else {
-            rs.base = az + (rs.ok ? rs.m : 0);
-        }
+    // tile t -> (z, n_tile, m_tile), m fastest
+    auto decode = [&](int t, int& z, int& m0, int& n0) {
+        z = t / tiles_per_z;
+        const int r = t - z * tiles_per_z;
+        const int nt = r / num_m;
+        m0 = (r - nt * num_m) * 128;
+        n0 = nt * BN;
+    };
 
+    if (warp >= C::kEpiWarps && warp < C::kEpiWarps + C::kProdWarps) {
+        // ---------------- A producers ----------------
+        const int pw = warp - C::kEpiWarps;
+        const int r = (pw & 3) * 32 + lane;
+        const int half = pw >> 2;
+        uint32_t g = 0; // global K-block counter (the smem ring spans tiles)
         bool alive = true;
-        float cur[16], nxt[16];
-        gather16(p, rs, 0, half, cur);
-        for (int kb = 0; kb < nkb; ++kb) {
-            if (kb + 1 < nkb) {
-                gather16(p, rs, kb + 1, half, nxt);
+        for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+            int z, m0, n0;
+            decode(t, z, m0, n0);
+            RowState rs;
+            rs.m = m0 + r;
+            rs.ok = rs.m < p.M;
+            rs.cin = 0;
+            rs.kh = 0;
+            rs.kw = 0;
+            const float* az = p.a + (int64_t)z * p.a_zstride;
+            if (p.mode == kAConvTap || p.mode == kAConvGeneric) {
+                const int mm = rs.ok ? rs.m : 0;
+                const int n_img = mm / (int)p.OHW;
+                const int pix = mm - n_img * (int)p.OHW;
+                const int oh = pix / p.OW;
+                const int ow = pix - oh * p.OW;
+                rs.ih0 = oh * p.sh - p.ph;
+                rs.iw0 = ow * p.sw - p.pw;
+                const float* img = az + (int64_t)n_img * p.img_stride;
+                rs.base = (p.mode == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
+            } else if (p.mode == kADenseK) {
+                rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
+            } else {
+                rs.base = az + (rs.ok ? rs.m : 0);
             }
-            const int s = kb % S;
-            const uint32_t ph = (kb / S) & 1;
-            if (!warp_wait(&empty[s], ph ^ 1, abort_flag, p.err)) {
-                alive = false;
+            // three register buffers: loads run two K blocks ahead of the stores
+            float b0[16], b1[16], b2[16];
+            gather16<MODE>(p, rs, 0, half, ktab, b0);
+            if (nkb > 1) {
+                gather16<MODE>(p, rs, 1, half, ktab, b1);
+            }
+            for (int kb = 0; kb < nkb; kb += 3) {
+                if (kb + 2 < nkb) {
+                    gather16<MODE>(p, rs, kb + 2, half, ktab, b2);
+                }
+                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b0, abort_flag,
+                                          p.err)) {
+                    alive = false;
+                    break;
+                }
+                ++g;
+                if (kb + 1 >= nkb) {
+                    break;
+                }
+                if (kb + 3 < nkb) {
+                    gather16<MODE>(p, rs, kb + 3, half, ktab, b0);
+                }
+                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b1, abort_flag,
+                                          p.err)) {
+                    alive = false;
+                    break;
+                }
+                ++g;
+                if (kb + 2 >= nkb) {
+                    break;
+                }
+                if (kb + 4 < nkb) {
+                    gather16<MODE>(p, rs, kb + 4, half, ktab, b1);
+                }
+                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b2, abort_flag,
+                                          p.err)) {
+                    alive = false;
+                    break;
+                }
+                ++g;
+            }
+        }
+    } else if (warp < C::kEpiWarps) {
+        // ---------------- epilogue ----------------
+        const int quarter = warp; // TMEM lanes quarter*32 .. +31
+        int i = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+            int z, m0, n0;
+            decode(t, z, m0, n0);
+            const int b = i & 1;
+            if (!warp_wait(&acc_full[b], (i >> 1) & 1, abort_flag, p.err)) {
                 break;
             }
-            store16<THREE>(a_hi(s), a_lo(s), r, half, cur);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&full_a[s]);
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                cur[i] = nxt[i];
-            }
-        }
-
-        // ---------------- epilogue ----------------
-        if (alive && warp_wait(acc_full, 0, abort_flag, p.err)) {
             tc_fence_after();
-            const int quarter = warp & 3;
-            const int col_base = (warp >> 2) * (BN / 2);
-            const bool row_ok = rs.m < p.M;
+            const int row = m0 + quarter * 32 + lane;
+            const bool row_ok = row < p.M;
             int64_t row_off;
             int64_t col_stride;
             if (p.conv_out) {
-                const int mm = row_ok ? rs.m : 0;
+                const int mm = row_ok ? row : 0;
                 const int n_img = mm / (int)p.OHW;
                 const int pix = mm - n_img * (int)p.OHW;
                 row_off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix;
                 col_stride = p.OHW;
             } else {
-                row_off = (int64_t)z * p.out_zstride + (int64_t)(row_ok ? rs.m : 0) * p.ldc;
+                row_off = (int64_t)z * p.out_zstride + (int64_t)(row_ok ? row : 0) * p.ldc;
                 col_stride = 1;
             }
-            const float* bias = p.bias ? p.bias + (int64_t)z * p.bias_zstride : nullptr;
+            const float* __restrict__ bias = p.bias ? p.bias + (int64_t)z * p.bias_zstride : nullptr;
+            const float* __restrict__ res = p.res;
+            float* __restrict__ out = p.out;
+            const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+            const uint32_t acc0 = tmem + lane_base + static_cast<uint32_t>(b * C::kAccs * BN);
+            const bool two = nkb > 1;
 #pragma unroll 1
-            for (int cc = 0; cc < BN / 2; cc += 16) {
-                float acc[16];
-                tmem_ld16(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + col_base + cc, acc);
-                if (row_ok) {
+            for (int cc = 0; cc < BN; cc += 16) {
+                float v0[16], v1[16], rv[16], bv[16];
+                tmem_ld16(acc0 + cc, v0);
+                if (two) {
+                    tmem_ld16(acc0 + BN + cc, v1);
+                }
+                // issue every load of the chunk before any store
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int n = n0 + col_base + cc + j;
-                        if (n < p.N) {
-                            float v = p.alpha * acc[j];
-                            if (bias) {
-                                v += p.bias_scale * __ldg(bias + n);
-                            }
-                            const int64_t off = row_off + (int64_t)n * col_stride;
-                            if (p.res) {
-                                v += p.res_scale * __ldg(p.res + off);
-                            }
-                            p.out[off] = apply_act(v, p.act);
-                        }
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + cc + j;
+                    const bool ok = row_ok && n < p.N;
+                    bv[j] = (bias && n < p.N) ? __ldg(bias + n) : 0.0f;
+                    rv[j] = (res && ok) ? __ldg(res + row_off + (int64_t)n * col_stride) : 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + cc + j;
+                    if (row_ok && n < p.N) {
+                        const float acc = two ? v0[j] + v1[j] : v0[j];
+                        float v = p.alpha * acc + p.bias_scale * bv[j] + p.res_scale * rv[j];
+                        out[row_off + (int64_t)n * col_stride] = apply_act(v, p.act);
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&acc_empty[b]);
+            }
         }
-    } else if (warp == 8) {
+    } else if (warp == C::kTmaWarp) {
         // ---------------- TMA producer for B ----------------
         if (lane == 0) {
-            int issued = 0;
-            const int row = n0 + z * p.b_zrows;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S;
-                const uint32_t ph = (kb / S) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.err)) {
-                    break;
+            uint32_t g = 0;
+            bool alive = true;
+            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+                int z, m0, n0;
+                decode(t, z, m0, n0);
+                const int row = n0 + z * p.b_zrows;
+                for (int kb = 0; kb < nkb; ++kb, ++g) {
+                    const int s = static_cast<int>(g % S);
+                    const uint32_t ph = (g / S) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) {
+                        alive = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
+                    tma_load_2d(b_hi(s), &tm_hi, kb * 32, row, &full_b[s]);
+                    if (THREE) {
+                        tma_load_2d(b_lo(s), &tm_lo, kb * 32, row, &full_b[s]);
+                    }
                 }
-                mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
-                tma_load_2d(b_hi(s), &tm_hi, kb * 32, row, &full_b[s]);
-                if (THREE) {
-                    tma_load_2d(b_lo(s), &tm_lo, kb * 32, row, &full_b[s]);
-                }
-                ++issued;
             }
-            // Never leave with a bulk copy still landing in shared memory.
-            for (int kb = issued - 1; kb >= 0 && kb >= issued - S; --kb) {
+            // never leave with a bulk copy still landing in shared memory
+            const uint32_t issued = g;
+            for (uint32_t q = issued > S ? issued - S : 0; q < issued; ++q) {
                 const long long t0 = clock64();
-                while (!mbar_try_wait(&full_b[kb % S], (kb / S) & 1) && clock64() - t0 < kWaitBoundCycles) {
+                while (!mbar_try_wait(&full_b[q % S], (q / S) & 1u) && clock64() - t0 < kWaitBoundCycles) {
                 }
             }
         }
+        __syncwarp();
     } else {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(128, BN);
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % S;
-                const uint32_t ph = (kb / S) & 1;
-                if (!mbar_wait(&full_a[s], ph, abort_flag, p.err) || !mbar_wait(&full_b[s], ph, abort_flag, p.err)) {
+            uint32_t g = 0;
+            int i = 0;
+            bool alive = true;
+            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++i) {
+                const int b = i & 1;
+                if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, abort_flag, p.err)) {
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
-                const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-                    const uint64_t adh = sdesc_k128(ah + kk * 32);
-                    const uint64_t bdh = sdesc_k128(bh + kk * 32);
-                    if (THREE) {
-                        const uint64_t adl = sdesc_k128(al + kk * 32);
-                        const uint64_t bdl = sdesc_k128(bl + kk * 32);
-                        mma_tf32(tmem, adl, bdh, idesc, first);
-                        mma_tf32(tmem, adh, bdl, idesc, 1u);
-                        mma_tf32(tmem, adh, bdh, idesc, 1u);
-                    } else {
-                        mma_tf32(tmem, adh, bdh, idesc, first);
+                const uint32_t d0 = tmem + static_cast<uint32_t>(b * C::kAccs * BN);
+                for (int kb = 0; kb < nkb; ++kb, ++g) {
+                    const int s = static_cast<int>(g % S);
+                    const uint32_t ph = (g / S) & 1u;
+                    if (!mbar_wait(&full_a[s], ph, abort_flag, p.err) || !mbar_wait(&full_b[s], ph, abort_flag, p.err)) {
+                        alive = false;
+                        break;
                     }
+                    tc_fence_after();
+                    const uint32_t d = d0 + static_cast<uint32_t>((kb & 1) * BN);
+                    const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
+                    const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t first = (kb < 2 && kk == 0) ? 0u : 1u;
+                        const uint64_t adh = sdesc_k128(ah + kk * 32);
+                        const uint64_t bdh = sdesc_k128(bh + kk * 32);
+                        if (THREE) {
+                            const uint64_t adl = sdesc_k128(al + kk * 32);
+                            const uint64_t bdl = sdesc_k128(bl + kk * 32);
+                            mma_tf32(d, adl, bdh, idesc, first);
+                            mma_tf32(d, adh, bdl, idesc, 1u);
+                            mma_tf32(d, adh, bdh, idesc, 1u);
+                        } else {
+                            mma_tf32(d, adh, bdh, idesc, first);
+                        }
+                    }
+                    mma_commit(&empty[s]);
                 }
-                mma_commit(&empty[s]);
+                if (alive) {
+                    mma_commit(&acc_full[b]);
+                }
             }
-            mma_commit(acc_full);
-            // Wait for this thread's own MMAs before the CTA may free TMEM.
+            // every MMA of this CTA must finish before TMEM is freed
+            mma_commit(mma_done);
             const long long t0 = clock64();
-            while (!mbar_try_wait(acc_full, 0) && clock64() - t0 < kWaitBoundCycles) {
+            while (!mbar_try_wait(mma_done, 0) && clock64() - t0 < kWaitBoundCycles) {
             }
         }
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -484,18 +613,37 @@ void make_tmap(CUtensorMap* map, const float* base, int64_t kpad, int64_t rows, 
     }
 }
 
+template <int BN, bool THREE, int MODE>
+void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo) {
+    using C = Cfg<BN, THREE>;
+    const int smem = C::kSmemBytes + (a.ktab_smem ? a.nkb * 32 * 8 : 0);
+    static int attr_bytes[64] = {};
+    if (attr_bytes[dev->ordinal] < smem) {
+        check_cuda(cudaFuncSetAttribute(igemm_kernel<BN, THREE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem),
+                   "cudaFuncSetAttribute(igemm)");
+        attr_bytes[dev->ordinal] = smem;
+    }
+    igemm_kernel<BN, THREE, MODE><<<grid, C::kThreads, smem, dev->stream>>>(a, hi, lo);
+    check_cuda(cudaGetLastError(), "igemm launch");
+}
+
 template <int BN, bool THREE>
 void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo) {
-    using C = Cfg<BN, THREE>;
-    static bool attr_set[64] = {};
-    if (!attr_set[dev->ordinal]) {
-        check_cuda(cudaFuncSetAttribute(igemm_kernel<BN, THREE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        C::kSmemBytes),
-                   "cudaFuncSetAttribute(igemm)");
-        attr_set[dev->ordinal] = true;
+    switch (a.mode) {
+    case kAConvTap:
+        launch_mode<BN, THREE, kAConvTap>(dev, a, grid, hi, lo);
+        break;
+    case kAConvGeneric:
+        launch_mode<BN, THREE, kAConvGeneric>(dev, a, grid, hi, lo);
+        break;
+    case kADenseK:
+        launch_mode<BN, THREE, kADenseK>(dev, a, grid, hi, lo);
+        break;
+    default:
+        launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo);
+        break;
     }
-    igemm_kernel<BN, THREE><<<grid, C::kThreads, C::kSmemBytes, dev->stream>>>(a, hi, lo);
-    check_cuda(cudaGetLastError(), "igemm launch");
 }
 
 void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total) {
@@ -505,11 +653,14 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     make_tmap(&hi, packed, kpad, rows_total, bn);
     make_tmap(&lo, packed + rows_total * kpad, kpad, rows_total, bn);
     a.err = dev->err_word;
-    const dim3 grid(static_cast<unsigned>((a.M + 127) / 128), static_cast<unsigned>((n_per_z + bn - 1) / bn),
-                    static_cast<unsigned>(z));
-    if (grid.y > 65535 || grid.z > 65535) {
-        fail(kStatusUnsupported, "igemm: grid too large");
+    a.zcount = static_cast<int>(z);
+    a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 24576) ? 1 : 0;
+    const int64_t tiles = ((a.M + 127) / 128) * ((n_per_z + bn - 1) / bn) * z;
+    if (tiles >= (1LL << 31)) {
+        fail(kStatusUnsupported, "igemm: too many tiles");
     }
+    // persistent: one CTA per SM (shared memory admits exactly one)
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, dev->num_sms)), 1, 1);
     const bool three = dev->precision == kPrec3xTF32;
     if (bn == 64) {
         three ? launch_bn<64, true>(dev, a, grid, hi, lo) : launch_bn<64, false>(dev, a, grid, hi, lo);

@@ -64,7 +64,8 @@ class Graph:
         self.outputs.append((name, None if dims is None else list(dims), dtype))
 
     def const(self, name: str, value: np.ndarray) -> str:
-        self.initializers[name] = np.ascontiguousarray(value)
+        # np.ascontiguousarray would turn a 0-d scalar into shape (1,)
+        self.initializers[name] = np.array(value, order="C", copy=True)
         return name
 
     def op(self, op_type: str, inputs: list[str], n_out: int = 1, name: str | None = None, **attrs) -> Any:
@@ -107,7 +108,7 @@ def _f32(fieldno: int, v: float) -> bytes:
 
 
 def _tensor(name: str, arr: np.ndarray) -> bytes:
-    arr = np.ascontiguousarray(arr)
+    arr = np.array(arr, order="C", copy=False) if arr.ndim == 0 else np.ascontiguousarray(arr)
     code = _CODE_OF[arr.dtype]
     out = b"".join(_vi(1, int(d)) for d in arr.shape)
     out += _vi(2, code) + _ld(8, name.encode())

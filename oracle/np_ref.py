@@ -208,7 +208,276 @@ def softmax(node, x):
     return (e / e.sum(axis=axis, keepdims=True)).astype(F32)
 
 
+def _unary32(fn, cite):
+    def op(node, x):
+        with np.errstate(all="ignore"):
+            return fn(x.astype(F32)).astype(F32)
+    op.__doc__ = f"reference {cite}: float32 std:: math per element."
+    return op
+
+
+def _erf32(x):
+    import math as _m
+
+    flat = x.astype(np.float64).ravel()
+    return np.array([_m.erf(v) for v in flat], np.float64).astype(F32).reshape(x.shape)
+
+
+erf = _unary32(_erf32, "kernels::Erf, src/kernels/erf.cpp:27-50")
+sqrt = _unary32(np.sqrt, "kernels::Sqrt, src/kernels/sqrt.cpp")
+tanh = _unary32(np.tanh, "kernels::Tanh, src/kernels/tanh.cpp")
+exp = _unary32(np.exp, "kernels::Exp, src/kernels/exp.cpp")
+neg = _unary32(np.negative, "kernels::Neg, src/kernels/neg.cpp")
+absolute = _unary32(np.abs, "kernels::Abs, src/kernels/abs.cpp")
+
+
+def power(node, a, b):
+    """reference kernels::Pow, src/kernels/pow.cpp: float32 std::pow with broadcasting."""
+    with np.errstate(all="ignore"):
+        return np.power(a.astype(F32), b.astype(F32)).astype(F32)
+
+
+def identity(node, x):
+    return x.copy()
+
+
+def layer_norm(node, x, scale, bias=None):
+    """reference kernels::LayerNormalization, src/kernels/layer_normalization.cpp:77-160:
+    float64 mean and population variance over the axes from `axis`."""
+    axis = _attr(node, "axis", -1)
+    if axis < 0:
+        axis += x.ndim
+    eps = float(np.float32(_attr(node, "epsilon", 1e-5)))
+    axes = tuple(range(axis, x.ndim))
+    x64 = x.astype(np.float64)
+    mean = x64.mean(axis=axes, keepdims=True)
+    var = ((x64 - mean) ** 2).mean(axis=axes, keepdims=True)
+    inv = 1.0 / np.sqrt(var + eps)
+    y = (x64 - mean) * inv * scale.astype(np.float64)
+    if bias is not None:
+        y = y + bias.astype(np.float64)
+    return y.astype(F32), mean.astype(F32), inv.astype(F32)
+
+
+def transpose(node, x):
+    """reference kernels::Transpose, src/kernels/transpose.cpp:54 (default: reverse)."""
+    perm = _attr(node, "perm", None)
+    return np.ascontiguousarray(np.transpose(x, perm))
+
+
+def concat(node, *xs):
+    """reference kernels::Concat, src/kernels/concat.cpp:64."""
+    return np.concatenate(xs, axis=_attr(node, "axis", 0))
+
+
+def split(node, x, sizes=None):
+    """reference kernels::Split, src/kernels/split.cpp:65 (sizes input from
+    opset 13, 'split' attribute before, else even split)."""
+    axis = _attr(node, "axis", 0)
+    n_out = len(node.outputs)
+    if sizes is None:
+        sizes = _attr(node, "split", None)
+    if sizes is None or len(sizes) == 0:
+        dim = x.shape[axis]
+        each = -(-dim // n_out)
+        sizes = [min(each, dim - i * each) for i in range(n_out)]
+    idx = np.cumsum(sizes)[:-1]
+    return [np.ascontiguousarray(p) for p in np.split(x, idx, axis=axis)]
+
+
+def slice_op(node, x, starts, ends, axes=None, steps=None):
+    """reference kernels::Slice, src/kernels/slice.cpp (ONNX clamping)."""
+    starts, ends = [int(v) for v in starts], [int(v) for v in ends]
+    axes = list(range(len(starts))) if axes is None else [int(v) for v in axes]
+    steps = [1] * len(starts) if steps is None else [int(v) for v in steps]
+    sl = [slice(None)] * x.ndim
+    for s, e, a, st in zip(starts, ends, axes, steps):
+        a = a + x.ndim if a < 0 else a
+        dim = x.shape[a]
+        s = s + dim if s < 0 else s
+        e = e + dim if e < 0 else e
+        if st > 0:
+            s, e = min(max(s, 0), dim), min(max(e, 0), dim)
+        else:
+            s, e = min(max(s, 0), dim - 1), min(max(e, -1), dim - 1)
+            e = None if e < 0 else e
+        sl[a] = slice(s, e, st)
+    return np.ascontiguousarray(x[tuple(sl)])
+
+
+def gather(node, x, idx):
+    """reference kernels::Gather, src/kernels/gather.cpp:49-129: negative
+    indices wrap; out-of-range indices are an error."""
+    axis = _attr(node, "axis", 0)
+    if axis < 0:
+        axis += x.ndim
+    dim = x.shape[axis]
+    idx = np.asarray(idx, np.int64)
+    if ((idx < -dim) | (idx >= dim)).any():
+        raise IndexError("Gather: index out of range")
+    return np.take(x, np.where(idx < 0, idx + dim, idx), axis=axis)
+
+
+def topk(node, x, k):
+    """reference kernels::TopK, src/kernels/top_k.cpp:53-142: largest, sorted,
+    order (value desc, index asc)."""
+    k = int(np.asarray(k).ravel()[0])
+    axis = _attr(node, "axis", -1)
+    xm = np.moveaxis(x, axis, -1)
+    flat = xm.reshape(-1, xm.shape[-1])
+    vals = np.empty((flat.shape[0], k), F32)
+    inds = np.empty((flat.shape[0], k), np.int64)
+    for r in range(flat.shape[0]):
+        order = np.lexsort((np.arange(flat.shape[1]), -flat[r].astype(np.float64)))[:k]
+        inds[r] = order
+        vals[r] = flat[r][order]
+    shape = xm.shape[:-1] + (k,)
+    return (np.moveaxis(vals.reshape(shape), -1, axis), np.moveaxis(inds.reshape(shape), -1, axis))
+
+
+def _cround(x):
+    """C++ std::round: halves away from zero."""
+    return math.floor(abs(x) + 0.5) * (1 if x >= 0 else -1)
+
+
+def _nearest(mode, x, n):
+    """reference NearestIndex, src/kernels/resize.cpp:78-93."""
+    f = math.floor(x)
+    if mode == "round_prefer_floor":
+        i = f if x - f == 0.5 else _cround(x)
+    elif mode == "round_prefer_ceil":
+        i = _cround(x)
+    elif mode == "floor":
+        i = f
+    else:
+        i = math.ceil(x)
+    return min(max(int(i), 0), n - 1)
+
+
+def resize(node, x, roi=None, scales=None, sizes=None):
+    """reference kernels::Resize, src/kernels/resize.cpp:62-290: per-axis
+    tables from the coordinate transform; nearest or (multi)linear."""
+    mode = _attr(node, "mode", "nearest")
+    tr = _attr(node, "coordinate_transformation_mode", "half_pixel")
+    nm = _attr(node, "nearest_mode", "round_prefer_floor")
+    r = x.ndim
+    if sizes is not None and np.size(sizes) > 0:
+        out = [int(v) for v in sizes]
+        sc = [float(np.float32(out[i]) / np.float32(x.shape[i])) for i in range(r)]
+    else:
+        sc = [float(v) for v in np.asarray(scales, F32)]
+        out = [int(math.floor(x.shape[i] * sc[i])) for i in range(r)]
+    tables = []
+    for d in range(r):
+        tab = []
+        for o in range(out[d]):
+            xo = float(o)
+            if tr == "half_pixel":
+                xs = (xo + 0.5) / sc[d] - 0.5
+            elif tr == "pytorch_half_pixel":
+                xs = (xo + 0.5) / sc[d] - 0.5 if out[d] > 1 else 0.0
+            elif tr == "align_corners":
+                xs = 0.0 if out[d] == 1 else xo * (x.shape[d] - 1) / (out[d] - 1)
+            else:
+                xs = xo / sc[d]
+            if mode == "nearest":
+                i = _nearest(nm, xs, x.shape[d])
+                tab.append((i, i, 0.0))
+            else:
+                cl = min(max(xs, 0.0), float(x.shape[d] - 1))
+                lo = int(math.floor(cl))
+                hi = min(lo + 1, x.shape[d] - 1)
+                tab.append((lo, hi, 0.0 if hi == lo else cl - lo))
+        tables.append(tab)
+    if mode == "nearest":
+        idx = [np.array([t[0] for t in tab]) for tab in tables]
+        return np.ascontiguousarray(x[np.ix_(*idx)])
+    y = np.zeros(out, np.float64)
+    x64 = x.astype(np.float64)
+    for pos in np.ndindex(*out):
+        taps = [((), 1.0)]
+        for d in range(r):
+            lo, hi, w = tables[d][pos[d]]
+            if w == 0.0:
+                taps = [(p + (lo,), wt) for p, wt in taps]
+            else:
+                taps = [(p + (lo,), wt * (1 - w)) for p, wt in taps] + [(p + (hi,), wt * w) for p, wt in taps]
+        y[pos] = sum(wt * x64[p] for p, wt in taps)
+    return y.astype(x.dtype)
+
+
+def cast(node, x):
+    """reference kernels::Cast, src/kernels/cast.cpp: float->int64 truncates."""
+    to = _attr(node, "to", 1)
+    if to == 7:
+        return np.trunc(x).astype(np.int64) if x.dtype != np.int64 else x.copy()
+    if to == 9:
+        return x != 0
+    return x.astype(F32)
+
+
+def unsqueeze(node, x, axes=None):
+    """reference kernels::Unsqueeze, src/kernels/unsqueeze.cpp."""
+    axes = _attr(node, "axes", None) if axes is None else axes
+    r = x.ndim + len(axes)
+    axes = sorted(int(a) + r if a < 0 else int(a) for a in axes)
+    y = x
+    for a in axes:
+        y = np.expand_dims(y, a)
+    return y
+
+
+def squeeze(node, x, axes=None):
+    """reference kernels::Squeeze, src/kernels/squeeze.cpp."""
+    axes = _attr(node, "axes", None) if axes is None else axes
+    if axes is None or len(axes) == 0:
+        return np.squeeze(x)
+    return np.squeeze(x, axis=tuple(int(a) + x.ndim if a < 0 else int(a) for a in axes))
+
+
+def reduce_mean(node, x, axes=None):
+    """reference kernels::ReduceMean, src/kernels/reduce_mean.cpp:44 (float64 sum)."""
+    axes = _attr(node, "axes", None) if axes is None else axes
+    keep = bool(_attr(node, "keepdims", 1))
+    ax = tuple(range(x.ndim)) if axes is None or len(axes) == 0 else tuple(int(a) % x.ndim for a in axes)
+    return x.astype(np.float64).mean(axis=ax, keepdims=keep).astype(F32)
+
+
+def _softmax_versioned(node, x):
+    """Softmax: opset < 13 coerces to 2-D at `axis` (default 1,
+    src/softmax_form.hpp); opset >= 13 normalises one axis (default -1)."""
+    if getattr(node, "opset", 13) < 13:
+        axis = _attr(node, "axis", 1)
+        if axis < 0:
+            axis += x.ndim
+        flat = x.reshape(int(np.prod(x.shape[:axis])), -1).astype(np.float64)
+        m = flat.max(axis=1, keepdims=True)
+        e = np.exp(flat - m)
+        return (e / e.sum(axis=1, keepdims=True)).astype(F32).reshape(x.shape)
+    return softmax(node, x)
+
+
 OPS = {
+    "Erf": erf,
+    "Sqrt": sqrt,
+    "Tanh": tanh,
+    "Exp": exp,
+    "Neg": neg,
+    "Abs": absolute,
+    "Pow": power,
+    "Identity": identity,
+    "LayerNormalization": layer_norm,
+    "Transpose": transpose,
+    "Concat": concat,
+    "Split": split,
+    "Slice": slice_op,
+    "Gather": gather,
+    "TopK": topk,
+    "Resize": resize,
+    "Cast": cast,
+    "Unsqueeze": unsqueeze,
+    "Squeeze": squeeze,
+    "ReduceMean": reduce_mean,
     "Conv": conv,
     "Gemm": gemm,
     "MatMul": matmul,
@@ -222,7 +491,7 @@ OPS = {
     "GlobalAveragePool": global_average_pool,
     "Flatten": flatten,
     "Reshape": reshape,
-    "Softmax": softmax,
+    "Softmax": _softmax_versioned,
 }
 
 
@@ -232,6 +501,7 @@ def run(graph, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
     env = dict(graph.initializers)
     env.update(inputs)
     for node in graph.nodes:
+        node.opset = graph.opset
         fn = OPS.get(node.op_type)
         if fn is None:
             raise NotImplementedError(f"np_ref: no restatement of {node.op_type}")
@@ -245,11 +515,13 @@ def run(graph, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
     return {name: env[name] for name, _, _ in graph.outputs}
 
 
-def run_op(op_type: str, attrs: dict, inputs: list[np.ndarray]) -> np.ndarray:
-    """Run one op on explicit arrays (for the known-answer checks)."""
+def run_op(op_type: str, attrs: dict, inputs: list, opset: int = 13, n_out: int = 1):
+    """Run one op on explicit arrays (None for an omitted optional input)."""
     from nert_b200.onnx_io import Node
 
-    return OPS[op_type](Node(op_type, [], [], "op", dict(attrs)), *inputs)
+    node = Node(op_type, [], [f"o{i}" for i in range(n_out)], "op", dict(attrs))
+    node.opset = opset
+    return OPS[op_type](node, *inputs)
 
 
 __all__ = ["run", "run_op", "OPS", "math"]

@@ -88,6 +88,46 @@ def test_many_models_in_one_process(cuda):
             assert rel_err(got, ref) <= TOL, (k, fuse)
 
 
+def test_vit_b16_b2(cuda):
+    """Config 4 (full 12-layer ViT-B/16) at batch 2."""
+    g = configs.vit_b16(2)
+    x = configs.vit_input(2)
+    ref = np_ref.run(g, {"input": x})["head_out"]
+    out, stats = _run(g, {"input": x})
+    assert rel_err(out["head_out"], ref) <= TOL
+    assert stats["fused_groups"] >= 12 * 6  # Q, K, V, proj(+res), fc1, fc2(+res) per layer
+
+
+def _yolo_check(out, ref, full_scores, tol=TOL):
+    """Scores within tolerance; each selected index either equals the
+    oracle's or swaps with a value tied within the tolerance; boxes and class
+    ids bit-exact / within tolerance where the indices agree."""
+    v_got, v_ref = out["topk_out0"], ref["topk_out0"]
+    assert rel_err(v_got, v_ref) <= tol
+    cls_got, cls_ref = out["class_idx_out"], ref["class_idx_out"]
+    b_got, b_ref = out["det_boxes_out"], ref["det_boxes_out"]
+    scale = np.abs(v_ref).max()
+    for bi in range(v_ref.shape[0]):
+        same = cls_got[bi] == cls_ref[bi]
+        assert same.mean() >= 0.9
+        assert rel_err(b_got[bi][same], b_ref[bi][same]) <= tol
+        # a differing pick must be a near-tie in the oracle's own scores
+        for j in np.where(~same)[0]:
+            assert abs(float(v_got[bi, j]) - float(v_ref[bi, j])) <= tol * scale
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_yolov8n(cuda, batch):
+    """Config 3 (YOLOv8n-style detector, 640x640)."""
+    g = configs.yolov8n(batch)
+    x = configs.yolo_input(batch)
+    ref = np_ref.run(g, {"images": x})
+    out, stats = _run(g, {"images": x})
+    assert out["class_idx_out"].dtype == np.int64
+    _yolo_check(out, ref, None)
+    assert stats["fused_groups"] >= 50
+
+
 def test_resnet50_b1_softmax(cuda):
     g = configs.resnet50(1)
     x = configs.resnet_input(1, "resnet50")

@@ -11,7 +11,8 @@ two oracles and the golden values agree with one another.
 import numpy as np
 import pytest
 
-from golden.known_answers import CASES
+from golden.known_answers import CASES, CASES2
+from helpers import case2_graph, check_outputs
 from nert_b200 import configs, onnx_io, synth
 from nert_b200.onnx_io import FLOAT, Graph
 from oracle import np_ref, ref
@@ -47,6 +48,19 @@ def test_reference_library_known_answers(case):
     got = list(out.values())[0]
     assert list(got.shape) == edims, cite
     np.testing.assert_array_equal(got.ravel(), np.array(exp, np.float32), err_msg=cite)
+
+
+@pytest.mark.parametrize("case", CASES2, ids=lambda c: c[0].split()[1] + ("_" + c[1] if "(" in c[0] else ""))
+def test_np_ref_known_answers_2(case):
+    g, feeds, expected = case2_graph(case)
+    check_outputs(np_ref.run(g, feeds), expected, case[5], case[0])
+
+
+@needs_ref
+@pytest.mark.parametrize("case", CASES2, ids=lambda c: c[0].split()[1] + ("_" + c[1] if "(" in c[0] else ""))
+def test_reference_library_known_answers_2(case):
+    g, feeds, expected = case2_graph(case)
+    check_outputs(ref.run_graph(g, feeds), expected, case[5], case[0])
 
 
 @needs_ref

@@ -1,0 +1,180 @@
+"""Parity of every remaining row on the B200 (engine single-op graphs and the
+nert::Device plug-in) against the oracle: the reference's known answers
+(CASES2) and seeded config-sized cases. Float rows within
+max|err| <= 1e-4 * max|ref|; int64 rows and TopK/Gather indices bit-exact."""
+
+import numpy as np
+import pytest
+
+from conftest import TOL, rel_err
+from golden.known_answers import CASES2
+from helpers import case2_graph, check_outputs
+from nert_b200 import synth
+from nert_b200.onnx_io import FLOAT, INT64, Graph
+from oracle import np_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def run_engine(g, feeds, **kw):
+    from nert_b200.model import Model
+
+    m = Model(g, {k: list(v.shape) for k, v in feeds.items()}, **kw)
+    try:
+        return m.run(feeds)
+    finally:
+        m.close()
+
+
+@pytest.mark.parametrize("case", CASES2, ids=lambda c: c[0].split()[1] + ("_" + c[1] if "(" in c[0] else ""))
+def test_known_answers_engine(cuda, case):
+    g, feeds, expected = case2_graph(case)
+    if not feeds:
+        pytest.skip("no runtime input")
+    check_outputs(run_engine(g, feeds), expected, max(case[5], 1e-6), case[0])
+
+
+def one(op, in_shapes, attrs=None, consts=None, n_out=1, opset=13, dtypes=None):
+    g = Graph(opset=opset)
+    names, feeds = [], {}
+    consts = consts or {}
+    for i, s in enumerate(in_shapes):
+        if i in consts:
+            names.append(g.const(f"c{i}", consts[i]))
+            continue
+        dt = (dtypes or {}).get(i, "f32")
+        if dt == "i64":
+            feeds[f"in{i}"] = np.asarray(synth.uniform(s, 0, 1, 100 + i) * 1000, np.int64)
+            names.append(g.add_input(f"in{i}", list(s), INT64))
+        else:
+            feeds[f"in{i}"] = synth.normal(s, 1.0, synth.seed_of("rows", f"{op}{i}{s}"))
+            names.append(g.add_input(f"in{i}", list(s)))
+    outs = g.op(op, names, n_out=n_out, name="node", **(attrs or {}))
+    for o in (outs if isinstance(outs, list) else [outs]):
+        g.add_output(o, None, FLOAT)
+    return g, feeds
+
+
+def compare(g, feeds):
+    ref = np_ref.run(g, feeds)
+    got = run_engine(g, feeds)
+    for k, want in ref.items():
+        have = got[k]
+        assert have.shape == want.shape, (k, have.shape, want.shape)
+        if want.dtype == np.int64:
+            np.testing.assert_array_equal(have, want)
+        else:
+            assert rel_err(have, want) <= TOL, (k, rel_err(have, want))
+
+
+ROW_CASES = [
+    ("softmax_vit", "Softmax", [(4, 12, 197, 197)], {"axis": -1}, {}),
+    ("softmax_long", "Softmax", [(8, 5000)], {"axis": -1}, {}),
+    ("softmax_dfl", "Softmax", [(2, 16, 4, 8400)], {"axis": 1}, {}),
+    ("layernorm_vit", "LayerNormalization", [(8, 197, 768), (768,), (768,)], {"axis": -1, "epsilon": 1e-6},
+     {1: synth.normal((768,), 1.0, 7), 2: synth.normal((768,), 1.0, 8)}),
+    ("layernorm_wide", "LayerNormalization", [(16, 2048), (2048,)], {"axis": -1}, {1: synth.normal((2048,), 1.0, 9)}),
+    ("erf", "Erf", [(3, 197, 3072)], {}, {}),
+    ("sigmoid", "Sigmoid", [(2, 80, 8400)], {}, {}),
+    ("sqrt_abs", "Abs", [(1000,)], {}, {}),
+    ("transpose_tokens", "Transpose", [(8, 768, 196)], {"perm": [0, 2, 1]}, {}),
+    ("transpose_heads", "Transpose", [(8, 197, 12, 64)], {"perm": [0, 2, 1, 3]}, {}),
+    ("transpose_k", "Transpose", [(8, 197, 12, 64)], {"perm": [0, 2, 3, 1]}, {}),
+    ("concat_c", "Concat", [(2, 16, 80, 80), (2, 16, 80, 80), (2, 32, 80, 80)], {"axis": 1}, {}),
+    ("concat_last", "Concat", [(2, 144, 6400), (2, 144, 1600), (2, 144, 400)], {"axis": 2}, {}),
+    ("maxpool_sppf", "MaxPool", [(2, 128, 20, 20)], {"kernel_shape": [5, 5], "strides": [1, 1], "pads": [2] * 4}, {}),
+    ("maxpool_ceil", "MaxPool", [(2, 8, 15, 15)],
+     {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [0, 0, 1, 1], "ceil_mode": 1}, {}),
+    ("gap_r50", "GlobalAveragePool", [(4, 2048, 7, 7)], {}, {}),
+    ("resize_up", "Resize", [(2, 256, 20, 20), (0,), (4,)], {"mode": "nearest"},
+     {1: np.zeros((0,), np.float32), 2: np.array([1, 1, 2, 2], np.float32)}),
+    ("resize_linear", "Resize", [(1, 3, 17, 23), (0,), (4,)], {"mode": "linear"},
+     {1: np.zeros((0,), np.float32), 2: np.array([1, 1, 1.5, 2.25], np.float32)}),
+    ("slice_step", "Slice", [(4, 30, 40), (2,), (2,), (2,), (2,)], {},
+     {1: np.array([1, 35], np.int64), 2: np.array([28, 2], np.int64), 3: np.array([1, 2], np.int64),
+      4: np.array([3, -2], np.int64)}),
+    ("reducemean_tail", "ReduceMean", [(4, 64, 7, 7)], {"axes": [2, 3], "keepdims": 1}, {}),
+    ("pow", "Pow", [(64, 64), (64, 64)], {}, {}),
+]
+
+
+@pytest.mark.parametrize("case", ROW_CASES, ids=lambda c: c[0])
+def test_row_parity(cuda, case):
+    name, op, shapes, attrs, consts = case
+    g, feeds = one(op, shapes, attrs, consts, opset=17 if op == "LayerNormalization" else 13)
+    if op == "Pow":
+        feeds["in0"] = np.abs(feeds["in0"]) + np.float32(0.5)
+    compare(g, feeds)
+
+
+def test_split_unequal(cuda):
+    g, feeds = one("Split", [(2, 96, 40, 40), (3,)], {"axis": 1}, {1: np.array([16, 48, 32], np.int64)}, n_out=3)
+    compare(g, feeds)
+
+
+def test_gather_rows_and_scalar(cuda):
+    g = Graph(opset=13)
+    g.add_input("x", [4, 197, 768])
+    y = g.op("Gather", ["x", g.const("i", np.array(0, np.int64))], name="cls", axis=1)
+    g.add_output(y, None, FLOAT)
+    compare(g, {"x": synth.normal((4, 197, 768), 1.0, 3)})
+    g = Graph(opset=13)
+    g.add_input("x", [8400, 4])
+    g.add_input("idx", [300], INT64)
+    y = g.op("Gather", ["x", "idx"], name="rows", axis=0)
+    g.add_output(y, None, FLOAT)
+    idx = (synth.uniform((300,), 0, 1, 4) * 8400).astype(np.int64)
+    idx[::7] -= 8400  # negative indices wrap
+    compare(g, {"x": synth.normal((8400, 4), 1.0, 5), "idx": idx})
+
+
+@pytest.mark.parametrize("rows,length,k", [(1, 672000, 300), (16, 672000, 300), (64, 1000, 5), (3, 50, 50)])
+def test_topk_bit_exact(cuda, rows, length, k):
+    """Tie-free inputs (a seeded permutation of distinct values): values and
+    int64 indices must match the reference order exactly."""
+    base = np.arange(rows * length, dtype=np.float64)
+    perm = np.argsort(synth.uniform((rows * length,), 0, 1, 11), kind="stable")
+    x = ((base[perm] / (rows * length)) * 2 - 1).astype(np.float32).reshape(rows, length)
+    g, _ = one("TopK", [(rows, length), (1,)], {"axis": -1}, {1: np.array([k], np.int64)}, n_out=2)
+    feeds = {"in0": x}
+    ref = np_ref.run(g, feeds)
+    got = run_engine(g, feeds)
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
+
+
+def test_topk_ties_take_smallest_index(cuda):
+    x = np.zeros((2, 4096), np.float32)
+    x[:, ::3] = 1.0  # many exact ties
+    g, _ = one("TopK", [(2, 4096), (1,)], {"axis": -1}, {1: np.array([100], np.int64)}, n_out=2)
+    ref = np_ref.run(g, {"in0": x})
+    got = run_engine(g, {"in0": x})
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
+
+
+def test_int64_index_arithmetic(cuda):
+    g = Graph(opset=13)
+    g.add_input("i", [2, 300], INT64)
+    a = g.op("Div", ["i", g.const("n", np.array(80, np.int64))], name="div")
+    c = g.op("Sub", ["i", g.op("Mul", [a, g.const("n2", np.array(80, np.int64))], name="mul")], name="sub")
+    g.add_output(a, None, INT64)
+    g.add_output(c, None, INT64)
+    i = (synth.uniform((2, 300), 0, 1, 6) * 672000).astype(np.int64)
+    compare(g, {"i": i})
+
+
+def test_gather_out_of_range_reports_device_error(cuda):
+    from nert_b200 import _lib
+
+    g = Graph(opset=13)
+    g.add_input("x", [10, 4])
+    g.add_input("idx", [3], INT64)
+    y = g.op("Gather", ["x", "idx"], name="rows", axis=0)
+    g.add_output(y, None, FLOAT)
+    with pytest.raises(_lib.NB2Error) as e:
+        run_engine(g, {"x": np.ones((10, 4), np.float32), "idx": np.array([1, 10, 2], np.int64)})
+    assert e.value.status == _lib.ERR_DEVICE
+    # the context stays usable after the reported error
+    out = run_engine(g, {"x": np.ones((10, 4), np.float32), "idx": np.array([1, 9, -10], np.int64)})
+    assert np.all(list(out.values())[0] == 1.0)
