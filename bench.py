@@ -2,23 +2,27 @@
 """ResNet-18 fp32 inference throughput on the B200 layer (images/s, bs64 per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload resnet18|resnet50|vit_b16|yolov8n|sweep] [--batch B]
 
-A step is one full ResNet-18 forward pass (batch 64 per GPU, 3x224x224,
-seeded synthetic input and Kaiming weights, BatchNorm folded) through the
-engine's public API. Multi-GPU runs are batch-sharded replicas (one process
-per GPU under torchrun, no collective on the data path); rank timings are
-combined as the max over ranks.
+A step is one full forward pass (default: ResNet-18, batch 64 per GPU,
+3x224x224, seeded synthetic input and Kaiming weights, BatchNorm folded)
+through the engine's public API. Multi-GPU runs are batch-sharded replicas
+(one process per GPU under torchrun, no collective on the data path); rank
+timings are combined as the max over ranks.
 
 * value:  device-resident input, one CUDA-graph replay per step, timed with
           CUDA events on the engine's stream; L2 is flushed (256 MB write)
           between steps, outside the timed events.
-* e2e:    the same through Model.run (pinned host input -> H2D -> run -> D2H
-          of the logits) per step.
-* roofline: the tensor-core Conv/Gemm kernel's algorithmic FLOP/s (from one
-          eager pass with an event between rows) against the measured TF32
-          dense peak / 3 (the 3xTF32 effective peak).
+* e2e:    the same through Model.run_async (pinned host input -> H2D -> run ->
+          D2H of every output) per step.
+* roofline: the tensor-core Conv/Gemm/MatMul kernel's algorithmic FLOP/s
+          (from an eager pass with an event between rows) against the
+          measured TF32 dense peak / 3 (the 3xTF32-effective peak).
 * cpu_baseline: the reference NERT CpuDevice (oracle/_ref, compiled from the
           reference sources) on the host cores, one image per process.
+
+Other workloads (the remaining benchmark configs) print the same line with
+their own metric; `sweep` prints the single-op sweep (config 1).
 """
 
 from __future__ import annotations
@@ -37,7 +41,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-18 fp32 images/s bs64 at 1/2/4/8 B200; Conv/GEMM % of TF32 tensor peak"
 UNIT = "images/s"
-BATCH = 64
+DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32}
 
 
 def parse():
@@ -46,10 +50,14 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--workload", default="resnet18", choices=list(DEFAULT_BATCH))
+    p.add_argument("--batch", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "1xtf32"])
-    return p.parse_args()
+    a = p.parse_args()
+    if a.batch is None:
+        a.batch = DEFAULT_BATCH[a.workload]
+    return a
 
 
 def dist_env():
@@ -57,16 +65,42 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+def metric_for(workload: str, batch: int) -> str:
+    if workload == "resnet18":
+        return METRIC
+    return {"resnet50": f"ResNet-50 fp32 images/s bs{batch} per B200",
+            "vit_b16": f"ViT-B/16 fp32 images/s bs{batch} per B200",
+            "yolov8n": f"YOLOv8n-style fp32 images/s bs{batch} per B200 (640x640, TopK 300)",
+            "sweep": "single-op sweep fp32 TFLOP/s per op (config 1)"}[workload]
+
+
+def build_workload(workload: str, batch: int):
+    """(graph, feeds) of one benchmark config."""
+    from nert_b200 import configs
+
+    if workload == "resnet18":
+        return configs.resnet18(batch), {"input": configs.resnet_input(batch)}
+    if workload == "resnet50":
+        return configs.resnet50(batch), {"input": configs.resnet_input(batch, "resnet50")}
+    if workload == "vit_b16":
+        return configs.vit_b16(batch), {"input": configs.vit_input(batch)}
+    if workload == "yolov8n":
+        return configs.yolov8n(batch), {"images": configs.yolo_input(batch)}
+    raise ValueError(workload)
+
+
 # ---- reference CPU leg (oracle/_ref, the reference's own CpuDevice) ----------
 
 _REF = None
+_REF_FEED = None
 
 
-def _ref_worker_init(onnx_path, batch):
-    global _REF
+def _ref_worker_init(onnx_path, input_name, shape):
+    global _REF, _REF_FEED
     from oracle import ref
 
-    _REF = ref.RefModel(onnx_path, {"input": [batch, 3, 224, 224]})
+    _REF = ref.RefModel(onnx_path, {input_name: list(shape)})
+    _REF_FEED = (input_name, shape)
 
 
 def _ref_worker_run(seed):
@@ -74,27 +108,31 @@ def _ref_worker_run(seed):
 
     from nert_b200 import synth
 
-    x = synth.uniform((1, 3, 224, 224), -1.0, 1.0, seed)
+    name, shape = _REF_FEED
+    x = synth.uniform(tuple(shape), -1.0, 1.0, seed)
     t0 = time.perf_counter()
-    _REF.run({"input": x.astype(np.float32)})
+    _REF.run({name: x.astype(np.float32)})
     return time.perf_counter() - t0
 
 
 class RefPool:
-    """One spawned process per core, each holding the reference Model (b1)."""
+    """One spawned process per core, each holding the reference Model at batch 1."""
 
-    def __init__(self, cores: int):
+    def __init__(self, cores: int, workload: str = "resnet18"):
         import multiprocessing as mp
 
-        from nert_b200 import configs, onnx_io
+        from nert_b200 import onnx_io
 
         self.tmp = tempfile.TemporaryDirectory()
-        path = onnx_io.save(configs.resnet18(1), os.path.join(self.tmp.name, "resnet18_b1.onnx"))
+        g, feeds = build_workload(workload, 1)
+        name, x = next(iter(feeds.items()))
+        path = onnx_io.save(g, os.path.join(self.tmp.name, f"{workload}_b1.onnx"))
         self.cores = cores
-        self.pool = mp.get_context("spawn").Pool(cores, initializer=_ref_worker_init, initargs=(path, 1))
+        self.pool = mp.get_context("spawn").Pool(cores, initializer=_ref_worker_init,
+                                                 initargs=(path, name, list(x.shape)))
 
     def step(self) -> float:
-        """P images in parallel; returns wall seconds."""
+        """`cores` images in parallel; returns wall seconds."""
         t0 = time.perf_counter()
         self.pool.map(_ref_worker_run, list(range(self.cores)), chunksize=1)
         return time.perf_counter() - t0
@@ -118,8 +156,11 @@ def run_reference(args):
     if not ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnert_ref.so was not built"}))
         return 0
+    if args.workload == "sweep":
+        print(json.dumps({"impl": "reference", "unavailable": "the sweep has no reference CPU arm"}))
+        return 0
     cores = ref_cores()
-    pool = RefPool(cores)
+    pool = RefPool(cores, args.workload)
     try:
         for _ in range(max(0, args.warmup)):
             pool.step()
@@ -128,14 +169,15 @@ def run_reference(args):
         pool.close()
     total = sum(walls)
     value = cores * args.steps / total
-    sample = f"{cores} ResNet-18 images per step (batch 1 each, one process per core) of the bs{args.batch} workload"
+    sample = (f"{cores} {args.workload} images per step (batch 1 each, one process per core) of the "
+              f"bs{args.batch} workload")
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "impl": "reference", "metric": metric_for(args.workload, args.batch), "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 accumulation)",
-        "data": "synthetic (seeded U[-1,1] input, Kaiming weights, BN folded)",
-        "config": {"workload": "resnet18", "model": "resnet18", "per_gpu_batch": args.batch,
-                   "global_batch": args.batch * args.gpus, "image": [3, 224, 224], "device": "host CPU"},
+        "data": "synthetic (seeded inputs and weights, BN folded)",
+        "config": {"workload": args.workload, "model": args.workload, "per_gpu_batch": args.batch,
+                   "global_batch": args.batch * args.gpus, "device": "host CPU"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -214,7 +256,87 @@ def measure_tf32_peak() -> float:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def contraction_flops(graph, analysis) -> dict:
+    """Algorithmic FLOPs (2*M*N*K) of every Conv / Gemm / MatMul row, by node name."""
+    import numpy as np
+
+    t = analysis["tensors"]
+    nodes = {n.name: n for n in graph.nodes}
+    shape = lambda name: graph.initializers[name].shape if name in graph.initializers else tuple(t[name]["dims"])
+    out = {}
+    for e in analysis["exec"]:
+        n = nodes[e["name"]]
+        y = t[e["outs"][0]]["dims"]
+        if e["op"] == "Conv":
+            k = int(np.prod(shape(n.inputs[1])[1:]))
+        elif e["op"] == "Gemm":
+            a = shape(n.inputs[0])
+            k = a[0] if n.attrs.get("transA", 0) else a[1]
+        elif e["op"] == "MatMul":
+            k = shape(n.inputs[0])[-1]
+        else:
+            continue
+        out[e["name"]] = 2.0 * float(np.prod(y)) * k
+    return out
+
+
 # ---- B200 leg ------------------------------------------------------------------------
+
+def run_sweep(args, local):
+    """Config 1: every Conv shape at batch 32 and every Gemm shape, one row each."""
+    import torch
+
+    from nert_b200 import configs
+    from nert_b200 import model as nbm
+
+    stream_ops = []
+    rows = []
+    cases = [(n, *configs.sweep_conv(n, args.batch)) for n, *_ in configs.SWEEP_CONVS]
+    cases += [(f"gemm_{m}x{n}x{k}", *configs.sweep_gemm(m, n, k)) for m, n, k in configs.SWEEP_GEMMS]
+    for name, g, feeds in cases:
+        m = nbm.Model(g, {k: list(v.shape) for k, v in feeds.items()}, device=local)
+        m.run(feeds)
+        flops = sum(contraction_flops(g, nbm.analyze(g, {k: list(v.shape) for k, v in feeds.items()})).values())
+        stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
+        flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+        evs = []
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                m.launch()
+            for _ in range(args.steps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                m.launch()
+                e.record(stream)
+                evs.append((s, e))
+        torch.cuda.synchronize()
+        ms = sum(s.elapsed_time(e) for s, e in evs) / len(evs)
+        rows.append({"op": name, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "gflop": flops / 1e9,
+                     "kernels_per_run": m.stats()["kernels_per_run"]})
+        stream_ops.append(m.stats()["kernels_per_run"] * args.steps)
+        del flush
+        m.close()
+    tf32 = measure_tf32_peak()
+    total_ms = sum(r["ms"] for r in rows)
+    total_flop = sum(r["gflop"] for r in rows) * 1e9
+    line = {
+        "metric": metric_for("sweep", args.batch), "value": total_flop / (total_ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (3xTF32 tensor-core contractions, fp32 accumulate)" if args.precision == "3xtf32"
+        else "f32 (1xTF32 contractions, opt-in)",
+        "data": "synthetic (seeded N(0,1) data, N(0,1)/sqrt(fan_in) weights)",
+        "config": {"workload": "sweep", "conv_batch": args.batch, "precision": args.precision,
+                   "l2": "flushed between timed steps"},
+        "ops": rows,
+        "roofline": {"bound": "tensor", "peak": tf32 / 3.0, "unit": "TFLOP/s", "tf32_dense_measured": tf32,
+                     "achieved": total_flop / (total_ms * 1e-3) / 1e12},
+        "gpu_launches": int(sum(stream_ops)),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
 
 def main():
     args = parse()
@@ -223,11 +345,11 @@ def main():
     rank, world, local = dist_env()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "sweep":
         from oracle import ref
 
         if ref.available():
-            cpu = {"pool": RefPool(ref_cores())}  # spawned before the first GPU call
+            cpu = {"pool": RefPool(ref_cores(), args.workload)}  # spawned before the first GPU call
 
     import numpy as np
     import torch
@@ -243,19 +365,24 @@ def main():
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(local)
 
-    from nert_b200 import configs
+    if args.workload == "sweep":
+        return run_sweep(args, local)
+
     from nert_b200 import model as nbm
 
     batch = args.batch
-    graph = configs.resnet18(batch)
-    m = nbm.Model(graph, {"input": [batch, 3, 224, 224]}, device=local)
+    graph, feeds = build_workload(args.workload, batch)
+    dims = {k: list(v.shape) for k, v in feeds.items()}
+    m = nbm.Model(graph, dims, device=local)
     stats = m.stats()
-    x = configs.resnet_input(batch)
-    h_in = nbm.HostBuffer(x.shape)
-    h_in.array[...] = x
-    out_shape = m.outputs[0]["shape"]
-    h_out = nbm.HostBuffer(out_shape)
-    m.run_into([h_in.ptr], [h_out.ptr])  # stages the input, captures the CUDA graph
+    h_in = []
+    for io in m.inputs:
+        hb = nbm.HostBuffer(io["shape"], io["dtype"])
+        hb.array[...] = feeds[io["name"]]
+        h_in.append(hb)
+    h_out = [nbm.HostBuffer(io["shape"], io["dtype"]) for io in m.outputs]
+    in_ptrs, out_ptrs = [b.ptr for b in h_in], [b.ptr for b in h_out]
+    m.run_into(in_ptrs, out_ptrs)  # stages the inputs, captures the CUDA graph
 
     stream = torch.cuda.ExternalStream(m.stream(), device=torch.device("cuda", local))
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB > 126 MB L2
@@ -278,30 +405,22 @@ def main():
         stream.synchronize()
         return [s.elapsed_time(e) for s, e in evs]
 
-    def run_device():
-        m.launch()
-
-    def run_e2e():
-        m.run_async([h_in.ptr], [h_out.ptr])
-
-    # warm-up
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
             m.launch()
-            m.run_async([h_in.ptr], [h_out.ptr])
+            m.run_async(in_ptrs, out_ptrs)
     m.synchronize()
     torch.cuda.synchronize()
 
-    # device-resident timed region
     barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
-    dev_ms = timed(run_device, args.steps)
+    dev_ms = timed(m.launch, args.steps)
     m.synchronize()
     clk = clocks.stop()
     barrier()
     torch.cuda.synchronize()
-    e2e_ms = timed(run_e2e, args.steps)
+    e2e_ms = timed(lambda: m.run_async(in_ptrs, out_ptrs), args.steps)
     m.synchronize()
     barrier()
 
@@ -312,35 +431,25 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         mean_dev, mean_e2e = float(t[0]), float(t[1])
 
-    # roofline of the tensor-core contraction kernel (one eager pass per repeat)
-    analysis = nbm.analyze(graph, {"input": [batch, 3, 224, 224]})
-    tensors = analysis["tensors"]
-    conv_flops = {}
-    for e in analysis["exec"]:
-        if e["op"] in ("Conv", "Gemm"):
-            y = tensors[e["outs"][0]]["dims"]
-            w = graph.initializers[graph_node(graph, e["name"]).inputs[1]]
-            if e["op"] == "Conv":
-                k = int(np.prod(w.shape[1:]))
-                conv_flops[e["name"]] = 2.0 * float(np.prod(y)) * k
-            else:
-                k = w.shape[1] if graph_node(graph, e["name"]).attrs.get("transB", 0) else w.shape[0]
-                conv_flops[e["name"]] = 2.0 * float(np.prod(y)) * k
+    # roofline of the tensor-core contraction kernel (eager passes, event per row)
+    flops = contraction_flops(graph, nbm.analyze(graph, dims))
     sums = {}
-    for _ in range(3):
+    reps = 3
+    for _ in range(reps):
         for label, ms in m.profile():
-            sums[label] = sums.get(label, 0.0) + ms / 3
-    tc_time = sum(ms for lab, ms in sums.items() if lab.split(":", 1)[1] in conv_flops)
-    tc_flop = sum(conv_flops.values())
+            sums[label] = sums.get(label, 0.0) + ms / reps
+    tc_time = sum(ms for lab, ms in sums.items() if lab.split(":", 1)[1] in flops)
+    tc_flop = sum(flops.values())
     total_prof = sum(sums.values())
     achieved = tc_flop / (tc_time * 1e-3) / 1e12 if tc_time > 0 else None
+    top_rows = sorted(sums.items(), key=lambda kv: -kv[1])[:5]
 
     line = None
     if rank == 0:
         tf32 = measure_tf32_peak()
         peak = tf32 / 3.0
         line = {
-            "metric": METRIC,
+            "metric": metric_for(args.workload, batch),
             "value": world * batch / (mean_dev * 1e-3),
             "unit": UNIT,
             "n_gpus": world,
@@ -352,24 +461,25 @@ def main():
             "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core contractions, fp32 accumulate)" if args.precision == "3xtf32"
             else "f32 (1xTF32 contractions, opt-in)",
-            "data": "synthetic (seeded U[-1,1] input, Kaiming weights, BN folded)",
-            "config": {"workload": "resnet18", "model": "resnet18", "per_gpu_batch": batch,
-                       "global_batch": batch * world, "image": [3, 224, 224], "parallelism": f"replicas{world}",
+            "data": "synthetic (seeded inputs, Kaiming / N(0,0.02) weights, BN folded)",
+            "config": {"workload": args.workload, "model": args.workload, "per_gpu_batch": batch,
+                       "global_batch": batch * world, "parallelism": f"replicas{world}",
                        "l2": "flushed (256 MB write) between timed steps, outside the step events",
                        "precision": args.precision, "cuda_graph": True,
                        "fused_groups": stats["fused_groups"], "rows_per_run": stats["exec_nodes"]},
             "e2e": {"value": world * batch / (mean_e2e * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(np.prod(out_shape) * 4),
-                    "ms_per_step": mean_e2e},
-            "roofline": {"bound": "tensor", "kernel": "igemm_kernel (tcgen05 implicit-GEMM Conv/Gemm)",
+                    "h2d_bytes_per_step": int(sum(b.nbytes for b in h_in)),
+                    "d2h_bytes_per_step": int(sum(b.nbytes for b in h_out)), "ms_per_step": mean_e2e},
+            "roofline": {"bound": "tensor", "kernel": "igemm_kernel (tcgen05 implicit-GEMM Conv/Gemm/MatMul)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None,
                          "peak_note": f"measured TF32 dense {tf32:.1f} TFLOP/s (torch TF32 GEMM 8192^3) / 3 = "
-                                      f"3xTF32-effective",
+                                      "3xTF32-effective",
                          "frac_of_tf32_dense": (achieved / tf32) if achieved else None,
                          "flops_per_step": tc_flop, "kernel_ms_per_step": tc_time,
                          "share_of_step": tc_time / total_prof if total_prof else None,
                          "traffic": None},
+            "top_rows_ms": [[lab, round(ms, 4)] for lab, ms in top_rows],
             "clocks": clk,
             "gpu_launches": int(stats["kernels_per_run"]) * args.steps,
         }
@@ -383,24 +493,18 @@ def main():
         pool = cpu["pool"]
         try:
             pool.step()  # warm
-            walls = [pool.step() for _ in range(2)]
+            walls = [pool.step() for _ in range(1 if args.workload != "resnet18" else 2)]
         finally:
             pool.close()
         v = pool.cores * len(walls) / sum(walls)
         line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": pool.cores, "kind": "reference",
-                                "sample": f"2 x {pool.cores} ResNet-18 images (batch 1, one process per core)"}
+                                "sample": f"{len(walls)} x {pool.cores} {args.workload} images (batch 1, one "
+                                          "process per core)"}
     elif rank == 0:
         line["cpu_baseline"] = None
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
-
-
-def graph_node(graph, name):
-    for n in graph.nodes:
-        if n.name == name:
-            return n
-    raise KeyError(name)
 
 
 if __name__ == "__main__":

@@ -504,7 +504,8 @@ int nb2_topk(nb2_device* dev, const float* x, float* values, int64_t* indices, i
         need(rows >= 0 && len >= 0 && k >= 0, "TopK: negative extent");
         need(k <= len, "TopK: K is larger than the axis");
         bind(dev);
-        topk(dev, x, values, indices, rows, len, k);
+        const size_t sb = topk_scratch_bytes(rows, len, k);
+        topk(dev, x, values, indices, rows, len, k, sb ? dev->scratch(sb) : nullptr);
     });
 }
 

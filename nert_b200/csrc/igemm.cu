@@ -73,11 +73,11 @@ struct Cfg {
     static constexpr int kAccs = 2;
     static constexpr int kTmemCols = 2 * kAccs * BN;
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 512;
-    static constexpr int kEpiWarps = 4;  // warps 0-3: epilogue (TMEM lane quarters 0-3)
-    static constexpr int kProdWarps = 8; // warps 4-11: A producers
-    static constexpr int kTmaWarp = 12;
-    static constexpr int kMmaWarp = 13;
-    static constexpr int kThreads = 14 * 32;
+    static constexpr int kEpiWarps = 8;  // warps 0-7: epilogue (lane quarter w&3, column half w>>2)
+    static constexpr int kProdWarps = 8; // warps 8-15: A producers
+    static constexpr int kTmaWarp = 16;
+    static constexpr int kMmaWarp = 17;
+    static constexpr int kThreads = 18 * 32;
 };
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -225,7 +225,9 @@ __device__ __forceinline__ bool produce_block(uint8_t* a_hi, uint8_t* a_lo, uint
 // TMEM accumulators are double buffered so the epilogue of one tile overlaps
 // the main loop of the next.
 template <int BN, bool THREE, int MODE>
-__global__ void __launch_bounds__(448, 1)
+// 18 warps: some SM sub-partitions hold 5 of them, and each sub-partition has
+// 16K registers, so the launch allows at most 96 registers per thread.
+__global__ void __launch_bounds__(576, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
                  const __grid_constant__ CUtensorMap tm_lo) {
     using C = Cfg<BN, THREE>;
@@ -308,19 +310,22 @@ __global__ void __launch_bounds__(448, 1)
         const int pw = warp - C::kEpiWarps;
         const int r = (pw & 3) * 32 + lane;
         const int half = pw >> 2;
-        uint32_t g = 0; // global K-block counter (the smem ring spans tiles)
-        bool alive = true;
-        for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+        // The (tile, K block) items of this CTA form one stream: the gather
+        // cursor runs two items ahead of the stores, across tile boundaries,
+        // so short-K layers also keep loads in flight.
+        int ct = blockIdx.x; // cursor tile
+        int ckb = 0;         // cursor K block
+        RowState rs;
+        auto start_tile = [&](int t) {
             int z, m0, n0;
             decode(t, z, m0, n0);
-            RowState rs;
             rs.m = m0 + r;
             rs.ok = rs.m < p.M;
             rs.cin = 0;
             rs.kh = 0;
             rs.kw = 0;
             const float* az = p.a + (int64_t)z * p.a_zstride;
-            if (p.mode == kAConvTap || p.mode == kAConvGeneric) {
+            if constexpr (MODE == kAConvTap || MODE == kAConvGeneric) {
                 const int mm = rs.ok ? rs.m : 0;
                 const int n_img = mm / (int)p.OHW;
                 const int pix = mm - n_img * (int)p.OHW;
@@ -329,57 +334,58 @@ __global__ void __launch_bounds__(448, 1)
                 rs.ih0 = oh * p.sh - p.ph;
                 rs.iw0 = ow * p.sw - p.pw;
                 const float* img = az + (int64_t)n_img * p.img_stride;
-                rs.base = (p.mode == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
-            } else if (p.mode == kADenseK) {
+                rs.base = (MODE == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
+            } else if constexpr (MODE == kADenseK) {
                 rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
             } else {
                 rs.base = az + (rs.ok ? rs.m : 0);
             }
-            // three register buffers: loads run two K blocks ahead of the stores
-            float b0[16], b1[16], b2[16];
-            gather16<MODE>(p, rs, 0, half, ktab, b0);
-            if (nkb > 1) {
-                gather16<MODE>(p, rs, 1, half, ktab, b1);
+        };
+        if (ct < num_tiles) {
+            start_tile(ct);
+        }
+        auto next = [&](float (&buf)[16]) -> bool {
+            if (ct >= num_tiles) {
+                return false;
             }
-            for (int kb = 0; kb < nkb; kb += 3) {
-                if (kb + 2 < nkb) {
-                    gather16<MODE>(p, rs, kb + 2, half, ktab, b2);
+            gather16<MODE>(p, rs, ckb, half, ktab, buf);
+            if (++ckb == nkb) {
+                ckb = 0;
+                ct += gridDim.x;
+                if (ct < num_tiles) {
+                    start_tile(ct);
                 }
-                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b0, abort_flag,
-                                          p.err)) {
-                    alive = false;
-                    break;
-                }
-                ++g;
-                if (kb + 1 >= nkb) {
-                    break;
-                }
-                if (kb + 3 < nkb) {
-                    gather16<MODE>(p, rs, kb + 3, half, ktab, b0);
-                }
-                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b1, abort_flag,
-                                          p.err)) {
-                    alive = false;
-                    break;
-                }
-                ++g;
-                if (kb + 2 >= nkb) {
-                    break;
-                }
-                if (kb + 4 < nkb) {
-                    gather16<MODE>(p, rs, kb + 4, half, ktab, b1);
-                }
-                if (!produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b2, abort_flag,
-                                          p.err)) {
-                    alive = false;
-                    break;
-                }
-                ++g;
             }
+            return true;
+        };
+        uint32_t g = 0; // global K-block counter (the smem ring spans tiles)
+        float b0[16], b1[16], b2[16];
+        bool h0 = next(b0);
+        bool h1 = next(b1);
+        while (true) {
+            const bool h2 = next(b2);
+            if (!h0 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b0,
+                                             abort_flag, p.err)) {
+                break;
+            }
+            ++g;
+            h0 = next(b0);
+            if (!h1 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b1,
+                                             abort_flag, p.err)) {
+                break;
+            }
+            ++g;
+            h1 = next(b1);
+            if (!h2 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b2,
+                                             abort_flag, p.err)) {
+                break;
+            }
+            ++g;
         }
     } else if (warp < C::kEpiWarps) {
         // ---------------- epilogue ----------------
-        const int quarter = warp; // TMEM lanes quarter*32 .. +31
+        const int quarter = warp & 3;                // TMEM lanes quarter*32 .. +31
+        const int col_lo = (warp >> 2) * (BN / 2);    // this warp's half of the columns
         int i = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
             int z, m0, n0;
@@ -410,7 +416,10 @@ __global__ void __launch_bounds__(448, 1)
             const uint32_t acc0 = tmem + lane_base + static_cast<uint32_t>(b * C::kAccs * BN);
             const bool two = nkb > 1;
 #pragma unroll 1
-            for (int cc = 0; cc < BN; cc += 16) {
+            for (int cc = col_lo; cc < col_lo + BN / 2; cc += 16) {
+                if (n0 + cc >= p.N) {
+                    break; // warp-uniform: the rest of this half is padding
+                }
                 float v0[16], v1[16], rv[16], bv[16];
                 tmem_ld16(acc0 + cc, v0);
                 if (two) {

@@ -667,7 +667,10 @@ MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::stri
         const float* xp = static_cast<const float*>(ptr(n.inputs[0]));
         float* vp = static_cast<float*>(ptr(n.outputs[0]));
         int64_t* ip = static_cast<int64_t*>(ptr(n.outputs[1]));
-        st.run = [=](nb2_device* dev) { topk(dev, xp, vp, ip, rows, L, k); };
+        const size_t sb = topk_scratch_bytes(rows, L, k);
+        uint8_t* scratch = sb ? dmalloc(static_cast<int64_t>(sb)) : nullptr;
+        st.launches = sb ? 7 : 1; // clear + 3 digit passes + count + collect + sort
+        st.run = [=](nb2_device* dev) { topk(dev, xp, vp, ip, rows, L, k, scratch); };
     } else if (n.op == "Resize") {
         const TensorInfo& x = sh(n.inputs[0]);
         const TensorInfo& y = sh(n.outputs[0]);

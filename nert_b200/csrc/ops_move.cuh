@@ -56,9 +56,12 @@ void resize_on_device_tables(nb2_device* dev, const void* x, void* y, const std:
 void cast(nb2_device* dev, const void* x, int from, void* y, int to, int64_t n);
 
 // TopK (largest, sorted) along the last axis of [rows, L]: values and int64
-// indices ordered by (value desc, index asc). `scratch` holds 8*rows*(L)
-// bytes only when a row is longer than the in-CTA path allows.
-void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t L, int64_t k);
+// indices ordered by (value desc, index asc). Long rows are split over many
+// CTAs and need `scratch` of topk_scratch_bytes(rows, L, k) bytes (0 for
+// short rows).
+size_t topk_scratch_bytes(int64_t rows, int64_t L, int64_t k);
+void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t L, int64_t k,
+          void* scratch);
 
 namespace eng {
 struct MoveStep {
