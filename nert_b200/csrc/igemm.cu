@@ -30,7 +30,9 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 namespace {
 
-enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3 };
+// kADenseTma: row-major A whose rows are 16-byte aligned; TMA brings the raw
+// fp32 tile into shared memory and the producer warps split it in place.
+enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3, kADenseTma = 4 };
 
 struct Args {
     int M, N, K, nkb;
@@ -40,6 +42,7 @@ struct Args {
     int64_t a_zstride;
     int64_t lda;
     int vec4; // dense K-major rows are 16-byte aligned with K % 4 == 0
+    int a_zrows; // kADenseTma: A-map row offset per z slice
     // conv geometry
     int C, H, W, OH, OW, KW, sh, sw, ph, pw, dh, dw, Cg;
     int64_t HW, OHW, img_stride;
@@ -229,7 +232,7 @@ template <int BN, bool THREE, int MODE>
 // 16K registers, so the launch allows at most 96 registers per thread.
 __global__ void __launch_bounds__(576, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
-                 const __grid_constant__ CUtensorMap tm_lo) {
+                 const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a) {
     using C = Cfg<BN, THREE>;
     constexpr int S = C::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -310,6 +313,49 @@ __global__ void __launch_bounds__(576, 1)
         const int pw = warp - C::kEpiWarps;
         const int r = (pw & 3) * 32 + lane;
         const int half = pw >> 2;
+        if constexpr (MODE == kADenseTma) {
+            // A arrived raw by TMA (with B, on full_b); rewrite it in place as
+            // tf32 hi and write the lo plane. 1024 16-byte chunks per stage,
+            // four per thread; each 8-lane phase covers one row's 8 chunks,
+            // which the swizzle spreads over all banks.
+            const int pt = pw * 32 + lane;
+            uint32_t g = 0;
+            const uint32_t items = static_cast<uint32_t>(((num_tiles - static_cast<int>(blockIdx.x) +
+                                                           static_cast<int>(gridDim.x) - 1) /
+                                                          static_cast<int>(gridDim.x)) * nkb);
+            for (; g < items; ++g) {
+                const int s = static_cast<int>(g % S);
+                if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err)) {
+                    break;
+                }
+                const uint32_t hi_base = smem_u32(a_hi(s)), lo_base = smem_u32(a_lo(s));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int c = pt + 256 * j;
+                    const int row = c >> 3, col = c & 7;
+                    const uint32_t off = static_cast<uint32_t>(row * 128 + ((col ^ (row & 7)) << 4));
+                    float x0, x1, x2, x3;
+                    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                 : "=f"(x0), "=f"(x1), "=f"(x2), "=f"(x3)
+                                 : "r"(hi_base + off)
+                                 : "memory");
+                    const float h0 = to_tf32(x0), h1 = to_tf32(x1), h2 = to_tf32(x2), h3 = to_tf32(x3);
+                    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(hi_base + off), "f"(h0), "f"(h1),
+                                 "f"(h2), "f"(h3)
+                                 : "memory");
+                    if (THREE) {
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(lo_base + off), "f"(x0 - h0),
+                                     "f"(x1 - h1), "f"(x2 - h2), "f"(x3 - h3)
+                                     : "memory");
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&full_a[s]);
+                }
+            }
+        } else {
         // The (tile, K block) items of this CTA form one stream: the gather
         // cursor runs two items ahead of the stores, across tile boundaries,
         // so short-K layers also keep loads in flight.
@@ -381,6 +427,7 @@ __global__ void __launch_bounds__(576, 1)
                 break;
             }
             ++g;
+        }
         }
     } else if (warp < C::kEpiWarps) {
         // ---------------- epilogue ----------------
@@ -465,7 +512,12 @@ __global__ void __launch_bounds__(576, 1)
                         alive = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
+                    if constexpr (MODE == kADenseTma) {
+                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes + C::kAPlane);
+                        tma_load_2d(a_hi(s), &tm_a, kb * 32, z * p.a_zrows + m0, &full_b[s]);
+                    } else {
+                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
+                    }
                     tma_load_2d(b_hi(s), &tm_hi, kb * 32, row, &full_b[s]);
                     if (THREE) {
                         tma_load_2d(b_lo(s), &tm_lo, kb * 32, row, &full_b[s]);
@@ -609,9 +661,14 @@ __global__ void conv_ktab_kernel(int2* tab, int K, int Kpad, int KHKW, int KW, i
     tab[k] = make_int2(static_cast<int>(cin * HW + (int64_t)kh * dh * W + (int64_t)kw * dw), ((kh * dh) << 16) | (kw * dw));
 }
 
-void make_tmap(CUtensorMap* map, const float* base, int64_t kpad, int64_t rows, int box_rows) {
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kpad), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kpad * 4)};
+// 2-D fp32 map over [rows][inner] (row stride `ld` elements) with 32 x
+// box_rows boxes in the 128-byte swizzle; out-of-range boxes read zeros.
+void make_tmap(CUtensorMap* map, const float* base, int64_t inner, int64_t rows, int box_rows, int64_t ld = -1) {
+    if (ld < 0) {
+        ld = inner;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
     const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode_tiled()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
@@ -623,7 +680,8 @@ void make_tmap(CUtensorMap* map, const float* base, int64_t kpad, int64_t rows, 
 }
 
 template <int BN, bool THREE, int MODE>
-void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo) {
+void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo,
+                 const CUtensorMap& am) {
     using C = Cfg<BN, THREE>;
     const int smem = C::kSmemBytes + (a.ktab_smem ? a.nkb * 32 * 8 : 0);
     static int attr_bytes[64] = {};
@@ -633,24 +691,28 @@ void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& h
                    "cudaFuncSetAttribute(igemm)");
         attr_bytes[dev->ordinal] = smem;
     }
-    igemm_kernel<BN, THREE, MODE><<<grid, C::kThreads, smem, dev->stream>>>(a, hi, lo);
+    igemm_kernel<BN, THREE, MODE><<<grid, C::kThreads, smem, dev->stream>>>(a, hi, lo, am);
     check_cuda(cudaGetLastError(), "igemm launch");
 }
 
 template <int BN, bool THREE>
-void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo) {
+void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo,
+               const CUtensorMap& am) {
     switch (a.mode) {
     case kAConvTap:
-        launch_mode<BN, THREE, kAConvTap>(dev, a, grid, hi, lo);
+        launch_mode<BN, THREE, kAConvTap>(dev, a, grid, hi, lo, am);
         break;
     case kAConvGeneric:
-        launch_mode<BN, THREE, kAConvGeneric>(dev, a, grid, hi, lo);
+        launch_mode<BN, THREE, kAConvGeneric>(dev, a, grid, hi, lo, am);
         break;
     case kADenseK:
-        launch_mode<BN, THREE, kADenseK>(dev, a, grid, hi, lo);
+        launch_mode<BN, THREE, kADenseK>(dev, a, grid, hi, lo, am);
+        break;
+    case kADenseTma:
+        launch_mode<BN, THREE, kADenseTma>(dev, a, grid, hi, lo, am);
         break;
     default:
-        launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo);
+        launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo, am);
         break;
     }
 }
@@ -664,6 +726,14 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     a.err = dev->err_word;
     a.zcount = static_cast<int>(z);
     a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 24576) ? 1 : 0;
+    // row-major A with 16-byte rows: TMA it (a zero stride broadcasts one A)
+    CUtensorMap am = hi;
+    if (a.mode == kADenseK && a.vec4 && (a.a_zstride % a.lda) == 0) {
+        a.mode = kADenseTma;
+        a.a_zrows = static_cast<int>(a.a_zstride / a.lda);
+        const int64_t a_rows = a.a_zstride == 0 ? a.M : static_cast<int64_t>(a.a_zrows) * (z - 1) + a.M;
+        make_tmap(&am, a.a, a.K, a_rows, 128, a.lda);
+    }
     const int64_t tiles = ((a.M + 127) / 128) * ((n_per_z + bn - 1) / bn) * z;
     if (tiles >= (1LL << 31)) {
         fail(kStatusUnsupported, "igemm: too many tiles");
@@ -672,9 +742,9 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, dev->num_sms)), 1, 1);
     const bool three = dev->precision == kPrec3xTF32;
     if (bn == 64) {
-        three ? launch_bn<64, true>(dev, a, grid, hi, lo) : launch_bn<64, false>(dev, a, grid, hi, lo);
+        three ? launch_bn<64, true>(dev, a, grid, hi, lo, am) : launch_bn<64, false>(dev, a, grid, hi, lo, am);
     } else {
-        three ? launch_bn<128, true>(dev, a, grid, hi, lo) : launch_bn<128, false>(dev, a, grid, hi, lo);
+        three ? launch_bn<128, true>(dev, a, grid, hi, lo, am) : launch_bn<128, false>(dev, a, grid, hi, lo, am);
     }
 }
 
