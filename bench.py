@@ -17,7 +17,7 @@ timings are combined as the max over ranks.
           D2H of every output) per step.
 * roofline: the tensor-core Conv/Gemm/MatMul kernel's algorithmic FLOP/s
           (from an eager pass with an event between rows) against the
-          measured TF32 dense peak / 3 (the 3xTF32-effective peak).
+          pool's measured bf16 GEMM peak / 2 (tf32) / 3 (3xTF32-effective).
 * cpu_baseline: the reference NERT CpuDevice (oracle/_ref, compiled from the
           reference sources) on the host cores, one image per process.
 
@@ -30,6 +30,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -256,6 +257,31 @@ def measure_tf32_peak() -> float:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def tensor_peak(precision: str) -> tuple[float, str]:
+    """Roofline denominator for the tf32 contraction kernel.
+
+    The measured dense bf16 GEMM rate of this GPU pool (MEASURED_PEAKS.json,
+    burst figure; 1590 TFLOP/s fallback when the file is absent) halved for
+    tf32 (the tensor pipe's tf32 rate is half its bf16 rate), and divided by
+    three more in 3xTF32 mode (three MMAs per product).
+    """
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            bf16, src = float(json.load(f)["bf16_tflops"]), "of measured"
+    except (OSError, KeyError, ValueError):
+        bf16, src = 1590.0, "of fallback"
+    div = 6.0 if precision == "3xtf32" else 2.0
+    return bf16 / div, f"{src} bf16 {bf16:.1f} TFLOP/s / {div:g} ({precision}: tf32 = bf16/2" + \
+        (", three MMAs per product)" if div == 6.0 else ")")
+
+
+def row_name(label: str) -> str:
+    """Node name of a profile label 'Op[+fused]:name[layout]'."""
+    name = label.split(":", 1)[1]
+    return re.sub(r"\[[^\]]*\]$", "", name)
+
+
 def contraction_flops(graph, analysis) -> dict:
     """Algorithmic FLOPs (2*M*N*K) of every Conv / Gemm / MatMul row, by node name."""
     import numpy as np
@@ -330,8 +356,10 @@ def run_sweep(args, local):
         "config": {"workload": "sweep", "conv_batch": args.batch, "precision": args.precision,
                    "l2": "flushed between timed steps"},
         "ops": rows,
-        "roofline": {"bound": "tensor", "peak": tf32 / 3.0, "unit": "TFLOP/s", "tf32_dense_measured": tf32,
-                     "achieved": total_flop / (total_ms * 1e-3) / 1e12},
+        "roofline": {"bound": "tensor", "peak": tensor_peak(args.precision)[0], "unit": "TFLOP/s",
+                     "peak_note": tensor_peak(args.precision)[1], "tf32_dense_live": tf32,
+                     "achieved": total_flop / (total_ms * 1e-3) / 1e12,
+                     "frac": total_flop / (total_ms * 1e-3) / 1e12 / tensor_peak(args.precision)[0]},
         "gpu_launches": int(sum(stream_ops)),
     }
     print(json.dumps(line), flush=True)
@@ -438,7 +466,7 @@ def main():
     for _ in range(reps):
         for label, ms in m.profile():
             sums[label] = sums.get(label, 0.0) + ms / reps
-    tc_time = sum(ms for lab, ms in sums.items() if lab.split(":", 1)[1] in flops)
+    tc_time = sum(ms for lab, ms in sums.items() if row_name(lab) in flops)
     tc_flop = sum(flops.values())
     total_prof = sum(sums.values())
     achieved = tc_flop / (tc_time * 1e-3) / 1e12 if tc_time > 0 else None
@@ -447,7 +475,7 @@ def main():
     line = None
     if rank == 0:
         tf32 = measure_tf32_peak()
-        peak = tf32 / 3.0
+        peak, peak_note = tensor_peak(args.precision)
         line = {
             "metric": metric_for(args.workload, batch),
             "value": world * batch / (mean_dev * 1e-3),
@@ -473,9 +501,9 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "igemm_kernel (tcgen05 implicit-GEMM Conv/Gemm/MatMul)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None,
-                         "peak_note": f"measured TF32 dense {tf32:.1f} TFLOP/s (torch TF32 GEMM 8192^3) / 3 = "
-                                      "3xTF32-effective",
-                         "frac_of_tf32_dense": (achieved / tf32) if achieved else None,
+                         "peak_note": peak_note,
+                         "tf32_dense_live": tf32,
+                         "frac_of_tf32_dense_live": (achieved / tf32) if achieved else None,
                          "flops_per_step": tc_flop, "kernel_ms_per_step": tc_time,
                          "share_of_step": tc_time / total_prof if total_prof else None,
                          "traffic": None},

@@ -360,3 +360,52 @@ def sweep_gemm(m: int, n: int, k: int):
     seed = synth.seed_of("sweep", f"gemm{m}x{n}x{k}")
     feed = {"a": synth.normal((m, k), 1.0, seed), "b": synth.normal((k, n), 1.0 / math.sqrt(k), seed ^ 1)}
     return g, feed
+
+
+def _conv_out(n: int, k: int, s: int, d: int, p0: int, p1: int) -> int:
+    return (n + p0 + p1 - d * (k - 1) - 1) // s + 1
+
+
+def conv_chain(batch: int, cin: int, h: int, w: int, c: int, m: int, kernel=(3, 3), strides=(1, 1),
+               pads=(1, 1, 1, 1), dilations=(1, 1), residual: bool = False, pool: bool = False,
+               gap: bool = False, tag: str = "chain"):
+    """A small Conv trunk around one Conv of the given geometry.
+
+    input [N,cin,H,W] -> Conv 1x1 (cin->c) + Relu [-> MaxPool 3x3/2 pad 1]
+    -> Conv(kernel, strides, pads, dilations; c->m) [+ 1x1 strided skip] + Relu
+    -> Conv 1x1 (m->16) [-> GlobalAveragePool] -> output.
+    Inside the engine the middle Conv reads and writes channels-last when
+    c % 32 == 0; the first writes it and the last reads it. Returns
+    (graph, feed).
+    """
+    b = _Builder(tag)
+    g = b.g
+    x = g.add_input("x", [batch, cin, h, w])
+
+    def conv(src, ci, co, k, s, p, d, name):
+        fan_in = ci * k[0] * k[1]
+        wt = synth.normal((co, ci, k[0], k[1]), math.sqrt(2.0 / fan_in), b.seed(name + ".w"))
+        bi = synth.normal((co,), 0.1, b.seed(name + ".b"))
+        return g.op("Conv", [src, g.const(name + ".w", wt), g.const(name + ".b", bi)], name=name,
+                    kernel_shape=list(k), strides=list(s), pads=list(p), dilations=list(d))
+
+    t = g.op("Relu", [conv(x, cin, c, (1, 1), (1, 1), (0, 0, 0, 0), (1, 1), "head")], name="head_relu")
+    if pool:
+        t = g.op("MaxPool", [t], name="pool", kernel_shape=[3, 3], strides=[2, 2], pads=[1, 1, 1, 1])
+        h, w = _conv_out(h, 3, 2, 1, 1, 1), _conv_out(w, 3, 2, 1, 1, 1)
+    y = conv(t, c, m, kernel, strides, pads, dilations, "mid")
+    oh = _conv_out(h, kernel[0], strides[0], dilations[0], pads[0], pads[2])
+    ow = _conv_out(w, kernel[1], strides[1], dilations[1], pads[1], pads[3])
+    if residual:
+        sh, sw = _conv_out(h, 1, strides[0], 1, 0, 0), _conv_out(w, 1, strides[1], 1, 0, 0)
+        if (sh, sw) != (oh, ow):
+            raise ValueError("residual needs a skip of the same extent")
+        skip = conv(t, c, m, (1, 1), strides, (0, 0, 0, 0), (1, 1), "skip")
+        y = g.op("Add", [y, skip], name="add")
+    y = g.op("Relu", [y], name="mid_relu")
+    y = conv(y, m, 16, (1, 1), (1, 1), (0, 0, 0, 0), (1, 1), "tail")
+    if gap:
+        y = g.op("GlobalAveragePool", [y], name="gap")
+    g.add_output(y, None, FLOAT)
+    feed = {"x": synth.normal(tuple(g.inputs[0][1]), 1.0, b.seed("x"))}
+    return g, feed

@@ -201,6 +201,9 @@ ConvGeom conv_geom(const Node& n, const TensorInfo& x, const TensorInfo& w, cons
     g.ph = one_d ? 0 : pb[0];
     g.pw = one_d ? pb[0] : pb[1];
     g.group = n.geti("group", 1);
+    // the end padding that the output extent implies (the last window's end)
+    g.pb = (g.OH - 1) * g.sh + g.dh * (g.KH - 1) + 1 - g.H - g.ph;
+    g.pr = (g.OW - 1) * g.sw + g.dw * (g.KW - 1) + 1 - g.W - g.pw;
     if (g.group <= 0 || g.C % g.group != 0 || g.M % g.group != 0 || w.dims[1] != g.C / g.group) {
         throw LoadError(n.where() + ": weight channel dimension does not match input/group");
     }
@@ -252,7 +255,20 @@ struct PlanResult {
     std::map<std::string, int> last_use;
     int64_t arena = 0;
     int64_t fused_groups = 0;
+    std::set<std::string> nhwc; // activations kept channels-last
 };
+
+// Channels-last trunk: a 4-D fp32 activation is stored NHWC when every node
+// touching it can work in that layout and at least one Conv produces a tensor
+// of its layout class. Conv reads either layout (TMA im2col for NHWC, C % 32 ==
+// 0) and writes either; MaxPool, unary and same-shape binary rows are layout
+// preserving (one class); GlobalAveragePool reads either layout and writes
+// [N, C, 1, 1], which is the same in both. Graph inputs and outputs, aliased
+// views and every other row stay NCHW, so the boundary layout is the
+// reference's.
+std::set<std::string> assign_nhwc(const Graph& g, const std::map<std::string, TensorInfo>& shapes,
+                                  const std::vector<ExecNode>& ex);
+
 
 PlanResult plan_graph(const Graph& g_, const std::map<std::string, std::vector<int64_t>>& input_dims, int flags) {
     PlanResult pr;
@@ -332,7 +348,112 @@ PlanResult plan_graph(const Graph& g_, const std::map<std::string, std::vector<i
     pr.offset = offset;
     pr.last_use = last_use;
     pr.arena = arena;
+    if ((flags & kNchwOnly) == 0) {
+        pr.nhwc = assign_nhwc(g_, shapes_, ex);
+    }
     return pr;
+}
+
+std::set<std::string> assign_nhwc(const Graph& g, const std::map<std::string, TensorInfo>& shapes,
+                                  const std::vector<ExecNode>& ex) {
+    std::set<std::string> io;
+    for (const auto& in : g.inputs) {
+        io.insert(in.first);
+    }
+    for (const auto& o : g.outputs) {
+        io.insert(o.first);
+    }
+    auto candidate = [&](const std::string& t) {
+        if (t.empty() || io.count(t) || g.constants.count(t)) {
+            return false;
+        }
+        auto it = shapes.find(t);
+        return it != shapes.end() && it->second.dtype == DType::F32 && it->second.dims.size() == 4;
+    };
+    // union-find over tensor names: members of a class share one layout
+    std::map<std::string, std::string> parent;
+    std::function<std::string(const std::string&)> find = [&](const std::string& t) -> std::string {
+        auto it = parent.find(t);
+        if (it == parent.end() || it->second == t) {
+            return t;
+        }
+        const std::string r = find(it->second);
+        parent[t] = r;
+        return r;
+    };
+    auto unite = [&](const std::string& a, const std::string& b) {
+        const std::string ra = find(a), rb = find(b);
+        if (ra != rb) {
+            parent[ra] = rb;
+        }
+    };
+    std::set<std::string> bad, conv_out, touched;
+    for (const auto& e : ex) {
+        const Node& n = *e.node;
+        for (const auto& t : e.ins) {
+            touched.insert(t);
+        }
+        for (const auto& t : e.outs) {
+            touched.insert(t);
+        }
+        if (e.op == "Conv") {
+            const auto& x = shapes.at(n.inputs[0]);
+            if (x.dims.size() == 4) {
+                const ConvGeom cg = conv_geom(n, x, shapes.at(n.inputs[1]), shapes.at(n.outputs[0]));
+                if (!cg.nhwc_input_ok()) {
+                    bad.insert(n.inputs[0]);
+                }
+            } else {
+                bad.insert(n.inputs[0]);
+            }
+            for (size_t i = 1; i < n.inputs.size(); ++i) {
+                bad.insert(n.inputs[i]);
+            }
+            if (!e.bias.empty()) {
+                bad.insert(e.bias);
+            }
+            if (!e.residual.empty()) {
+                unite(e.residual, e.out);
+            }
+            conv_out.insert(e.out);
+        } else if (e.op == "MaxPool" && n.outputs.size() == 1) {
+            unite(n.inputs[0], n.outputs[0]);
+        } else if (e.op == "GlobalAveragePool") {
+            bad.insert(n.outputs[0]);
+        } else if (e.op == "Relu" || e.op == "Sigmoid" || e.op == "Erf" || e.op == "Sqrt" || e.op == "Neg" ||
+                   e.op == "Abs" || e.op == "Exp" || e.op == "Tanh") {
+            unite(n.inputs[0], n.outputs[0]);
+        } else if ((e.op == "Add" || e.op == "Sub" || e.op == "Mul" || e.op == "Div" || e.op == "Pow") &&
+                   shapes.at(n.inputs[0]).dims == shapes.at(n.outputs[0]).dims &&
+                   shapes.at(n.inputs[1]).dims == shapes.at(n.outputs[0]).dims) {
+            unite(n.inputs[0], n.outputs[0]);
+            unite(n.inputs[1], n.outputs[0]);
+        } else {
+            for (const auto& t : e.ins) {
+                bad.insert(t);
+            }
+            for (const auto& t : e.outs) {
+                bad.insert(t);
+            }
+        }
+    }
+    std::set<std::string> bad_class, has_conv;
+    for (const auto& t : touched) {
+        if (bad.count(t) || !candidate(t)) {
+            bad_class.insert(find(t));
+        }
+        if (conv_out.count(t)) {
+            has_conv.insert(find(t));
+        }
+    }
+    std::set<std::string> out;
+    for (const auto& t : touched) {
+        const std::string r = find(t);
+        if (!bad_class.count(r) && has_conv.count(r)) {
+            out.insert(t);
+        }
+    }
+    return out;
 }
 
 } // namespace
@@ -349,6 +470,8 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
         return it == root.end() ? t : it->second;
     };
     const std::map<std::string, int64_t>& offset = pr.offset;
+    const std::set<std::string>& nhwc = pr.nhwc;
+    nhwc_tensors_ = static_cast<int64_t>(nhwc.size());
     arena_bytes_ = pr.arena;
 
     // ---- device buffers: arena, graph inputs, constants, packed weights
@@ -463,6 +586,11 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
         st.label = n.op + (e.group > 1 ? "+fused" : "") + ":" + n.name;
         if (e.op == "Conv") {
             ConvGeom geom = conv_geom(n, shapes_.at(n.inputs[0]), shapes_.at(n.inputs[1]), shapes_.at(n.outputs[0]));
+            geom.in_nhwc = nhwc.count(n.inputs[0]) > 0;
+            geom.out_nhwc = nhwc.count(e.out) > 0;
+            if (geom.in_nhwc || geom.out_nhwc) {
+                st.label += geom.in_nhwc ? (geom.out_nhwc ? "[nhwc]" : "[nhwc>nchw]") : "[nchw>nhwc]";
+            }
             Epilogue ep;
             ep.bias = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;
             ep.res = e.residual.empty() ? nullptr : F(e.residual);
@@ -642,7 +770,12 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             const float* x = F(n.inputs[0]);
             float* y = F(n.outputs[0]);
             nb2_device* dev = dev_;
-            st.run = [=] { maxpool2d(dev, pg, x, y); };
+            if (nhwc.count(n.inputs[0])) {
+                st.label += "[nhwc]";
+                st.run = [=] { maxpool2d_nhwc(dev, pg, x, y); };
+            } else {
+                st.run = [=] { maxpool2d(dev, pg, x, y); };
+            }
         } else if (e.op == "GlobalAveragePool" || e.op == "ReduceMean") {
             const auto& xd = dims(n.inputs[0]);
             int64_t rows = 1, inner = 1;
@@ -676,7 +809,13 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             const float* x = F(n.inputs[0]);
             float* y = F(n.outputs[0]);
             nb2_device* dev = dev_;
-            st.run = [=] { row_mean(dev, x, y, rows, inner); };
+            if (e.op == "GlobalAveragePool" && nhwc.count(n.inputs[0])) {
+                const int64_t N = xd[0], C = xd[1];
+                st.label += "[nhwc]";
+                st.run = [=] { mean_nhwc(dev, x, y, N, inner, C); };
+            } else {
+                st.run = [=] { row_mean(dev, x, y, rows, inner); };
+            }
         } else if (e.op == "Softmax") {
             const auto& xd = dims(n.inputs[0]);
             const int64_t r = static_cast<int64_t>(xd.size());
@@ -910,7 +1049,8 @@ std::string analyze_json(const uint8_t* onnx, size_t size, const std::map<std::s
              ",\"dtype\":" + std::to_string(static_cast<int>(kv.second.dtype)) + ",\"root\":" + jstr(r) +
              ",\"offset\":" + (off == pr.offset.end() ? std::string("-1") : std::to_string(off->second)) +
              ",\"bytes\":" + std::to_string(numel(kv.second.dims) * dtype_size(kv.second.dtype)) +
-             ",\"last_use\":" + (lu == pr.last_use.end() ? std::string("-1") : std::to_string(lu->second)) + "}";
+             ",\"last_use\":" + (lu == pr.last_use.end() ? std::string("-1") : std::to_string(lu->second)) +
+             ",\"nhwc\":" + (pr.nhwc.count(kv.first) ? "true" : "false") + "}";
         first = false;
     }
     return o + "}}";

@@ -23,7 +23,8 @@
 namespace nb2 {
 namespace eng {
 
-enum ModelFlags : int { kNoFusion = 1, kNoGraph = 2 };
+// kNchwOnly keeps every activation NCHW (no channels-last trunk).
+enum ModelFlags : int { kNoFusion = 1, kNoGraph = 2, kNchwOnly = 4 };
 
 struct IOInfo {
     std::string name;
@@ -56,6 +57,7 @@ class Model {
     int64_t weight_bytes() const { return weight_bytes_; }
     int64_t fused_groups() const { return fused_groups_; }
     int64_t exec_nodes() const { return static_cast<int64_t>(steps_.size()); }
+    int64_t nhwc_tensors() const { return nhwc_tensors_; }
     nb2_device* device() const { return dev_; }
     // Per-step device time of one eager pass (ms), with the step labels.
     std::vector<std::pair<std::string, float>> profile();
@@ -76,7 +78,7 @@ class Model {
     std::vector<IOInfo> inputs_, outputs_;
     std::vector<void*> allocations_;
     void* scratch_ = nullptr;
-    int64_t arena_bytes_ = 0, weight_bytes_ = 0, launches_ = 0, fused_groups_ = 0;
+    int64_t arena_bytes_ = 0, weight_bytes_ = 0, launches_ = 0, fused_groups_ = 0, nhwc_tensors_ = 0;
     bool use_graph_ = true;
     cudaGraphExec_t exec_ = nullptr;
     int exec_precision_ = -1;

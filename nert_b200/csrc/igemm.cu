@@ -32,7 +32,9 @@ namespace {
 
 // kADenseTma: row-major A whose rows are 16-byte aligned; TMA brings the raw
 // fp32 tile into shared memory and the producer warps split it in place.
-enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3, kADenseTma = 4 };
+// kAConvNhwc: Conv over NHWC activations (C % 32 == 0); TMA im2col brings the
+// raw fp32 tile for one (filter tap, 32-channel block) per K block.
+enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3, kADenseTma = 4, kAConvNhwc = 5 };
 
 struct Args {
     int M, N, K, nkb;
@@ -54,6 +56,7 @@ struct Args {
     float* out;
     int64_t out_zstride, out_img_stride, ldc;
     int conv_out;
+    int vec_out; // rows are 16-byte aligned and contiguous in n (and so are bias / res)
     const float* bias;
     int bias_zstride;
     float bias_scale;
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(576, 1)
         const int pw = warp - C::kEpiWarps;
         const int r = (pw & 3) * 32 + lane;
         const int half = pw >> 2;
-        if constexpr (MODE == kADenseTma) {
+        if constexpr (MODE == kADenseTma || MODE == kAConvNhwc) {
             // A arrived raw by TMA (with B, on full_b); rewrite it in place as
             // tf32 hi and write the lo plane. 1024 16-byte chunks per stage,
             // four per thread; each 8-lane phase covers one row's 8 chunks,
@@ -472,6 +475,34 @@ __global__ void __launch_bounds__(576, 1)
                 if (two) {
                     tmem_ld16(acc0 + BN + cc, v1);
                 }
+                if (p.vec_out && n0 + cc + 16 <= p.N) {
+                    // row-contiguous output: 16-byte loads and stores
+                    const int64_t o = row_off + n0 + cc;
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias + n0 + cc + j))
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 r4 = (res && row_ok) ? __ldg(reinterpret_cast<const float4*>(res + o + j))
+                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                        bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
+                        rv[j] = r4.x, rv[j + 1] = r4.y, rv[j + 2] = r4.z, rv[j + 3] = r4.w;
+                    }
+                    if (row_ok) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            float4 w;
+                            float* wv = &w.x;
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float acc = two ? v0[j + q] + v1[j + q] : v0[j + q];
+                                wv[q] = apply_act(p.alpha * acc + p.bias_scale * bv[j + q] + p.res_scale * rv[j + q],
+                                                  p.act);
+                            }
+                            *reinterpret_cast<float4*>(out + o + j) = w;
+                        }
+                    }
+                    continue;
+                }
                 // issue every load of the chunk before any store
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
@@ -505,6 +536,14 @@ __global__ void __launch_bounds__(576, 1)
                 int z, m0, n0;
                 decode(t, z, m0, n0);
                 const int row = n0 + z * p.b_zrows;
+                int nn0 = 0, nh0 = 0, nw0 = 0; // kAConvNhwc: window start of the tile's first pixel
+                if constexpr (MODE == kAConvNhwc) {
+                    nn0 = m0 / (int)p.OHW;
+                    const int pix = m0 - nn0 * (int)p.OHW;
+                    const int oh = pix / p.OW;
+                    nh0 = oh * p.sh - p.ph;
+                    nw0 = (pix - oh * p.OW) * p.sw - p.pw;
+                }
                 for (int kb = 0; kb < nkb; ++kb, ++g) {
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
@@ -515,6 +554,15 @@ __global__ void __launch_bounds__(576, 1)
                     if constexpr (MODE == kADenseTma) {
                         mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes + C::kAPlane);
                         tma_load_2d(a_hi(s), &tm_a, kb * 32, z * p.a_zrows + m0, &full_b[s]);
+                    } else if constexpr (MODE == kAConvNhwc) {
+                        // K ordered (kh, kw, cin): block kb = (tap, 32-channel block)
+                        const int cblocks = p.Cg >> 5;
+                        const int tap = kb / cblocks;
+                        const int c0 = (kb - tap * cblocks) * 32;
+                        const int kh = tap / p.KW, kw = tap - (tap / p.KW) * p.KW;
+                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes + C::kAPlane);
+                        tma_load_im2col_4d(a_hi(s), &tm_a, c0, nw0, nh0, nn0, static_cast<uint16_t>(kw * p.dw),
+                                           static_cast<uint16_t>(kh * p.dh), &full_b[s]);
                     } else {
                         mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
                     }
@@ -711,13 +759,17 @@ void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi,
     case kADenseTma:
         launch_mode<BN, THREE, kADenseTma>(dev, a, grid, hi, lo, am);
         break;
+    case kAConvNhwc:
+        launch_mode<BN, THREE, kAConvNhwc>(dev, a, grid, hi, lo, am);
+        break;
     default:
         launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo, am);
         break;
     }
 }
 
-void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total) {
+void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total,
+            const CUtensorMap* a_map = nullptr) {
     const int64_t kpad = static_cast<int64_t>(a.nkb) * 32;
     const int bn = n_per_z <= 64 ? 64 : 128;
     CUtensorMap hi, lo;
@@ -725,9 +777,14 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     make_tmap(&lo, packed + rows_total * kpad, kpad, rows_total, bn);
     a.err = dev->err_word;
     a.zcount = static_cast<int>(z);
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    a.vec_out = (!a.conv_out && a.ldc % 4 == 0 && a.out_zstride % 4 == 0 && al16(a.out) &&
+                 (a.res == nullptr || al16(a.res)) && (a.bias == nullptr || (al16(a.bias) && a.bias_zstride % 4 == 0)))
+                    ? 1
+                    : 0;
     a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 24576) ? 1 : 0;
     // row-major A with 16-byte rows: TMA it (a zero stride broadcasts one A)
-    CUtensorMap am = hi;
+    CUtensorMap am = a_map ? *a_map : hi;
     if (a.mode == kADenseK && a.vec4 && (a.a_zstride % a.lda) == 0) {
         a.mode = kADenseTma;
         a.a_zrows = static_cast<int>(a.a_zstride / a.lda);
@@ -801,7 +858,10 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.N = static_cast<int>(g.Mg());
     a.K = static_cast<int>(K);
     a.nkb = static_cast<int>(kpad / 32);
-    a.mode = g.tap_major() ? kAConvTap : kAConvGeneric;
+    a.mode = g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
+    if (g.in_nhwc && !g.nhwc_input_ok()) {
+        fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 32 == 0 and strides <= 8");
+    }
     a.a = x;
     a.a_zstride = g.Cg() * g.H * g.W;
     a.C = static_cast<int>(g.C);
@@ -824,11 +884,41 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.ktab = g.tap_major() ? nullptr : reinterpret_cast<const int2*>(hi + 2 * g.M * kpad);
     a.b_zrows = static_cast<int>(g.Mg());
     a.out = y;
-    a.out_zstride = g.Mg() * ohw;
-    a.out_img_stride = g.M * ohw;
-    a.conv_out = 1;
+    if (g.out_nhwc) {
+        // rows are pixels, columns channels: y[pixel][M]; a group is a channel offset
+        a.conv_out = 0;
+        a.ldc = g.M;
+        a.out_zstride = g.Mg();
+    } else {
+        a.out_zstride = g.Mg() * ohw;
+        a.out_img_stride = g.M * ohw;
+        a.conv_out = 1;
+    }
     a.bias_zstride = static_cast<int>(g.Mg());
     fill_epilogue(a, ep);
+    if (g.in_nhwc) {
+        // im2col map over x[N][H][W][C]: window starts from -pad to the last
+        // start (the upper corner is pad_end - dil*(k-1), relative to the far
+        // edge); 128 pixels x 32 channels per load, 128-byte swizzle.
+        CUtensorMap am;
+        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(g.C), static_cast<cuuint64_t>(g.W),
+                                    static_cast<cuuint64_t>(g.H), static_cast<cuuint64_t>(g.N)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.C * 4), static_cast<cuuint64_t>(g.W * g.C * 4),
+                                       static_cast<cuuint64_t>(g.H * g.W * g.C * 4)};
+        const int64_t pb = g.pad_bottom(), pr = g.pad_right();
+        const int lower[2] = {static_cast<int>(-g.pw), static_cast<int>(-g.ph)};
+        const int upper[2] = {static_cast<int>(pr - g.dw * (g.KW - 1)), static_cast<int>(pb - g.dh * (g.KH - 1))};
+        const cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(g.sw), static_cast<cuuint32_t>(g.sh), 1};
+        const CUresult r = encode_im2col()(&am, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(x), dims,
+                                           strides, lower, upper, 32, 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            fail(kStatusCuda, "cuTensorMapEncodeIm2col failed (" + std::to_string(static_cast<int>(r)) + ")");
+        }
+        launch(dev, a, g.Mg(), g.group, hi, g.M, &am);
+        return;
+    }
     launch(dev, a, g.Mg(), g.group, hi, g.M);
 }
 

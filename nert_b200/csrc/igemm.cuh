@@ -32,10 +32,25 @@ struct ConvGeom {
     int64_t M, KH, KW;   // weight [M, C/group, KH, KW]
     int64_t OH, OW;      // output
     int64_t sh, sw, ph, pw, dh, dw, group;
+    static constexpr int64_t kPadUnset = INT64_MIN;
+    int64_t pb = kPadUnset, pr = kPadUnset; // bottom / right padding (unset: as top / left)
+    // Physical layouts (the engine keeps ResNet-style trunks in NHWC; the
+    // C ABI and the nert::Device rows are NCHW). An NHWC input needs
+    // nhwc_input_ok(): A is then brought in by TMA im2col.
+    bool in_nhwc = false, out_nhwc = false;
     int64_t Cg() const { return C / group; }
     int64_t Mg() const { return M / group; }
     int64_t K() const { return Cg() * KH * KW; }
     bool tap_major() const { return Cg() % 32 == 0; }
+    int64_t pad_bottom() const { return pb == kPadUnset ? ph : pb; }
+    int64_t pad_right() const { return pr == kPadUnset ? pw : pr; }
+    // TMA im2col limits for a 4-D map: traversal strides 1..8, box corners in
+    // [-128, 127] and filter offsets in [0, 255] (kept well inside here).
+    bool nhwc_input_ok() const {
+        return group == 1 && C % 32 == 0 && sh >= 1 && sh <= 8 && sw >= 1 && sw <= 8 && ph <= 64 && pw <= 64 &&
+               pad_bottom() >= -64 && pad_bottom() <= 64 && pad_right() >= -64 && pad_right() <= 64 &&
+               dh * (KH - 1) <= 64 && dw * (KW - 1) <= 64;
+    }
 };
 
 int64_t round_up(int64_t v, int64_t m);

@@ -41,6 +41,10 @@ struct PoolGeom {
     int64_t N, C, H, W, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
 };
 void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
+// The same window over channels-last x[N][H][W][C] -> y[N][OH][OW][C].
+void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
+// y[n][c] = mean over the hw pixels of channels-last x[n][hw][c]
+void mean_nhwc(nb2_device* dev, const float* x, float* y, int64_t n, int64_t hw, int64_t c);
 // mean over the trailing `inner` elements of each of `rows` rows
 void row_mean(nb2_device* dev, const float* x, float* y, int64_t rows, int64_t inner);
 

@@ -105,7 +105,127 @@ __global__ void row_mean_block_kernel(const float* __restrict__ x, float* __rest
     }
 }
 
+// Channels-last max pool: one thread per (output pixel, 4 channels), so a
+// warp reads 512 contiguous bytes of one input pixel per tap (C % 4 == 0).
+__global__ void maxpool2d_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y, PoolGeom g,
+                                       int64_t total) {
+    const int64_t C4 = g.C >> 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c4 = i % C4;
+        int64_t t = i / C4;
+        const int64_t ow = t % g.OW;
+        t /= g.OW;
+        const int64_t oh = t % g.OH;
+        const int64_t n = t / g.OH;
+        const int64_t h0 = oh * g.sh - g.ph;
+        const int64_t w0 = ow * g.sw - g.pw;
+        float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        for (int64_t kh = 0; kh < g.KH; ++kh) {
+            const int64_t ih = h0 + kh * g.dh;
+            if (ih < 0 || ih >= g.H) {
+                continue;
+            }
+            const float4* row = x + ((n * g.H + ih) * g.W) * C4 + c4;
+            for (int64_t kw = 0; kw < g.KW; ++kw) {
+                const int64_t iw = w0 + kw * g.dw;
+                if (iw < 0 || iw >= g.W) {
+                    continue;
+                }
+                const float4 v = __ldg(row + iw * C4);
+                best.x = v.x > best.x ? v.x : best.x;
+                best.y = v.y > best.y ? v.y : best.y;
+                best.z = v.z > best.z ? v.z : best.z;
+                best.w = v.w > best.w ? v.w : best.w;
+            }
+        }
+        y[i] = best;
+    }
+}
+
+__global__ void maxpool2d_nhwc1_kernel(const float* __restrict__ x, float* __restrict__ y, PoolGeom g, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = i % g.C;
+        int64_t t = i / g.C;
+        const int64_t ow = t % g.OW;
+        t /= g.OW;
+        const int64_t oh = t % g.OH;
+        const int64_t n = t / g.OH;
+        const int64_t h0 = oh * g.sh - g.ph;
+        const int64_t w0 = ow * g.sw - g.pw;
+        float best = -INFINITY;
+        for (int64_t kh = 0; kh < g.KH; ++kh) {
+            const int64_t ih = h0 + kh * g.dh;
+            if (ih < 0 || ih >= g.H) {
+                continue;
+            }
+            for (int64_t kw = 0; kw < g.KW; ++kw) {
+                const int64_t iw = w0 + kw * g.dw;
+                if (iw < 0 || iw >= g.W) {
+                    continue;
+                }
+                const float v = __ldg(x + ((n * g.H + ih) * g.W + iw) * g.C + c);
+                best = v > best ? v : best;
+            }
+        }
+        y[i] = best;
+    }
+}
+
+// Channels-last spatial mean: a 32 x 8 block owns 32 channels of one image;
+// threadIdx.y strides the pixels, the 8 partial double sums meet in shared
+// memory. Reads are 128-byte coalesced along the channels.
+__global__ void mean_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t hw, int64_t C) {
+    __shared__ double part[8][33];
+    const int64_t c = blockIdx.x * 32 + threadIdx.x;
+    const int64_t n = blockIdx.y;
+    double s = 0.0;
+    if (c < C) {
+        const float* p = x + n * hw * C + c;
+        for (int64_t q = threadIdx.y; q < hw; q += 8) {
+            s += static_cast<double>(__ldg(p + q * C));
+        }
+    }
+    part[threadIdx.y][threadIdx.x] = s;
+    __syncthreads();
+    if (threadIdx.y == 0 && c < C) {
+        double t = 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            t += part[j][threadIdx.x];
+        }
+        y[n * C + c] = static_cast<float>(t / static_cast<double>(hw));
+    }
+}
+
 } // namespace
+
+void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {
+    const bool v4 = g.C % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    const int64_t total = g.N * g.OH * g.OW * (v4 ? g.C / 4 : g.C);
+    if (total <= 0) {
+        return;
+    }
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
+    if (v4) {
+        maxpool2d_nhwc4_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(
+            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), g, total);
+    } else {
+        maxpool2d_nhwc1_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
+    }
+    check_cuda(cudaGetLastError(), "maxpool_nhwc launch");
+}
+
+void mean_nhwc(nb2_device* dev, const float* x, float* y, int64_t n, int64_t hw, int64_t c) {
+    if (n <= 0 || c <= 0 || hw <= 0) {
+        return;
+    }
+    if (n > 65535) {
+        fail(kStatusUnsupported, "GlobalAveragePool: batch above 65535 in channels-last form");
+    }
+    const dim3 grid(static_cast<unsigned>((c + 31) / 32), static_cast<unsigned>(n), 1);
+    mean_nhwc_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(x, y, hw, c);
+    check_cuda(cudaGetLastError(), "mean_nhwc launch");
+}
 
 void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {
     const int64_t total = g.N * g.C * g.OH * g.OW;

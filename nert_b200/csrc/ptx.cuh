@@ -91,6 +91,20 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// 4-D im2col TMA load (NHWC activations): from the window start (w, h, n) of
+// the first output pixel, `pixelsPerColumn` consecutive output pixels x the
+// map's channelsPerPixel channels starting at channel c, at filter offset
+// (off_w, off_h); padding reads zeros. No multicast.
+__device__ __forceinline__ void tma_load_im2col_4d(void* dst, const CUtensorMap* map, int c, int w, int h, int n,
+                                                   uint16_t off_w, uint16_t off_h, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w),
+        "h"(off_h)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

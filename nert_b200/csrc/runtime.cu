@@ -42,6 +42,20 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+EncodeIm2colFn encode_im2col() {
+    static EncodeIm2colFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q),
+                   "cudaGetDriverEntryPoint(cuTensorMapEncodeIm2col)");
+        if (p == nullptr || q != cudaDriverEntryPointSuccess) {
+            fail(kStatusCuda, "cuTensorMapEncodeIm2col is unavailable");
+        }
+        return reinterpret_cast<EncodeIm2colFn>(p);
+    }();
+    return fn;
+}
+
 nb2_device* device(int ordinal) {
     if (ordinal < 0 || ordinal >= 64) {
         fail(kStatusInvalid, "device ordinal out of range");

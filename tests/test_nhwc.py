@@ -1,0 +1,116 @@
+"""Channels-last (NHWC) trunk of the B200 engine.
+
+The engine keeps a Conv trunk NHWC inside its arena (the Conv A operand then
+arrives by TMA im2col); graph inputs and outputs stay NCHW, so results must
+equal the all-NCHW path and the oracle. CPU tests check the layout assignment
+through the host-only planner; GPU tests run both layouts against the numpy
+restatement of the reference kernels (max|err| <= 1e-4 * max|ref|).
+"""
+
+import numpy as np
+import pytest
+
+from conftest import TOL, rel_err
+from nert_b200 import configs, model
+from oracle import np_ref
+
+# (id, batch, cin, h, w, c, m, kernel, strides, pads, dilations, residual, pool, gap)
+CHAINS = [
+    ("3x3s1_res", 2, 3, 20, 20, 32, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
+    ("3x3s2_m40", 2, 8, 16, 15, 64, 40, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1), False, False, False),
+    ("1x1s2_res", 2, 16, 14, 14, 64, 128, (1, 1), (2, 2), (0, 0, 0, 0), (1, 1), True, False, False),
+    ("7x7s2p3", 1, 3, 23, 29, 32, 32, (7, 7), (2, 2), (3, 3, 3, 3), (1, 1), False, False, False),
+    ("asym_pads", 2, 4, 17, 13, 32, 48, (3, 3), (2, 2), (0, 0, 1, 1), (1, 1), False, False, False),
+    ("dil2", 1, 5, 19, 21, 96, 64, (3, 3), (1, 1), (2, 2, 2, 2), (2, 2), False, False, False),
+    ("5x3_s3x1_m42", 2, 3, 25, 11, 32, 42, (5, 3), (3, 1), (2, 1, 2, 1), (1, 1), False, False, False),
+    ("pool_gap", 2, 3, 33, 31, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, True, True),
+    ("b4_56x56", 4, 16, 56, 56, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
+]
+
+
+def _chain(case):
+    _, n, cin, h, w, c, m, k, s, p, d, res, pool, gap = case
+    return configs.conv_chain(n, cin, h, w, c, m, kernel=k, strides=s, pads=p, dilations=d, residual=res,
+                              pool=pool, gap=gap, tag="nhwc_" + case[0])
+
+
+def _layout(g, flags=0):
+    a = model.analyze(g, {n: d for n, d, _ in g.inputs}, flags)
+    return {k: v["nhwc"] for k, v in a["tensors"].items()}
+
+
+@pytest.mark.parametrize("case", CHAINS, ids=[c[0] for c in CHAINS])
+def test_chain_layout_assignment(case):
+    g, _ = _chain(case)
+    lay = _layout(g)
+    io = {n for n, _, _ in g.inputs} | {o[0] for o in g.outputs}
+    assert not any(lay[t] for t in io), "graph inputs and outputs stay NCHW"
+    mid_in = [n for n in g.nodes if n.name == "mid"][0].inputs[0]
+    assert lay[mid_in], "the middle Conv reads channels-last"
+    assert not any(_layout(g, model.NCHW_ONLY).values())
+
+
+def test_resnet_trunk_is_channels_last_and_vit_is_not():
+    lay = _layout(configs.resnet18(1))
+    assert lay["maxpool_out"] and lay["layer4.1.relu_out_out"]
+    assert not lay["input"] and not lay["avgpool_out"] and not lay["fc_out"]
+    assert not any(_layout(configs.vit_b16(1, layers=1)).values())
+
+
+def test_grouped_and_narrow_convs_keep_their_input_nchw():
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    g = Graph(name="grp", opset=13)
+    x = g.add_input("x", [1, 8, 10, 10])
+    w0 = np.ones((32, 8, 1, 1), np.float32)
+    w1 = np.ones((32, 8, 3, 3), np.float32)
+    w2 = np.ones((24, 32, 1, 1), np.float32)
+    w3 = np.ones((8, 24, 1, 1), np.float32)
+    t0 = g.op("Conv", [x, g.const("w0", w0)], name="c0", kernel_shape=[1, 1])
+    t1 = g.op("Conv", [t0, g.const("w1", w1)], name="grouped", kernel_shape=[3, 3], pads=[1] * 4, group=4)
+    t2 = g.op("Conv", [t1, g.const("w2", w2)], name="c2", kernel_shape=[1, 1])
+    t3 = g.op("Conv", [t2, g.const("w3", w3)], name="narrow_in", kernel_shape=[1, 1])
+    y = g.op("Conv", [t3, g.const("w4", np.ones((8, 8, 1, 1), np.float32))], name="out", kernel_shape=[1, 1])
+    g.add_output(y, None, FLOAT)
+    lay = _layout(g)
+    assert not lay[t0]   # read by a grouped Conv
+    assert lay[t1]       # produced by a Conv, read by a C % 32 == 0 Conv
+    assert not lay[t2]   # 24 channels: TMA im2col needs C % 32 == 0
+    assert not lay[t3]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CHAINS, ids=[c[0] for c in CHAINS])
+def test_chain_channels_last_matches_nchw_and_oracle(cuda, case):
+    g, feed = _chain(case)
+    ref = np_ref.run(g, feed)
+    out_name = g.outputs[0][0]
+    outs = {}
+    for cl in (True, False):
+        m = model.Model(g, {k: list(v.shape) for k, v in feed.items()}, channels_last=cl)
+        try:
+            outs[cl] = m.run(feed)[out_name]
+            labels = [lab for lab, _ in m.profile()]
+        finally:
+            m.close()
+        assert any("nhwc" in lab for lab in labels) == cl, labels
+        assert rel_err(outs[cl], ref[out_name]) <= TOL, cl
+    assert rel_err(outs[True], outs[False]) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("builder,batch,out", [(configs.resnet18, 2, "fc_out"), (configs.resnet50, 1, None)])
+def test_resnet_channels_last_equals_nchw(cuda, builder, batch, out):
+    g = builder(batch)
+    x = configs.resnet_input(batch)
+    out = out or g.outputs[0][0]
+    res = {}
+    for cl in (True, False):
+        m = model.Model(g, {"input": list(x.shape)}, channels_last=cl)
+        try:
+            res[cl] = m.run({"input": x})[out]
+        finally:
+            m.close()
+    ref = np_ref.run(g, {"input": x})[out]
+    assert rel_err(res[True], ref) <= TOL
+    assert rel_err(res[False], ref) <= TOL
