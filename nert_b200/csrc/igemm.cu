@@ -67,23 +67,56 @@ struct Args {
     int* err;
 };
 
+constexpr int pow2_at_least(int v) {
+    int p = 32;
+    while (p < v) {
+        p *= 2;
+    }
+    return p;
+}
+
 template <int BN, bool THREE>
 struct Cfg {
+    // A operand in tensor memory (BN <= 64): the producers write the tf32
+    // hi/lo planes of A to TMEM with tcgen05.st and the MMA reads A from
+    // there, so shared memory only carries B (and A raw tiles that TMA
+    // brings). With a narrow B tile the MMA's A reads from shared memory
+    // would otherwise outweigh the tensor work. Wider tiles need all 512
+    // TMEM columns for the accumulators and keep A in shared memory.
+    static constexpr bool kATmem = BN <= 64;
     static constexpr int kAPlane = 128 * 128;
     static constexpr int kBPlane = BN * 128;
     static constexpr int kPlanes = THREE ? 2 : 1;
-    static constexpr int kStageBytes = (kAPlane + kBPlane) * kPlanes;
+    static constexpr int kBStageBytes = kBPlane * kPlanes;
+    // A in shared memory: one ring of stages [A hi][A lo][B hi][B lo].
+    // A in TMEM: a ring of raw A tiles (TMA-fed modes; released by the
+    // converter once read) and a ring of B tiles (released by the MMA), both
+    // kStages deep, plus kTStages TMEM A stages.
+    static constexpr int kStageBytes = kATmem ? kAPlane + kBStageBytes : (kAPlane + kBPlane) * kPlanes;
     static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
-    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     // two accumulators per tile (even / odd K blocks) x two tiles in flight
     static constexpr int kAccs = 2;
-    static constexpr int kTmemCols = 2 * kAccs * BN;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 512;
+    static constexpr int kAccCols = 2 * kAccs * BN;
+    static constexpr int kAStageCols = 32 * kPlanes; // hi plane, then lo plane
+    static constexpr int kTStagesRaw = (512 - kAccCols) / kAStageCols;
+    static constexpr int kMin3(int a, int b, int c) { return a < b ? (a < c ? a : c) : (b < c ? b : c); }
+    // A in TMEM: TMEM stage t == shared-memory stage s, so one MMA commit
+    // frees both
+    static constexpr int kStages = kATmem ? kMin3(kStagesRaw, kTStagesRaw, 8) : (kStagesRaw > 8 ? 8 : kStagesRaw);
+    static constexpr int kTStages = kATmem ? kStages : 0;
+    static constexpr int kTmemCols = pow2_at_least(kAccCols + kTStages * kAStageCols);
+    static constexpr int kRingBytes = kStages * kStageBytes;
+    static_assert(kTmemCols <= 512, "TMEM budget");
+    static constexpr int kSmemBytes = kRingBytes + 1024 + 512;
     static constexpr int kEpiWarps = 8;  // warps 0-7: epilogue (lane quarter w&3, column half w>>2)
     static constexpr int kProdWarps = 8; // warps 8-15: A producers
-    static constexpr int kTmaWarp = 16;
+    // One thread issues at most one TMA copy every few hundred cycles, so the
+    // copies of a K block are spread over three issuing warps.
+    static constexpr int kTmaWarp = 16;    // B hi plane
     static constexpr int kMmaWarp = 17;
-    static constexpr int kThreads = 18 * 32;
+    static constexpr int kTmaAWarp = 18;   // raw A tile (TMA-fed A modes)
+    static constexpr int kTmaBloWarp = 19; // B lo plane (3xTF32)
+    static constexpr int kThreads = 20 * 32;
 };
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -226,33 +259,78 @@ __device__ __forceinline__ bool produce_block(uint8_t* a_hi, uint8_t* a_lo, uint
     return true;
 }
 
+// tf32 hi/lo planes of 16 consecutive K values of one A row into TMEM:
+// columns [col, col+16) of the hi plane and [col+32, col+48) of the lo plane,
+// lane = the thread's row (the warp's lane quarter is fixed by its id).
+template <bool THREE>
+__device__ __forceinline__ void store16_tmem(uint32_t taddr, const float (&v)[16]) {
+    float h[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        h[i] = to_tf32(v[i]);
+    }
+    tmem_st16(taddr, h);
+    if (THREE) {
+        float l[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            l[i] = v[i] - h[i];
+        }
+        tmem_st16(taddr + 32, l);
+    }
+}
+
+// Publishes a TMEM A stage to the MMA issuer (one arrive per warp).
+__device__ __forceinline__ void publish_tmem(uint64_t* bar, int lane) {
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(bar);
+    }
+}
+
 // Persistent, warp-specialised contraction kernel: one CTA per SM walks the
 // output tiles (m fastest, so concurrent CTAs share the B tile in L2); the
 // TMEM accumulators are double buffered so the epilogue of one tile overlaps
 // the main loop of the next.
 template <int BN, bool THREE, int MODE>
-// 18 warps: some SM sub-partitions hold 5 of them, and each sub-partition has
-// 16K registers, so the launch allows at most 96 registers per thread.
-__global__ void __launch_bounds__(576, 1)
+// 20 warps: each SM sub-partition holds 5 of them and has 16K registers, so
+// the launch allows at most 96 registers per thread.
+__global__ void __launch_bounds__(640, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
                  const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a) {
     using C = Cfg<BN, THREE>;
     constexpr int S = C::kStages;
+    constexpr int ST = C::kTStages;
+    constexpr bool kATm = C::kATmem;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+    // A in shared memory: full_a = A planes written (producer warps), full_b =
+    // A raw (TMA-fed modes) and B landed, empty = stage consumed (MMA).
+    // A in TMEM: full_a = A raw landed, empty_a = A raw read (producer
+    // warps), full_b = B landed, t_full = TMEM A stage written (producer
+    // warps), empty = B stage and TMEM A stage consumed (MMA).
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + C::kRingBytes);
     uint64_t* full_b = full_a + S;
     uint64_t* empty = full_b + S;
-    uint64_t* acc_full = empty + S;  // [2]
+    uint64_t* empty_a = empty + S;
+    uint64_t* t_full = empty_a + S;
+    uint64_t* acc_full = t_full + ST;  // [2]
     uint64_t* acc_empty = acc_full + 2; // [2]
     uint64_t* mma_done = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    auto a_hi = [&](int s) { return smem + s * C::kStageBytes; };
+    // A in shared memory: stage s = [A hi][A lo][B hi][B lo]; A in TMEM: the
+    // raw A ring (S x 16 KB), then the B ring (S x [B hi][B lo])
+    auto a_hi = [&](int s) { return kATm ? smem + s * C::kAPlane : smem + s * C::kStageBytes; };
     auto a_lo = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane; };
-    auto b_hi = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane * C::kPlanes; };
-    auto b_lo = [&](int s) { return smem + s * C::kStageBytes + C::kAPlane * C::kPlanes + C::kBPlane; };
+    auto b_hi = [&](int s) {
+        return kATm ? smem + S * C::kAPlane + s * C::kBStageBytes
+                    : smem + s * C::kStageBytes + C::kAPlane * C::kPlanes;
+    };
+    auto b_lo = [&](int s) { return b_hi(s) + C::kBPlane; };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -264,9 +342,16 @@ __global__ void __launch_bounds__(576, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full_a[s], C::kProdWarps);
-            mbar_init(&full_b[s], 1);
+            mbar_init(&full_a[s], kATm ? 1 : C::kProdWarps);
+            // one arrival per issuing TMA thread that completes on full_b
+            mbar_init(&full_b[s], (THREE ? 2 : 1) + ((!kATm && (MODE == kADenseTma || MODE == kAConvNhwc)) ? 1 : 0));
             mbar_init(&empty[s], 1);
+            mbar_init(&empty_a[s], C::kProdWarps / 2);
+        }
+        for (int t = 0; t < ST; ++t) {
+            // TMA-fed A: one 4-warp converter group per item; gathered A: all
+            // 8 producer warps (each writes half of the columns)
+            mbar_init(&t_full[t], (MODE == kADenseTma || MODE == kAConvNhwc) ? C::kProdWarps / 2 : C::kProdWarps);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -280,7 +365,7 @@ __global__ void __launch_bounds__(576, 1)
     const int2* ktab = p.ktab;
     if constexpr (MODE == kAConvGeneric) {
         if (p.ktab_smem) {
-            int2* t = reinterpret_cast<int2*>(smem + S * C::kStageBytes + 512);
+            int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512);
             for (int k = threadIdx.x; k < nkb * 32; k += blockDim.x) {
                 t[k] = p.ktab[k];
             }
@@ -290,12 +375,6 @@ __global__ void __launch_bounds__(576, 1)
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::kTmemCols);
         tmem_relinquish();
-    }
-    if (warp == C::kTmaWarp && lane == 0) {
-        prefetch_tmap(&tm_hi);
-        if (THREE) {
-            prefetch_tmap(&tm_lo);
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -326,6 +405,50 @@ __global__ void __launch_bounds__(576, 1)
             const uint32_t items = static_cast<uint32_t>(((num_tiles - static_cast<int>(blockIdx.x) +
                                                            static_cast<int>(gridDim.x) - 1) /
                                                           static_cast<int>(gridDim.x)) * nkb);
+            if constexpr (kATm) {
+                // Two 4-warp groups take alternate items, so one group's TMEM
+                // stores overlap the other's loads. Thread = row r (its warp's
+                // lane quarter), all 32 K values: eight swizzled 16-byte
+                // chunks of the raw tile, released as soon as they are read.
+                // even ring depths: every use of a stage falls to one group,
+                // which waits on its phases in order
+                static_assert(S % 2 == 0 && ST % 2 == 0, "converter groups need even ring depths");
+                const int grp = pw >> 2;
+                const uint32_t tq = tmem + (static_cast<uint32_t>((pw & 3) * 32) << 16) + C::kAccCols;
+                for (g = static_cast<uint32_t>(grp); g < items; g += 2) {
+                    const int s = static_cast<int>(g % S);
+                    const int t = static_cast<int>(g % ST);
+                    if (!warp_wait(&full_a[s], (g / S) & 1u, abort_flag, p.err)) {
+                        break;
+                    }
+                    const uint32_t row = smem_u32(a_hi(s)) + r * 128;
+                    float v[32];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                                     : "=f"(v[4 * c]), "=f"(v[4 * c + 1]), "=f"(v[4 * c + 2]), "=f"(v[4 * c + 3])
+                                     : "r"(row + ((c ^ (r & 7)) << 4))
+                                     : "memory");
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&empty_a[s]);
+                    }
+                    // TMEM stage t == s is free once the MMA released stage s
+                    if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err)) {
+                        break;
+                    }
+                    const uint32_t ta = tq + t * C::kAStageCols;
+                    store16_tmem<THREE>(ta, *reinterpret_cast<const float(*)[16]>(&v[0]));
+                    store16_tmem<THREE>(ta + 16, *reinterpret_cast<const float(*)[16]>(&v[16]));
+                    // B landed too, so the MMA issuer waits on t_full alone
+                    if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err)) {
+                        break;
+                    }
+                    publish_tmem(&t_full[t], lane);
+                }
+                g = items; // the loop below has nothing left
+            }
             for (; g < items; ++g) {
                 const int s = static_cast<int>(g % S);
                 if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err)) {
@@ -408,25 +531,37 @@ __global__ void __launch_bounds__(576, 1)
             return true;
         };
         uint32_t g = 0; // global K-block counter (the smem ring spans tiles)
+        const uint32_t tq = tmem + (static_cast<uint32_t>((pw & 3) * 32) << 16) + C::kAccCols + half * 16;
+        auto produce = [&](const float (&v)[16]) -> bool {
+            if constexpr (kATm) {
+                const int t = static_cast<int>(g % ST);
+                if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err)) {
+                    return false;
+                }
+                store16_tmem<THREE>(tq + t * C::kAStageCols, v);
+                publish_tmem(&t_full[t], lane);
+                return true;
+            } else {
+                return produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, v,
+                                            abort_flag, p.err);
+            }
+        };
         float b0[16], b1[16], b2[16];
         bool h0 = next(b0);
         bool h1 = next(b1);
         while (true) {
             const bool h2 = next(b2);
-            if (!h0 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b0,
-                                             abort_flag, p.err)) {
+            if (!h0 || !produce(b0)) {
                 break;
             }
             ++g;
             h0 = next(b0);
-            if (!h1 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b1,
-                                             abort_flag, p.err)) {
+            if (!h1 || !produce(b1)) {
                 break;
             }
             ++g;
             h1 = next(b1);
-            if (!h2 || !produce_block<THREE>(a_hi(g % S), a_lo(g % S), empty, full_a, g, S, r, half, lane, b2,
-                                             abort_flag, p.err)) {
+            if (!h2 || !produce(b2)) {
                 break;
             }
             ++g;
@@ -527,9 +662,16 @@ __global__ void __launch_bounds__(576, 1)
                 mbar_arrive(&acc_empty[b]);
             }
         }
-    } else if (warp == C::kTmaWarp) {
-        // ---------------- TMA producer for B ----------------
-        if (lane == 0) {
+    } else if (warp == C::kTmaWarp || warp == C::kTmaAWarp || warp == C::kTmaBloWarp) {
+        // ---------------- TMA issuers: B hi, raw A, B lo ----------------
+        constexpr bool kTmaA = MODE == kADenseTma || MODE == kAConvNhwc;
+        const int role = warp == C::kTmaWarp ? 0 : warp == C::kTmaAWarp ? 1 : 2;
+        const bool active = role == 0 || (role == 1 && kTmaA) || (role == 2 && THREE);
+        // raw A lands on its own ring when A goes to TMEM
+        uint64_t* const my_full = (role == 1 && kATm) ? full_a : full_b;
+        if (lane == 0 && active) {
+            const CUtensorMap* map = role == 0 ? &tm_hi : role == 1 ? &tm_a : &tm_lo;
+            prefetch_tmap(map);
             uint32_t g = 0;
             bool alive = true;
             for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
@@ -547,28 +689,27 @@ __global__ void __launch_bounds__(576, 1)
                 for (int kb = 0; kb < nkb; ++kb, ++g) {
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.err)) {
+                    uint64_t* free_bar = (role == 1 && kATm) ? &empty_a[s] : &empty[s];
+                    if (!mbar_wait(free_bar, ph ^ 1u, abort_flag, p.err)) {
                         alive = false;
                         break;
                     }
-                    if constexpr (MODE == kADenseTma) {
-                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes + C::kAPlane);
-                        tma_load_2d(a_hi(s), &tm_a, kb * 32, z * p.a_zrows + m0, &full_b[s]);
-                    } else if constexpr (MODE == kAConvNhwc) {
-                        // K ordered (kh, kw, cin): block kb = (tap, 32-channel block)
-                        const int cblocks = p.Cg >> 5;
-                        const int tap = kb / cblocks;
-                        const int c0 = (kb - tap * cblocks) * 32;
-                        const int kh = tap / p.KW, kw = tap - (tap / p.KW) * p.KW;
-                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes + C::kAPlane);
-                        tma_load_im2col_4d(a_hi(s), &tm_a, c0, nw0, nh0, nn0, static_cast<uint16_t>(kw * p.dw),
-                                           static_cast<uint16_t>(kh * p.dh), &full_b[s]);
+                    if (role == 1) {
+                        mbar_arrive_expect_tx(&my_full[s], C::kAPlane);
+                        if constexpr (MODE == kADenseTma) {
+                            tma_load_2d(a_hi(s), &tm_a, kb * 32, z * p.a_zrows + m0, &my_full[s]);
+                        } else if constexpr (MODE == kAConvNhwc) {
+                            // K ordered (kh, kw, cin): block kb = (tap, 32-channel block)
+                            const int cblocks = p.Cg >> 5;
+                            const int tap = kb / cblocks;
+                            const int c0 = (kb - tap * cblocks) * 32;
+                            const int kh = tap / p.KW, kw = tap - (tap / p.KW) * p.KW;
+                            tma_load_im2col_4d(a_hi(s), &tm_a, c0, nw0, nh0, nn0, static_cast<uint16_t>(kw * p.dw),
+                                               static_cast<uint16_t>(kh * p.dh), &my_full[s]);
+                        }
                     } else {
-                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane * C::kPlanes);
-                    }
-                    tma_load_2d(b_hi(s), &tm_hi, kb * 32, row, &full_b[s]);
-                    if (THREE) {
-                        tma_load_2d(b_lo(s), &tm_lo, kb * 32, row, &full_b[s]);
+                        mbar_arrive_expect_tx(&full_b[s], C::kBPlane);
+                        tma_load_2d(role == 0 ? b_hi(s) : b_lo(s), map, kb * 32, row, &full_b[s]);
                     }
                 }
             }
@@ -576,12 +717,12 @@ __global__ void __launch_bounds__(576, 1)
             const uint32_t issued = g;
             for (uint32_t q = issued > S ? issued - S : 0; q < issued; ++q) {
                 const long long t0 = clock64();
-                while (!mbar_try_wait(&full_b[q % S], (q / S) & 1u) && clock64() - t0 < kWaitBoundCycles) {
+                while (!mbar_try_wait(&my_full[q % S], (q / S) & 1u) && clock64() - t0 < kWaitBoundCycles) {
                 }
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp == C::kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(128, BN);
@@ -598,7 +739,12 @@ __global__ void __launch_bounds__(576, 1)
                 for (int kb = 0; kb < nkb; ++kb, ++g) {
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
-                    if (!mbar_wait(&full_a[s], ph, abort_flag, p.err) || !mbar_wait(&full_b[s], ph, abort_flag, p.err)) {
+                    const int t = s; // TMEM A stage (A in TMEM)
+                    // TMA-fed A: the converter publishes only after B landed
+                    constexpr bool kOneWait = MODE == kADenseTma || MODE == kAConvNhwc;
+                    uint64_t* a_ready = kATm ? &t_full[t] : &full_a[s];
+                    if (!mbar_wait(a_ready, ph, abort_flag, p.err) ||
+                        (!kOneWait && !mbar_wait(&full_b[s], ph, abort_flag, p.err))) {
                         alive = false;
                         break;
                     }
@@ -606,19 +752,37 @@ __global__ void __launch_bounds__(576, 1)
                     const uint32_t d = d0 + static_cast<uint32_t>((kb & 1) * BN);
                     const uint32_t ah = smem_u32(a_hi(s)), al = smem_u32(a_lo(s));
                     const uint32_t bh = smem_u32(b_hi(s)), bl = smem_u32(b_lo(s));
+                    if constexpr (kATm) {
+                        const uint32_t at = tmem + C::kAccCols + static_cast<uint32_t>(t * C::kAStageCols);
+                        // a K step of 8 tf32 is 32 bytes: +2 in the descriptor's address field
+                        const uint64_t bdh0 = sdesc_k128(bh), bdl0 = sdesc_k128(bl);
+                        const uint32_t first = kb < 2 ? 0u : 1u;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint32_t acc = kk == 0 ? first : 1u;
+                            if (THREE) {
+                                mma_tf32_ta(d, at + 32 + kk * 8, bdh0 + 2 * kk, idesc, acc);
+                                mma_tf32_ta(d, at + kk * 8, bdl0 + 2 * kk, idesc, 1u);
+                                mma_tf32_ta(d, at + kk * 8, bdh0 + 2 * kk, idesc, 1u);
+                            } else {
+                                mma_tf32_ta(d, at + kk * 8, bdh0 + 2 * kk, idesc, acc);
+                            }
+                        }
+                        mma_commit(&empty[s]);
+                        continue;
+                    }
+                    const uint64_t adh0 = sdesc_k128(ah), adl0 = sdesc_k128(al);
+                    const uint64_t bdh0 = sdesc_k128(bh), bdl0 = sdesc_k128(bl);
+                    const uint32_t first = kb < 2 ? 0u : 1u;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t first = (kb < 2 && kk == 0) ? 0u : 1u;
-                        const uint64_t adh = sdesc_k128(ah + kk * 32);
-                        const uint64_t bdh = sdesc_k128(bh + kk * 32);
+                        const uint32_t acc = kk == 0 ? first : 1u;
                         if (THREE) {
-                            const uint64_t adl = sdesc_k128(al + kk * 32);
-                            const uint64_t bdl = sdesc_k128(bl + kk * 32);
-                            mma_tf32(d, adl, bdh, idesc, first);
-                            mma_tf32(d, adh, bdl, idesc, 1u);
-                            mma_tf32(d, adh, bdh, idesc, 1u);
+                            mma_tf32(d, adl0 + 2 * kk, bdh0 + 2 * kk, idesc, acc);
+                            mma_tf32(d, adh0 + 2 * kk, bdl0 + 2 * kk, idesc, 1u);
+                            mma_tf32(d, adh0 + 2 * kk, bdh0 + 2 * kk, idesc, 1u);
                         } else {
-                            mma_tf32(d, adh, bdh, idesc, first);
+                            mma_tf32(d, adh0 + 2 * kk, bdh0 + 2 * kk, idesc, acc);
                         }
                     }
                     mma_commit(&empty[s]);

@@ -4,6 +4,10 @@
     python -m nert_b200.probe gemm M N K [REPS]
     python -m nert_b200.probe maxpool N C H W K STRIDE PAD [REPS]
     python -m nert_b200.probe resnet18 BATCH [REPS]
+    python -m nert_b200.probe chain N C H W M K STRIDE PAD [REPS]
+        (engine graph: 1x1 Conv 16->C, the KxK Conv C->M reading and writing
+        channels-last, 1x1 Conv M->16; the middle Conv is the second igemm
+        launch of each run)
 
 Inputs are seeded synthetic data; each mode prints one line with the
 geometry and exits 0 on success.
@@ -57,6 +61,19 @@ def main(argv):
         for _ in range(reps):
             out = m.run({"input": x})
         print("resnet18", out["fc_out"].shape)
+    elif mode == "chain":
+        from . import configs
+        from .model import Model
+
+        n, c, h, w, m_, k, s, p = (int(v) for v in argv[1:9])
+        reps = int(argv[9]) if len(argv) > 9 else 3
+        g, feed = configs.conv_chain(n, 16, h, w, c, m_, kernel=(k, k), strides=(s, s), pads=(p,) * 4,
+                                     tag="probe")
+        m = Model(g, {"x": list(feed["x"].shape)})
+        for _ in range(reps):
+            out = m.run(feed)
+        m.close()
+        print("chain", next(iter(out.values())).shape)
     else:
         raise SystemExit(__doc__)
     return 0
