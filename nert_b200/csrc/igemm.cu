@@ -108,15 +108,18 @@ struct Cfg {
     static constexpr int kRingBytes = kStages * kStageBytes;
     static_assert(kTmemCols <= 512, "TMEM budget");
     static constexpr int kSmemBytes = kRingBytes + 1024 + 512;
-    static constexpr int kEpiWarps = 8;  // warps 0-7: epilogue (lane quarter w&3, column half w>>2)
-    static constexpr int kProdWarps = 8; // warps 8-15: A producers
-    // One thread issues at most one TMA copy every few hundred cycles, so the
-    // copies of a K block are spread over three issuing warps.
-    static constexpr int kTmaWarp = 16;    // B hi plane
-    static constexpr int kMmaWarp = 17;
-    static constexpr int kTmaAWarp = 18;   // raw A tile (TMA-fed A modes)
-    static constexpr int kTmaBloWarp = 19; // B lo plane (3xTF32)
-    static constexpr int kThreads = 20 * 32;
+    static constexpr int kEpiWarps = 4;  // warps 0-3: epilogue (warp w = TMEM lane quarter w, all columns)
+    static constexpr int kProdWarps = 8; // warps 4-11: A producers (lane quarter w&3, K half)
+    // One thread issues at most one TMA copy every few hundred cycles, and
+    // one tcgen05.mma per ~50 cycles whatever its width, so the copies of a
+    // K block are spread over three issuing warps and the MMAs over two
+    // threads (even and odd K blocks, which feed separate accumulators).
+    static constexpr int kTmaWarp = 12;    // B hi plane
+    static constexpr int kMmaWarp = 13;    // even K blocks
+    static constexpr int kTmaAWarp = 14;   // raw A tile (TMA-fed A modes)
+    static constexpr int kTmaBloWarp = 15; // B lo plane (3xTF32)
+    static constexpr int kMma2Warp = 16;   // odd K blocks
+    static constexpr int kThreads = 17 * 32;
 };
 
 __device__ __forceinline__ float apply_act(float v, int act) {
@@ -295,8 +298,9 @@ __device__ __forceinline__ void publish_tmem(uint64_t* bar, int lane) {
 // TMEM accumulators are double buffered so the epilogue of one tile overlaps
 // the main loop of the next.
 template <int BN, bool THREE, int MODE>
-// 20 warps: each SM sub-partition holds 5 of them and has 16K registers, so
-// the launch allows at most 96 registers per thread.
+// 17 warps: an SM sub-partition holds up to 5 of them and has 16K
+// registers, so a thread may use at most 96 (the bound below is 640 threads
+// to make the compiler keep to that).
 __global__ void __launch_bounds__(640, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
                  const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a) {
@@ -354,10 +358,10 @@ __global__ void __launch_bounds__(640, 1)
             mbar_init(&t_full[t], (MODE == kADenseTma || MODE == kAConvNhwc) ? C::kProdWarps / 2 : C::kProdWarps);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_full[b], 2); // both MMA issuers commit
             mbar_init(&acc_empty[b], C::kEpiWarps);
         }
-        mbar_init(mma_done, 1);
+        mbar_init(mma_done, 2);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -570,7 +574,8 @@ __global__ void __launch_bounds__(640, 1)
     } else if (warp < C::kEpiWarps) {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3;                // TMEM lanes quarter*32 .. +31
-        const int col_lo = (warp >> 2) * (BN / 2);    // this warp's half of the columns
+        constexpr int kCols = BN / (C::kEpiWarps / 4); // columns per warp
+        const int col_lo = (warp >> 2) * kCols;
         int i = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
             int z, m0, n0;
@@ -601,7 +606,7 @@ __global__ void __launch_bounds__(640, 1)
             const uint32_t acc0 = tmem + lane_base + static_cast<uint32_t>(b * C::kAccs * BN);
             const bool two = nkb > 1;
 #pragma unroll 1
-            for (int cc = col_lo; cc < col_lo + BN / 2; cc += 16) {
+            for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
                 if (n0 + cc >= p.N) {
                     break; // warp-uniform: the rest of this half is padding
                 }
@@ -722,9 +727,10 @@ __global__ void __launch_bounds__(640, 1)
             }
         }
         __syncwarp();
-    } else if (warp == C::kMmaWarp) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == C::kMmaWarp || warp == C::kMma2Warp) {
+        // ---------------- MMA issuers: even / odd K blocks ----------------
         if (lane == 0) {
+            const int par = warp == C::kMmaWarp ? 0 : 1;
             constexpr uint32_t idesc = idesc_tf32(128, BN);
             uint32_t g = 0;
             int i = 0;
@@ -737,6 +743,9 @@ __global__ void __launch_bounds__(640, 1)
                 tc_fence_after();
                 const uint32_t d0 = tmem + static_cast<uint32_t>(b * C::kAccs * BN);
                 for (int kb = 0; kb < nkb; ++kb, ++g) {
+                    if ((kb & 1) != par) {
+                        continue; // the other issuer's K block
+                    }
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
                     const int t = s; // TMEM A stage (A in TMEM)
