@@ -9,6 +9,7 @@
 #include "../ops_norm.cuh"
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <list>
 #include <set>
@@ -33,6 +34,8 @@ struct ExecNode {
     std::string residual;          // fused residual Add operand
     std::string bias;              // fused MatMul bias (Add of a constant [N])
     int act = kActNone;
+    float act_a = 0.f, act_b = 0.f, act_c = 0.f; // GELU constants
+    float alpha = 1.f;                           // fused scale (Div / Mul by a power of two)
     int pos = 0;
     bool alias = false; // output is a view of input 0
     int group = 1;      // nodes in the group
@@ -90,8 +93,37 @@ std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInf
         const bool mm_const_b = n.op == "MatMul" && g.constants.count(n.inputs[1]) &&
                                 g.constants.at(n.inputs[1]).dims.size() == 2 &&
                                 shapes.at(n.inputs[0]).dims.size() >= 2;
-        if (enable && (n.op == "Conv" || n.op == "Gemm" || mm_const_b)) {
+        const bool mm = n.op == "MatMul" && shapes.at(n.inputs[0]).dims.size() >= 2 &&
+                        shapes.at(n.inputs[1]).dims.size() >= 2;
+        // a float scalar constant
+        auto scalar_of = [&](const std::string& t, float& v) {
+            auto c = g.constants.find(t);
+            if (c == g.constants.end() || c->second.dtype != DType::F32 || c->second.count() != 1) {
+                return false;
+            }
+            std::memcpy(&v, c->second.bytes.data(), 4);
+            return true;
+        };
+        if (enable && (n.op == "Conv" || n.op == "Gemm" || mm)) {
             std::string cur = e.out;
+            if (mm && !mm_const_b) {
+                // QK^T / sqrt(d): a Div (or Mul) by a power of two is exact as
+                // the epilogue's alpha
+                const int j = single(cur);
+                float c = 0.f;
+                if (j >= 0 && (g.nodes[j].op == "Div" || g.nodes[j].op == "Mul") && g.nodes[j].inputs[0] == cur &&
+                    scalar_of(g.nodes[j].inputs[1], c) && c != 0.f) {
+                    int ex = 0;
+                    const float m = std::frexp(c, &ex);
+                    if (m == 0.5f || m == -0.5f) {
+                        e.alpha = g.nodes[j].op == "Div" ? 1.0f / c : c;
+                        absorbed[j] = true;
+                        e.pos = j;
+                        e.group++;
+                        cur = g.nodes[j].outputs[0];
+                    }
+                }
+            }
             if (mm_const_b) {
                 const int j = single(cur);
                 if (j >= 0 && g.nodes[j].op == "Add") {
@@ -131,6 +163,49 @@ std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInf
                 e.pos = j;
                 e.group++;
                 cur = g.nodes[j].outputs[0];
+            } else if (!outputs.count(cur) && consumers.count(cur) && consumers[cur].size() == 2 &&
+                       (g.nodes[consumers[cur][0]].op == "Div" || g.nodes[consumers[cur][1]].op == "Div")) {
+                // GELU, erf form: Div(cur, a) -> Erf -> Add(., b) -> Mul(cur, .) -> Mul(., c)
+                const int c0 = consumers[cur][0], c1 = consumers[cur][1];
+                const int dv = g.nodes[c0].op == "Div" ? c0 : c1;
+                const int m1 = dv == c0 ? c1 : c0;
+                float a = 0.f, b = 0.f, c = 0.f;
+                const Node& div = g.nodes[dv];
+                const int ef = div.inputs[0] == cur && scalar_of(div.inputs[1], a) && a != 0.f ? single(div.outputs[0])
+                                                                                              : -1;
+                const int ad = ef >= 0 && g.nodes[ef].op == "Erf" ? single(g.nodes[ef].outputs[0]) : -1;
+                int mu = -1;
+                if (ad >= 0 && g.nodes[ad].op == "Add") {
+                    const Node& add = g.nodes[ad];
+                    const std::string eo = g.nodes[ef].outputs[0];
+                    const std::string other = add.inputs[0] == eo ? add.inputs[1] : add.inputs[0];
+                    if (scalar_of(other, b)) {
+                        mu = single(add.outputs[0]);
+                    }
+                }
+                int m2 = -1;
+                if (mu == m1 && !absorbed[m1] && g.nodes[m1].op == "Mul") {
+                    const Node& mul = g.nodes[m1];
+                    const std::string ao = g.nodes[ad].outputs[0];
+                    const bool pair = (mul.inputs[0] == cur && mul.inputs[1] == ao) ||
+                                      (mul.inputs[1] == cur && mul.inputs[0] == ao);
+                    m2 = pair ? single(mul.outputs[0]) : -1;
+                }
+                if (m2 >= 0 && g.nodes[m2].op == "Mul") {
+                    const Node& h = g.nodes[m2];
+                    const std::string mo = g.nodes[m1].outputs[0];
+                    const std::string other = h.inputs[0] == mo ? h.inputs[1] : h.inputs[0];
+                    if (scalar_of(other, c) && !absorbed[dv] && !absorbed[ef] && !absorbed[ad] && !absorbed[m2]) {
+                        e.act = kActGeluErf;
+                        e.act_a = a;
+                        e.act_b = b;
+                        e.act_c = c;
+                        absorbed[dv] = absorbed[ef] = absorbed[ad] = absorbed[m1] = absorbed[m2] = true;
+                        e.pos = std::max({dv, ef, ad, m1, m2});
+                        e.group += 5;
+                        cur = h.outputs[0];
+                    }
+                }
             } else if (!outputs.count(cur) && consumers.count(cur) && consumers[cur].size() == 2) {
                 // SiLU: Sigmoid(cur) feeding only Mul(cur, sigmoid)
                 const int c0 = consumers[cur][0], c1 = consumers[cur][1];
@@ -595,6 +670,9 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             ep.bias = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;
             ep.res = e.residual.empty() ? nullptr : F(e.residual);
             ep.act = e.act;
+            ep.act_a = e.act_a;
+            ep.act_b = e.act_b;
+            ep.act_c = e.act_c;
             const float* x = F(n.inputs[0]);
             float* y = F(e.out);
             const int64_t pbytes = static_cast<int64_t>(conv_packed_bytes(geom));
@@ -705,6 +783,10 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 }
             }
             ep.act = e.act;
+            ep.act_a = e.act_a;
+            ep.act_b = e.act_b;
+            ep.act_c = e.act_c;
+            ep.alpha *= e.alpha;
             const float* A = F(n.inputs[0]);
             float* y = F(e.out);
             const int64_t pbytes = static_cast<int64_t>(gemm_packed_bytes(gg));

@@ -64,6 +64,7 @@ struct Args {
     float res_scale;
     float alpha;
     int act;
+    float act_a, act_b, act_c; // GELU (erf form) constants
     int* err;
 };
 
@@ -107,7 +108,6 @@ struct Cfg {
     static constexpr int kTmemCols = pow2_at_least(kAccCols + kTStages * kAStageCols);
     static constexpr int kRingBytes = kStages * kStageBytes;
     static_assert(kTmemCols <= 512, "TMEM budget");
-    static constexpr int kSmemBytes = kRingBytes + 1024 + 512;
     static constexpr int kEpiWarps = 4;  // warps 0-3: epilogue (warp w = TMEM lane quarter w, all columns)
     static constexpr int kProdWarps = 8; // warps 4-11: A producers (lane quarter w&3, K half)
     // One thread issues at most one TMA copy every few hundred cycles, and
@@ -120,17 +120,32 @@ struct Cfg {
     static constexpr int kTmaBloWarp = 15; // B lo plane (3xTF32)
     static constexpr int kMma2Warp = 16;   // odd K blocks
     static constexpr int kThreads = 17 * 32;
+    // epilogue staging: one 32 x 17 fp32 tile per epilogue warp (row-major
+    // outputs are written as 64-byte row pieces, not one column per lane)
+    static constexpr int kEpiTileFloats = 32 * 17;
+    static constexpr int kEpiBytes = kEpiWarps * kEpiTileFloats * 4;
+    static constexpr int kSmemBytes = kRingBytes + 1024 + 512 + kEpiBytes;
 };
 
-__device__ __forceinline__ float apply_act(float v, int act) {
-    switch (act) {
-    case kActRelu:
+template <int A>
+struct ActTag {
+    static constexpr int value = A;
+};
+
+// Fused activation, resolved at compile time. The GELU form is the ONNX
+// export's op sequence, kept in order so the fused value equals the unfused
+// rows': ((x * (erf(x / a) + b)) * c).
+template <int ACT>
+__device__ __forceinline__ float act_of(float v, const Args& p) {
+    if constexpr (ACT == kActGeluErf) {
+        return (v * (erff(v / p.act_a) + p.act_b)) * p.act_c;
+    } else if constexpr (ACT == kActRelu) {
         return v > 0.0f ? v : 0.0f;
-    case kActSilu:
+    } else if constexpr (ACT == kActSilu) {
         return v * (1.0f / (1.0f + expf(-v)));
-    case kActSigmoid:
+    } else if constexpr (ACT == kActSigmoid) {
         return 1.0f / (1.0f + expf(-v));
-    default:
+    } else {
         return v;
     }
 }
@@ -369,7 +384,7 @@ __global__ void __launch_bounds__(640, 1)
     const int2* ktab = p.ktab;
     if constexpr (MODE == kAConvGeneric) {
         if (p.ktab_smem) {
-            int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512);
+            int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512 + C::kEpiBytes);
             for (int k = threadIdx.x; k < nkb * 32; k += blockDim.x) {
                 t[k] = p.ktab[k];
             }
@@ -573,99 +588,172 @@ __global__ void __launch_bounds__(640, 1)
         }
     } else if (warp < C::kEpiWarps) {
         // ---------------- epilogue ----------------
-        const int quarter = warp & 3;                // TMEM lanes quarter*32 .. +31
+        // The activation is a template argument of the tile loop (one switch
+        // per launch, not per element); per-element work is two FMAs, the
+        // activation and the store.
+        const int quarter = warp & 3;                  // TMEM lanes quarter*32 .. +31
         constexpr int kCols = BN / (C::kEpiWarps / 4); // columns per warp
         const int col_lo = (warp >> 2) * kCols;
-        int i = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
-            int z, m0, n0;
-            decode(t, z, m0, n0);
-            const int b = i & 1;
-            if (!warp_wait(&acc_full[b], (i >> 1) & 1, abort_flag, p.err)) {
-                break;
-            }
-            tc_fence_after();
-            const int row = m0 + quarter * 32 + lane;
-            const bool row_ok = row < p.M;
-            int64_t row_off;
-            int64_t col_stride;
-            if (p.conv_out) {
-                const int mm = row_ok ? row : 0;
-                const int n_img = mm / (int)p.OHW;
-                const int pix = mm - n_img * (int)p.OHW;
-                row_off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix;
-                col_stride = p.OHW;
-            } else {
-                row_off = (int64_t)z * p.out_zstride + (int64_t)(row_ok ? row : 0) * p.ldc;
-                col_stride = 1;
-            }
-            const float* __restrict__ bias = p.bias ? p.bias + (int64_t)z * p.bias_zstride : nullptr;
-            const float* __restrict__ res = p.res;
-            float* __restrict__ out = p.out;
-            const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-            const uint32_t acc0 = tmem + lane_base + static_cast<uint32_t>(b * C::kAccs * BN);
-            const bool two = nkb > 1;
+        float* const stile = reinterpret_cast<float*>(smem + C::kRingBytes + 512) + warp * C::kEpiTileFloats;
+        // 0: NCHW conv output, 1: row-major with 16-byte rows, 2: other row-major
+        const int path = p.conv_out ? 0 : (p.vec_out ? 1 : 2);
+        auto tiles = [&](auto act_tag) {
+            constexpr int ACT = decltype(act_tag)::value;
+            int i = 0;
+            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+                int z, m0, n0;
+                decode(t, z, m0, n0);
+                const int b = i & 1;
+                if (!warp_wait(&acc_full[b], (i >> 1) & 1, abort_flag, p.err)) {
+                    break;
+                }
+                tc_fence_after();
+                const int row = m0 + quarter * 32 + lane;
+                const bool row_ok = row < p.M;
+                int64_t row_off;
+                int64_t col_stride;
+                if (path == 0) {
+                    const int mm = row_ok ? row : 0;
+                    const int n_img = mm / (int)p.OHW;
+                    const int pix = mm - n_img * (int)p.OHW;
+                    row_off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix;
+                    col_stride = p.OHW;
+                } else {
+                    row_off = (int64_t)z * p.out_zstride + (int64_t)(row_ok ? row : 0) * p.ldc;
+                    col_stride = 1;
+                }
+                const float* __restrict__ bias = p.bias ? p.bias + (int64_t)z * p.bias_zstride : nullptr;
+                const float* __restrict__ res = p.res;
+                float* __restrict__ out = p.out;
+                const float alpha = p.alpha, bsc = p.bias_scale, rsc = p.res_scale;
+                const uint32_t acc0 = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                      static_cast<uint32_t>(b * C::kAccs * BN);
+                const bool two = nkb > 1;
 #pragma unroll 1
-            for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
-                if (n0 + cc >= p.N) {
-                    break; // warp-uniform: the rest of this half is padding
-                }
-                float v0[16], v1[16], rv[16], bv[16];
-                tmem_ld16(acc0 + cc, v0);
-                if (two) {
-                    tmem_ld16(acc0 + BN + cc, v1);
-                }
-                if (p.vec_out && n0 + cc + 16 <= p.N) {
-                    // row-contiguous output: 16-byte loads and stores
-                    const int64_t o = row_off + n0 + cc;
-#pragma unroll
-                    for (int j = 0; j < 16; j += 4) {
-                        const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias + n0 + cc + j))
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                        const float4 r4 = (res && row_ok) ? __ldg(reinterpret_cast<const float4*>(res + o + j))
-                                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                        bv[j] = b4.x, bv[j + 1] = b4.y, bv[j + 2] = b4.z, bv[j + 3] = b4.w;
-                        rv[j] = r4.x, rv[j + 1] = r4.y, rv[j + 2] = r4.z, rv[j + 3] = r4.w;
+                for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
+                    if (n0 + cc >= p.N) {
+                        break; // warp-uniform: the rest is padding
                     }
-                    if (row_ok) {
+                    float v[16];
+                    {
+                        float v1[16];
+                        tmem_ld16(acc0 + cc, v);
+                        if (two) {
+                            tmem_ld16(acc0 + BN + cc, v1);
 #pragma unroll
-                        for (int j = 0; j < 16; j += 4) {
-                            float4 w;
-                            float* wv = &w.x;
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const float acc = two ? v0[j + q] + v1[j + q] : v0[j + q];
-                                wv[q] = apply_act(p.alpha * acc + p.bias_scale * bv[j + q] + p.res_scale * rv[j + q],
-                                                  p.act);
+                            for (int j = 0; j < 16; ++j) {
+                                v[j] += v1[j];
                             }
-                            *reinterpret_cast<float4*>(out + o + j) = w;
                         }
                     }
-                    continue;
-                }
-                // issue every load of the chunk before any store
+                    if (path == 2) {
+                        // rows not 16-byte aligned: through this warp's shared
+                        // tile, so a store writes two 64-byte row pieces
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + cc + j;
-                    const bool ok = row_ok && n < p.N;
-                    bv[j] = (bias && n < p.N) ? __ldg(bias + n) : 0.0f;
-                    rv[j] = (res && ok) ? __ldg(res + row_off + (int64_t)n * col_stride) : 0.0f;
-                }
+                        for (int j = 0; j < 16; ++j) {
+                            stile[lane * 17 + j] = v[j];
+                        }
+                        __syncwarp();
+                        const int jj = lane & 15, hr = lane >> 4;
+                        const int col = n0 + cc + jj;
+                        const bool col_ok = col < p.N;
+                        const float bl = (bias && col_ok) ? bsc * __ldg(bias + col) : 0.0f;
+                        const int lim = p.M - (m0 + quarter * 32) - hr; // rows 2*rr + hr < M
+                        const int64_t base = (int64_t)z * p.out_zstride + (int64_t)(m0 + quarter * 32 + hr) * p.ldc + col;
+                        float* o = out + base;
+                        const float* ro = res ? res + base : nullptr;
+                        const int ld2 = 2 * static_cast<int>(p.ldc);
+                        const float* sp = stile + hr * 17 + jj;
+                        if (col_ok) {
+                            if (ro) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + cc + j;
-                    if (row_ok && n < p.N) {
-                        const float acc = two ? v0[j] + v1[j] : v0[j];
-                        float v = p.alpha * acc + p.bias_scale * bv[j] + p.res_scale * rv[j];
-                        out[row_off + (int64_t)n * col_stride] = apply_act(v, p.act);
+                                for (int rr = 0; rr < 16; ++rr) {
+                                    if (2 * rr < lim) {
+                                        const float x = fmaf(rsc, __ldg(ro + rr * ld2), fmaf(alpha, sp[rr * 34], bl));
+                                        o[rr * ld2] = act_of<ACT>(x, p);
+                                    }
+                                }
+                            } else {
+#pragma unroll
+                                for (int rr = 0; rr < 16; ++rr) {
+                                    if (2 * rr < lim) {
+                                        o[rr * ld2] = act_of<ACT>(fmaf(alpha, sp[rr * 34], bl), p);
+                                    }
+                                }
+                            }
+                        }
+                        __syncwarp();
+                    } else if (path == 1) {
+                        // 16-byte rows: four vector stores per thread
+                        if (row_ok && n0 + cc + 16 <= p.N) {
+                            const int64_t o = row_off + n0 + cc;
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4) {
+                                float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), rv = bb;
+                                if (bias) {
+                                    bb = __ldg(reinterpret_cast<const float4*>(bias + n0 + cc + j));
+                                }
+                                if (res) {
+                                    rv = __ldg(reinterpret_cast<const float4*>(res + o + j));
+                                }
+                                float4 w;
+                                w.x = act_of<ACT>(fmaf(rsc, rv.x, fmaf(alpha, v[j], bsc * bb.x)), p);
+                                w.y = act_of<ACT>(fmaf(rsc, rv.y, fmaf(alpha, v[j + 1], bsc * bb.y)), p);
+                                w.z = act_of<ACT>(fmaf(rsc, rv.z, fmaf(alpha, v[j + 2], bsc * bb.z)), p);
+                                w.w = act_of<ACT>(fmaf(rsc, rv.w, fmaf(alpha, v[j + 3], bsc * bb.w)), p);
+                                *reinterpret_cast<float4*>(out + o + j) = w;
+                            }
+                        } else if (row_ok) {
+                            for (int j = 0; j < 16 && n0 + cc + j < p.N; ++j) {
+                                const int n = n0 + cc + j;
+                                const float bb = bias ? __ldg(bias + n) : 0.0f;
+                                const float rv = res ? __ldg(res + row_off + n) : 0.0f;
+                                out[row_off + n] = act_of<ACT>(fmaf(rsc, rv, fmaf(alpha, v[j], bsc * bb)), p);
+                            }
+                        }
+                    } else {
+                        // NCHW: a lane's row is a pixel, so each store covers 32
+                        // consecutive pixels of one channel
+                        float rv[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = n0 + cc + j;
+                            rv[j] = (res && row_ok && n < p.N) ? __ldg(res + row_off + (int64_t)n * col_stride) : 0.0f;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = n0 + cc + j;
+                            if (row_ok && n < p.N) {
+                                const float bb = bias ? __ldg(bias + n) : 0.0f;
+                                out[row_off + (int64_t)n * col_stride] =
+                                    act_of<ACT>(fmaf(rsc, rv[j], fmaf(alpha, v[j], bsc * bb)), p);
+                            }
+                        }
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[b]);
+                }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&acc_empty[b]);
-            }
+        };
+        switch (p.act) {
+        case kActRelu:
+            tiles(ActTag<kActRelu>{});
+            break;
+        case kActSilu:
+            tiles(ActTag<kActSilu>{});
+            break;
+        case kActSigmoid:
+            tiles(ActTag<kActSigmoid>{});
+            break;
+        case kActGeluErf:
+            tiles(ActTag<kActGeluErf>{});
+            break;
+        default:
+            tiles(ActTag<kActNone>{});
+            break;
         }
     } else if (warp == C::kTmaWarp || warp == C::kTmaAWarp || warp == C::kTmaBloWarp) {
         // ---------------- TMA issuers: B hi, raw A, B lo ----------------
@@ -955,7 +1043,7 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
                  (a.res == nullptr || al16(a.res)) && (a.bias == nullptr || (al16(a.bias) && a.bias_zstride % 4 == 0)))
                     ? 1
                     : 0;
-    a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 24576) ? 1 : 0;
+    a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 16384) ? 1 : 0;
     // row-major A with 16-byte rows: TMA it (a zero stride broadcasts one A)
     CUtensorMap am = a_map ? *a_map : hi;
     if (a.mode == kADenseK && a.vec4 && (a.a_zstride % a.lda) == 0) {
@@ -980,6 +1068,9 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
 
 void fill_epilogue(Args& a, const Epilogue& ep) {
     a.alpha = ep.alpha;
+    a.act_a = ep.act_a;
+    a.act_b = ep.act_b;
+    a.act_c = ep.act_c;
     a.bias = ep.bias;
     a.bias_scale = ep.bias_scale;
     a.res = ep.res;

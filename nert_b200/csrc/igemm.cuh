@@ -15,7 +15,9 @@
 
 namespace nb2 {
 
-enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActSigmoid = 3 };
+// kActGeluErf: ((x * (erf(x / act_a) + act_b)) * act_c), the erf form of GELU
+// as exported to ONNX (Div, Erf, Add, Mul, Mul).
+enum Act : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActSigmoid = 3, kActGeluErf = 4 };
 
 struct Epilogue {
     float alpha = 1.0f;
@@ -24,6 +26,7 @@ struct Epilogue {
     const float* res = nullptr; // same layout as the output
     float res_scale = 1.0f;
     int act = kActNone;
+    float act_a = 0.f, act_b = 0.f, act_c = 0.f;
 };
 
 // 2-D convolution geometry (1-D convolutions use H = KH = 1).

@@ -103,6 +103,53 @@ __global__ void binary_same_vec4_kernel(int op, const float4* __restrict__ a, co
     }
 }
 
+// Two-axis broadcast after collapsing: y is [outer][inner] with inner % 4 ==
+// 0; each operand is full (0), repeats a row of `inner` (1), holds one value
+// per row (2) or is a scalar (3). 32-bit indices.
+template <int M>
+__device__ __forceinline__ float4 bload(const float* __restrict__ p, uint32_t i4, uint32_t inner4) {
+    if constexpr (M == 0) {
+        return reinterpret_cast<const float4*>(p)[i4];
+    } else if constexpr (M == 1) {
+        return reinterpret_cast<const float4*>(p)[i4 % inner4];
+    } else if constexpr (M == 2) {
+        const float v = p[i4 / inner4];
+        return make_float4(v, v, v, v);
+    } else {
+        const float v = p[0];
+        return make_float4(v, v, v, v);
+    }
+}
+
+template <int MA, int MB>
+__global__ void bcast2_vec4_kernel(int op, const float* __restrict__ a, const float* __restrict__ b,
+                                   float4* __restrict__ y, uint32_t n4, uint32_t inner4) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const float4 u = bload<MA>(a, i, inner4), v = bload<MB>(b, i, inner4);
+        y[i] = make_float4(binary_f(op, u.x, v.x), binary_f(op, u.y, v.y), binary_f(op, u.z, v.z),
+                           binary_f(op, u.w, v.w));
+    }
+}
+
+template <int MA>
+void launch_bcast2(int mb, dim3 grid, cudaStream_t st, int op, const float* a, const float* b, float4* y, uint32_t n4,
+                   uint32_t inner4) {
+    switch (mb) {
+    case 0:
+        bcast2_vec4_kernel<MA, 0><<<grid, 256, 0, st>>>(op, a, b, y, n4, inner4);
+        break;
+    case 1:
+        bcast2_vec4_kernel<MA, 1><<<grid, 256, 0, st>>>(op, a, b, y, n4, inner4);
+        break;
+    case 2:
+        bcast2_vec4_kernel<MA, 2><<<grid, 256, 0, st>>>(op, a, b, y, n4, inner4);
+        break;
+    default:
+        bcast2_vec4_kernel<MA, 3><<<grid, 256, 0, st>>>(op, a, b, y, n4, inner4);
+        break;
+    }
+}
+
 struct BStrides {
     int rank;
     int64_t ydims[kMaxRank];
@@ -168,6 +215,82 @@ void binary(nb2_device* dev, int op, int dtype, const void* a, const std::vector
             op, static_cast<const float4*>(a), static_cast<const float4*>(b), static_cast<float4*>(y), n / 4);
         check_cuda(cudaGetLastError(), "binary launch");
         return;
+    }
+    if (dtype == kF32 && n < (int64_t(1) << 31)) {
+        // collapse to y[outer][inner] and classify each operand
+        const int r = static_cast<int>(yd.size());
+        std::vector<int64_t> ys, as, bs;
+        auto stride_of = [&](const std::vector<int64_t>& dims, int d, int64_t run) {
+            const int src = d - (r - static_cast<int>(dims.size()));
+            return (src < 0 || dims[src] == 1) ? int64_t(0) : run;
+        };
+        int64_t arun = 1, brun = 1;
+        std::vector<int64_t> a_st(r), b_st(r);
+        for (int d = r - 1; d >= 0; --d) {
+            a_st[d] = stride_of(ad, d, arun);
+            b_st[d] = stride_of(bd, d, brun);
+            const int sa = d - (r - static_cast<int>(ad.size())), sb = d - (r - static_cast<int>(bd.size()));
+            arun *= sa >= 0 ? ad[sa] : 1;
+            brun *= sb >= 0 ? bd[sb] : 1;
+        }
+        for (int d = 0; d < r; ++d) {
+            if (yd[d] == 1) {
+                continue;
+            }
+            if (!ys.empty() && as.back() == a_st[d] * yd[d] && bs.back() == b_st[d] * yd[d]) {
+                ys.back() *= yd[d];
+                as.back() = a_st[d];
+                bs.back() = b_st[d];
+                continue;
+            }
+            ys.push_back(yd[d]);
+            as.push_back(a_st[d]);
+            bs.push_back(b_st[d]);
+        }
+        if (ys.size() == 1) {
+            ys.insert(ys.begin(), 1);
+            as.insert(as.begin(), 0);
+            bs.insert(bs.begin(), 0);
+        }
+        if (ys.size() == 2 && ys[1] % 4 == 0) {
+            const int64_t inner = ys[1];
+            auto mode = [&](int64_t so, int64_t si) {
+                if (si == 1) {
+                    return (so == inner || ys[0] == 1) ? 0 : (so == 0 ? 1 : -1);
+                }
+                if (si == 0) {
+                    return so == 0 ? 3 : (so == 1 ? 2 : -1);
+                }
+                return -1;
+            };
+            const int ma = mode(as[0], as[1]), mb = mode(bs[0], bs[1]);
+            auto vec_ok = [](int m, const void* p) {
+                return m >= 2 || (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+            };
+            if (ma >= 0 && mb >= 0 && vec_ok(ma, a) && vec_ok(mb, b) && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+                const uint32_t n4 = static_cast<uint32_t>(n / 4), inner4 = static_cast<uint32_t>(inner / 4);
+                const dim3 grid(grid_for(dev, n4));
+                const float* fa = static_cast<const float*>(a);
+                const float* fb = static_cast<const float*>(b);
+                float4* fy = static_cast<float4*>(y);
+                switch (ma) {
+                case 0:
+                    launch_bcast2<0>(mb, grid, dev->stream, op, fa, fb, fy, n4, inner4);
+                    break;
+                case 1:
+                    launch_bcast2<1>(mb, grid, dev->stream, op, fa, fb, fy, n4, inner4);
+                    break;
+                case 2:
+                    launch_bcast2<2>(mb, grid, dev->stream, op, fa, fb, fy, n4, inner4);
+                    break;
+                default:
+                    launch_bcast2<3>(mb, grid, dev->stream, op, fa, fb, fy, n4, inner4);
+                    break;
+                }
+                check_cuda(cudaGetLastError(), "binary launch");
+                return;
+            }
+        }
     }
     BStrides s{};
     s.rank = static_cast<int>(yd.size());

@@ -11,6 +11,7 @@
 // (resize.cpp:62-158); Cast truncates float->int64 toward zero (cast.cpp).
 
 #include "ops_move.cuh"
+#include "ops.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -27,15 +28,18 @@ struct SegTable {
     int n;
 };
 
-// blockIdx.y = segment; grid-stride over rows x (row_bytes / unit).
-template <typename U>
+// blockIdx.y = segment; grid-stride over rows x (row_bytes / unit). I is
+// the index type (32-bit whenever every segment fits, which keeps the
+// per-element divide cheap).
+template <typename U, typename I>
 __global__ void segment_copy_kernel(SegTable t) {
     const CopySeg s = t.s[blockIdx.y];
-    const int64_t per_row = s.row_bytes / static_cast<int64_t>(sizeof(U));
-    const int64_t total = per_row * s.rows;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / per_row, c = i - r * per_row;
-        reinterpret_cast<U*>(s.dst + r * s.dst_pitch)[c] = reinterpret_cast<const U*>(s.src + r * s.src_pitch)[c];
+    const I per_row = static_cast<I>(s.row_bytes / static_cast<int64_t>(sizeof(U)));
+    const I total = per_row * static_cast<I>(s.rows);
+    for (I i = blockIdx.x * (I)blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+        const I r = i / per_row, c = i - r * per_row;
+        reinterpret_cast<U*>(s.dst + (int64_t)r * s.dst_pitch)[c] =
+            reinterpret_cast<const U*>(s.src + (int64_t)r * s.src_pitch)[c];
     }
 }
 
@@ -54,6 +58,73 @@ __global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ y, int
             src += c * in_stride_of_out_axis.d[d];
         }
         y[i] = x[src];
+    }
+}
+
+// Permutes whose innermost axis stays innermost: rows of `L` contiguous
+// elements move as a block (16-byte vectors when L % 4 == 0). The row index
+// decomposes over the collapsed output axes (32-bit math).
+struct RowPerm {
+    int rank;         // output axes other than the innermost
+    uint32_t od[7];   // their extents
+    int64_t ist[7];   // input stride (elements) of each
+};
+
+template <typename V>
+__global__ void permute_rows_kernel(const V* __restrict__ x, V* __restrict__ y, RowPerm p, uint32_t rows,
+                                    uint32_t L) {
+    const uint32_t total = rows * L;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t row = i / L, c = i - row * L;
+        uint32_t rem = row;
+        int64_t src = 0;
+        for (int d = p.rank - 1; d >= 0; --d) {
+            const uint32_t q = rem / p.od[d];
+            src += (int64_t)(rem - q * p.od[d]) * p.ist[d];
+            rem = q;
+        }
+        y[i] = x[src + c];
+    }
+}
+
+// General 2-D tiled permute: u = the input's innermost axis (contiguous in x),
+// v = the output's innermost axis (contiguous in y); the other axes form the
+// batch (blockIdx.z, decomposed once per block).
+struct TilePerm {
+    int nb;            // batch axes
+    int64_t bd[6];     // extents
+    int64_t bin[6];    // input strides
+    int64_t bout[6];   // output strides
+    int64_t U, V;      // tile axis extents
+    int64_t in_v;      // input stride of v
+    int64_t out_u;     // output stride of u
+};
+
+__global__ void permute_tile_kernel(const float* __restrict__ x, float* __restrict__ y, TilePerm p, int64_t batches) {
+    __shared__ float tile[32][33];
+    for (int64_t b = blockIdx.z; b < batches; b += gridDim.z) {
+        int64_t rem = b, ib = 0, ob = 0;
+        for (int d = p.nb - 1; d >= 0; --d) {
+            const int64_t c = rem % p.bd[d];
+            rem /= p.bd[d];
+            ib += c * p.bin[d];
+            ob += c * p.bout[d];
+        }
+        const int64_t u0 = blockIdx.x * 32, v0 = blockIdx.y * 32;
+        for (int i = threadIdx.y; i < 32; i += 8) {
+            const int64_t v = v0 + i, u = u0 + threadIdx.x;
+            if (u < p.U && v < p.V) {
+                tile[i][threadIdx.x] = x[ib + v * p.in_v + u];
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.y; i < 32; i += 8) {
+            const int64_t u = u0 + i, v = v0 + threadIdx.x;
+            if (u < p.U && v < p.V) {
+                y[ob + u * p.out_u + v] = tile[threadIdx.x][i];
+            }
+        }
+        __syncthreads();
     }
 }
 
@@ -211,15 +282,19 @@ void segment_copy(nb2_device* dev, const std::vector<CopySeg>& segs) {
         if (most == 0) {
             continue;
         }
+        const bool narrow = most < (int64_t(1) << 31);
         if ((bits & 15) == 0) {
             const dim3 grid(blocks_for(dev, most / 16), t.n);
-            segment_copy_kernel<uint4><<<grid, 256, 0, dev->stream>>>(t);
+            narrow ? segment_copy_kernel<uint4, uint32_t><<<grid, 256, 0, dev->stream>>>(t)
+                   : segment_copy_kernel<uint4, int64_t><<<grid, 256, 0, dev->stream>>>(t);
         } else if ((bits & 3) == 0) {
             const dim3 grid(blocks_for(dev, most / 4), t.n);
-            segment_copy_kernel<uint32_t><<<grid, 256, 0, dev->stream>>>(t);
+            narrow ? segment_copy_kernel<uint32_t, uint32_t><<<grid, 256, 0, dev->stream>>>(t)
+                   : segment_copy_kernel<uint32_t, int64_t><<<grid, 256, 0, dev->stream>>>(t);
         } else {
             const dim3 grid(blocks_for(dev, most), t.n);
-            segment_copy_kernel<uint8_t><<<grid, 256, 0, dev->stream>>>(t);
+            narrow ? segment_copy_kernel<uint8_t, uint32_t><<<grid, 256, 0, dev->stream>>>(t)
+                   : segment_copy_kernel<uint8_t, int64_t><<<grid, 256, 0, dev->stream>>>(t);
         }
         check_cuda(cudaGetLastError(), "segment copy launch");
     }
@@ -241,6 +316,132 @@ void transpose(nb2_device* dev, const void* x, void* y, const std::vector<int64_
     std::vector<int64_t> in_strides(rank, 1);
     for (int d = rank - 2; d >= 0; --d) {
         in_strides[d] = in_strides[d + 1] * in_dims[d + 1];
+    }
+    if (elem_bytes == 4) {
+        // collapse: drop unit axes, merge input axes that stay adjacent and in
+        // order in the output
+        std::vector<int64_t> cd;  // collapsed input extents
+        std::vector<int> cperm;   // collapsed permutation
+        {
+            std::vector<int> keep;
+            for (int d = 0; d < rank; ++d) {
+                if (in_dims[d] != 1) {
+                    keep.push_back(d);
+                }
+            }
+            std::vector<int> p2; // output order over kept input axes
+            for (int d = 0; d < rank; ++d) {
+                if (in_dims[perm[d]] != 1) {
+                    p2.push_back(static_cast<int>(perm[d]));
+                }
+            }
+            // groups: maximal runs in p2 of consecutive kept input axes
+            std::vector<std::vector<int>> groups;
+            for (size_t i = 0; i < p2.size(); ++i) {
+                const auto pos = std::find(keep.begin(), keep.end(), p2[i]) - keep.begin();
+                if (!groups.empty()) {
+                    const int last = groups.back().back();
+                    const auto lpos = std::find(keep.begin(), keep.end(), last) - keep.begin();
+                    if (pos == lpos + 1) {
+                        groups.back().push_back(p2[i]);
+                        continue;
+                    }
+                }
+                groups.push_back({p2[i]});
+            }
+            // collapsed input axes are the groups ordered by their first input axis
+            std::vector<int> order(groups.size());
+            for (size_t i = 0; i < order.size(); ++i) {
+                order[i] = static_cast<int>(i);
+            }
+            std::sort(order.begin(), order.end(), [&](int a, int b) { return groups[a][0] < groups[b][0]; });
+            std::vector<int> in_index(groups.size());
+            for (size_t j = 0; j < order.size(); ++j) {
+                in_index[order[j]] = static_cast<int>(j);
+                int64_t ext = 1;
+                for (int a : groups[order[j]]) {
+                    ext *= in_dims[a];
+                }
+                cd.push_back(ext);
+            }
+            for (size_t i = 0; i < groups.size(); ++i) {
+                cperm.push_back(in_index[i]);
+            }
+        }
+        const int cr = static_cast<int>(cd.size());
+        std::vector<int64_t> cst(cr, 1);
+        for (int d = cr - 2; d >= 0; --d) {
+            cst[d] = cst[d + 1] * cd[d + 1];
+        }
+        if (cr <= 1) {
+            copy(dev, x, y, n * 4);
+            return;
+        }
+        if (cr <= 8 && cperm[cr - 1] == cr - 1 && n < (int64_t(1) << 31)) {
+            // innermost axis stays: move rows
+            RowPerm rp{};
+            rp.rank = cr - 1;
+            for (int d = 0; d < cr - 1; ++d) {
+                rp.od[d] = static_cast<uint32_t>(cd[cperm[d]]);
+                rp.ist[d] = cst[cperm[d]];
+            }
+            const int64_t L = cd[cr - 1];
+            const int64_t rows = n / L;
+            const bool v4 = L % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+            if (v4) {
+                for (int d = 0; d < rp.rank; ++d) {
+                    rp.ist[d] /= 4;
+                }
+                permute_rows_kernel<float4><<<blocks_for(dev, n / 4), 256, 0, dev->stream>>>(
+                    static_cast<const float4*>(x), static_cast<float4*>(y), rp, static_cast<uint32_t>(rows),
+                    static_cast<uint32_t>(L / 4));
+            } else {
+                permute_rows_kernel<float><<<blocks_for(dev, n), 256, 0, dev->stream>>>(
+                    static_cast<const float*>(x), static_cast<float*>(y), rp, static_cast<uint32_t>(rows),
+                    static_cast<uint32_t>(L));
+            }
+            check_cuda(cudaGetLastError(), "transpose launch");
+            return;
+        }
+        if (cr <= 8) {
+            // tiled: u = input axis cr-1, v = the output's innermost axis
+            const int v_in = cperm[cr - 1];
+            int u_out = 0;
+            for (int d = 0; d < cr; ++d) {
+                if (cperm[d] == cr - 1) {
+                    u_out = d;
+                }
+            }
+            std::vector<int64_t> ost(cr, 1); // output strides by output axis
+            for (int d = cr - 2; d >= 0; --d) {
+                ost[d] = ost[d + 1] * cd[cperm[d + 1]];
+            }
+            TilePerm tp{};
+            tp.U = cd[cr - 1];
+            tp.V = cd[v_in];
+            tp.in_v = cst[v_in];
+            tp.out_u = ost[u_out];
+            int64_t batches = 1;
+            for (int d = 0; d < cr; ++d) {
+                if (d == u_out || d == cr - 1) {
+                    continue;
+                }
+                tp.bd[tp.nb] = cd[cperm[d]];
+                tp.bin[tp.nb] = cst[cperm[d]];
+                tp.bout[tp.nb] = ost[d];
+                batches *= cd[cperm[d]];
+                ++tp.nb;
+            }
+            const int64_t gx = (tp.U + 31) / 32, gy = (tp.V + 31) / 32;
+            if (gy <= 65535) {
+                const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
+                                static_cast<unsigned>(std::min<int64_t>(batches, 65535)));
+                permute_tile_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(static_cast<const float*>(x),
+                                                                            static_cast<float*>(y), tp, batches);
+                check_cuda(cudaGetLastError(), "transpose launch");
+                return;
+            }
+        }
     }
     // fast path: swap of the last two axes, leading axes in order
     bool last2 = rank >= 2 && perm[rank - 1] == rank - 2 && perm[rank - 2] == rank - 1;

@@ -149,3 +149,14 @@ def test_onnx_file_roundtrip_through_engine_reader(tmp_path):
     p = onnx_io.save(g, str(tmp_path / "r18.onnx"))
     a = nbm.analyze(p, {"input": [2, 3, 224, 224]})
     assert a["opset"] == 13 and a["tensors"]["fc_out"]["dims"] == [2, 1000]
+
+
+def test_vit_gelu_and_scale_fusion_plan():
+    from nert_b200 import configs
+
+    g = configs.vit_b16(2, layers=1)
+    a = nbm.analyze(g, {"input": [2, 3, 224, 224]})
+    rows = {e["name"]: e for e in a["exec"]}
+    assert rows["blk0.fc1"]["group"] == 7 and rows["blk0.fc1"]["act"] == 4  # bias + erf-form GELU
+    assert rows["blk0.qk"]["group"] == 2  # / sqrt(64) as the epilogue scale
+    assert not any(e["op"] in ("Erf", "Div") for e in a["exec"])

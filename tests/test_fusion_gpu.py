@@ -67,3 +67,55 @@ def test_fused_group(cuda, kind):
             m.close()
     assert rel_err(outs[False], ref[name]) <= TOL, "unfused"
     assert rel_err(outs[True], ref[name]) <= TOL, "fused"
+
+
+def _attn_graph(scale):
+    """MatMul(q, k^T) / scale -> Softmax -> MatMul(., v), runtime operands."""
+    g = Graph(opset=13)
+    q = g.add_input("q", [2, 3, 37, 16])
+    k = g.add_input("k", [2, 3, 16, 37])
+    v = g.add_input("v", [2, 3, 37, 16])
+    s = g.op("MatMul", [q, k], name="qk")
+    s = g.op("Div", [s, g.const("scale", np.array(scale, np.float32))], name="scaled")
+    a = g.op("Softmax", [s], name="sm", axis=-1)
+    g.add_output(g.op("MatMul", [a, v], name="av"), None, FLOAT)
+    feeds = {n: synth.normal(tuple(d), 1.0, synth.seed_of("attn", n)) for n, d, _ in g.inputs}
+    return g, feeds
+
+
+def _gelu_graph():
+    """MatMul + bias + GELU in the ONNX export's erf form, then a second MatMul."""
+    g = Graph(opset=13)
+    x = g.add_input("x", [2, 50, 64])
+    w1 = synth.normal((64, 256), 0.1, synth.seed_of("gelu", "w1"))
+    b1 = synth.normal((256,), 0.1, synth.seed_of("gelu", "b1"))
+    f = g.op("Add", [g.op("MatMul", [x, g.const("w1", w1)], name="fc1"), g.const("b1", b1)], name="fc1.bias")
+    e = g.op("Erf", [g.op("Div", [f, g.const("sqrt2", np.array(np.sqrt(2.0), np.float32))], name="div")],
+             name="erf")
+    e = g.op("Add", [e, g.const("one", np.array(1.0, np.float32))], name="add1")
+    f = g.op("Mul", [g.op("Mul", [f, e], name="mul"), g.const("half", np.array(0.5, np.float32))], name="half")
+    w2 = synth.normal((256, 32), 0.1, synth.seed_of("gelu", "w2"))
+    g.add_output(g.op("MatMul", [f, g.const("w2", w2)], name="fc2"), None, FLOAT)
+    return g, {"x": synth.normal((2, 50, 64), 1.0, synth.seed_of("gelu", "x"))}
+
+
+@pytest.mark.parametrize("kind", ["gelu", "attn_pow2", "attn_other"])
+def test_fused_matmul_epilogues(cuda, kind):
+    from nert_b200.model import Model, analyze
+
+    g, ins = _gelu_graph() if kind == "gelu" else _attn_graph(8.0 if kind == "attn_pow2" else 3.0)
+    plan = analyze(g, {k: list(v.shape) for k, v in ins.items()})
+    groups = {e["name"]: e["group"] for e in plan["exec"]}
+    if kind == "gelu":
+        assert groups["fc1"] == 7  # MatMul, bias, Div, Erf, Add, Mul, Mul
+    else:
+        assert groups["qk"] == (2 if kind == "attn_pow2" else 1)
+    ref = np_ref.run(g, ins)
+    name = g.outputs[0][0]
+    for fuse in (True, False):
+        m = Model(g, {k: list(v.shape) for k, v in ins.items()}, fuse=fuse)
+        try:
+            out = m.run(ins)[name]
+        finally:
+            m.close()
+        assert rel_err(out, ref[name]) <= TOL, fuse

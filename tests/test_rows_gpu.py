@@ -95,6 +95,21 @@ ROW_CASES = [
       4: np.array([3, -2], np.int64)}),
     ("reducemean_tail", "ReduceMean", [(4, 64, 7, 7)], {"axes": [2, 3], "keepdims": 1}, {}),
     ("pow", "Pow", [(64, 64), (64, 64)], {}, {}),
+    # broadcast binaries: scalar, row, per-row value, mirrored, unaligned and rank-3 forms
+    ("div_scalar", "Div", [(3, 197, 3072), ()], {}, {1: np.array(1.4142135, np.float32)}),
+    ("sub_scalar_first", "Sub", [(), (4, 197, 768)], {}, {0: np.array(1.0, np.float32)}),
+    ("add_row", "Add", [(8, 197, 768), (1, 197, 768)], {}, {}),
+    ("mul_col", "Mul", [(96, 400), (96, 1)], {}, {}),
+    ("div_row_first", "Div", [(768,), (16, 768)], {}, {}),
+    ("add_row_unaligned", "Add", [(6, 7, 13), (7, 13)], {}, {}),
+    ("mul_channel", "Mul", [(2, 64, 20, 20), (1, 64, 1, 1)], {}, {}),
+    ("sub_outer", "Sub", [(5, 1, 12), (1, 9, 1)], {}, {}),
+    # permutes: rows kept (vector and scalar widths), tiled, unit axes, rank 5
+    ("transpose_ctx", "Transpose", [(8, 12, 197, 64)], {"perm": [0, 2, 1, 3]}, {}),
+    ("transpose_rows_odd", "Transpose", [(3, 5, 7, 9)], {"perm": [1, 0, 2, 3]}, {}),
+    ("transpose_unit", "Transpose", [(1, 197, 1, 768)], {"perm": [2, 3, 0, 1]}, {}),
+    ("transpose_r5", "Transpose", [(2, 3, 4, 5, 6)], {"perm": [4, 2, 0, 3, 1]}, {}),
+    ("transpose_nchw_nhwc", "Transpose", [(2, 80, 33, 35)], {"perm": [0, 2, 3, 1]}, {}),
 ]
 
 
