@@ -279,7 +279,7 @@ def tensor_peak(precision: str) -> tuple[float, str]:
 def row_name(label: str) -> str:
     """Node name of a profile label 'Op[+fused]:name[layout]'."""
     name = label.split(":", 1)[1]
-    return re.sub(r"\[[^\]]*\]$", "", name)
+    return re.sub(r"(\[[^\]]*\])+$", "", name)
 
 
 def contraction_flops(graph, analysis) -> dict:

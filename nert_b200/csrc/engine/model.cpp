@@ -663,6 +663,10 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             ConvGeom geom = conv_geom(n, shapes_.at(n.inputs[0]), shapes_.at(n.inputs[1]), shapes_.at(n.outputs[0]));
             geom.in_nhwc = nhwc.count(n.inputs[0]) > 0;
             geom.out_nhwc = nhwc.count(e.out) > 0;
+            // a narrow NCHW input (an image): convert it to x[N][H][W][4] so
+            // each tap is one 16-byte load (packed weights only)
+            geom.in_c4 = (flags & kNchwOnly) == 0 && !geom.in_nhwc && geom.c4_input_ok() &&
+                         packed_conv.count(n.inputs[1]) > 0;
             if (geom.in_nhwc || geom.out_nhwc) {
                 st.label += geom.in_nhwc ? (geom.out_nhwc ? "[nhwc]" : "[nhwc>nchw]") : "[nchw>nhwc]";
             }
@@ -690,7 +694,17 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 cudaFree(tmp);
                 weight_bytes_ += pbytes;
                 nb2_device* dev = dev_;
-                st.run = [=] { conv_run(dev, geom, x, packed, y, ep); };
+                if (geom.in_c4) {
+                    float* x4 = reinterpret_cast<float*>(dmalloc(align_up(geom.N * geom.H * geom.W * 16)));
+                    st.label += "[c4]";
+                    st.launches = 2;
+                    st.run = [=] {
+                        nchw_to_nhwc4(dev, x, x4, geom.N, geom.C, geom.H, geom.W);
+                        conv_run(dev, geom, x4, packed, y, ep);
+                    };
+                } else {
+                    st.run = [=] { conv_run(dev, geom, x, packed, y, ep); };
+                }
             } else {
                 const float* w = F(n.inputs[1]);
                 scratch_need = std::max(scratch_need, pbytes);

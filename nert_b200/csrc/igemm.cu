@@ -34,7 +34,18 @@ namespace {
 // fp32 tile into shared memory and the producer warps split it in place.
 // kAConvNhwc: Conv over NHWC activations (C % 32 == 0); TMA im2col brings the
 // raw fp32 tile for one (filter tap, 32-channel block) per K block.
-enum AMode : int { kAConvTap = 0, kAConvGeneric = 1, kADenseK = 2, kADenseM = 3, kADenseTma = 4, kAConvNhwc = 5 };
+// kAConvC4: Conv over x[N][H][W][4] (C <= 4 zero-padded to 4, e.g. a stem's
+// RGB input); K ordered (tap, channel), a K half-block is 4 taps, each one
+// 16-byte load.
+enum AMode : int {
+    kAConvTap = 0,
+    kAConvGeneric = 1,
+    kADenseK = 2,
+    kADenseM = 3,
+    kADenseTma = 4,
+    kAConvNhwc = 5,
+    kAConvC4 = 6
+};
 
 struct Args {
     int M, N, K, nkb;
@@ -46,7 +57,7 @@ struct Args {
     int vec4; // dense K-major rows are 16-byte aligned with K % 4 == 0
     int a_zrows; // kADenseTma: A-map row offset per z slice
     // conv geometry
-    int C, H, W, OH, OW, KW, sh, sw, ph, pw, dh, dw, Cg;
+    int C, H, W, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw, Cg;
     int64_t HW, OHW, img_stride;
     const int2* ktab;
     int ktab_smem; // copy the tap table into shared memory
@@ -81,10 +92,10 @@ struct Cfg {
     // A operand in tensor memory (BN <= 64): the producers write the tf32
     // hi/lo planes of A to TMEM with tcgen05.st and the MMA reads A from
     // there, so shared memory only carries B (and A raw tiles that TMA
-    // brings). With a narrow B tile the MMA's A reads from shared memory
-    // would otherwise outweigh the tensor work. Wider tiles need all 512
-    // TMEM columns for the accumulators and keep A in shared memory.
-    static constexpr bool kATmem = BN <= 64;
+    // brings). An MMA that reads A (4 KB) and B (N x 32 B) from shared memory
+    // needs 128 B/clock at N = 128, all the shared-memory bandwidth, which
+    // starves the converter and the TMA writes; with A in TMEM it needs 64.
+    static constexpr bool kATmem = BN <= 128;
     static constexpr int kAPlane = 128 * 128;
     static constexpr int kBPlane = BN * 128;
     static constexpr int kPlanes = THREE ? 2 : 1;
@@ -95,9 +106,12 @@ struct Cfg {
     // kStages deep, plus kTStages TMEM A stages.
     static constexpr int kStageBytes = kATmem ? kAPlane + kBStageBytes : (kAPlane + kBPlane) * kPlanes;
     static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
-    // two accumulators per tile (even / odd K blocks) x two tiles in flight
+    // two accumulators per tile (even / odd K blocks) x kAccBufs tiles in
+    // flight: two for BN = 64 (the epilogue overlaps the next tile's MMAs),
+    // one for BN = 128 (the other 256 columns hold the A stages)
     static constexpr int kAccs = 2;
-    static constexpr int kAccCols = 2 * kAccs * BN;
+    static constexpr int kAccBufs = BN <= 64 ? 2 : 1;
+    static constexpr int kAccCols = kAccBufs * kAccs * BN;
     static constexpr int kAStageCols = 32 * kPlanes; // hi plane, then lo plane
     static constexpr int kTStagesRaw = (512 - kAccCols) / kAStageCols;
     static constexpr int kMin3(int a, int b, int c) { return a < b ? (a < c ? a : c) : (b < c ? b : c); }
@@ -183,6 +197,21 @@ __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, in
                 rs.kw = 0;
                 ++rs.kh;
             }
+        }
+    } else if constexpr (MODE == kAConvC4) {
+        // 4 taps x 4 channels; ktab[t] = (kh*dh, kw*dw), y = -1 past the last tap
+        const int t0 = kb * 8 + half * 4;
+        const float4* img = reinterpret_cast<const float4*>(rs.base);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int2 e = ktab[t0 + q];
+            const int ih = rs.ih0 + e.x, iw = rs.iw0 + e.y;
+            const bool ok = rs.ok & (e.y >= 0) & ((unsigned)ih < (unsigned)p.H) & ((unsigned)iw < (unsigned)p.W);
+            const float4 t = ok ? __ldg(img + (int64_t)ih * p.W + iw) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * q] = t.x;
+            v[4 * q + 1] = t.y;
+            v[4 * q + 2] = t.z;
+            v[4 * q + 3] = t.w;
         }
     } else if constexpr (MODE == kAConvGeneric) {
         // per-k tap table (shared memory when it fits); branch-free: an
@@ -309,8 +338,8 @@ __device__ __forceinline__ void publish_tmem(uint64_t* bar, int lane) {
 }
 
 // Persistent, warp-specialised contraction kernel: one CTA per SM walks the
-// output tiles (m fastest, so concurrent CTAs share the B tile in L2); the
-// TMEM accumulators are double buffered so the epilogue of one tile overlaps
+// output tiles (m fastest, so concurrent CTAs share the B tile in L2). With
+// two TMEM accumulator buffers (BN = 64) the epilogue of one tile overlaps
 // the main loop of the next.
 template <int BN, bool THREE, int MODE>
 // 17 warps: an SM sub-partition holds up to 5 of them and has 16K
@@ -390,6 +419,15 @@ __global__ void __launch_bounds__(640, 1)
             }
             ktab = t;
         }
+    } else if constexpr (MODE == kAConvC4) {
+        // per-tap filter offsets, built here (8 taps per K block)
+        int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512 + C::kEpiBytes);
+        const int taps = p.KH * p.KW;
+        for (int k = threadIdx.x; k < nkb * 8; k += blockDim.x) {
+            const int kh = k / p.KW;
+            t[k] = k < taps ? make_int2(kh * p.dh, (k - kh * p.KW) * p.dw) : make_int2(0, -1);
+        }
+        ktab = t;
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -449,10 +487,6 @@ __global__ void __launch_bounds__(640, 1)
                                      : "r"(row + ((c ^ (r & 7)) << 4))
                                      : "memory");
                     }
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&empty_a[s]);
-                    }
                     // TMEM stage t == s is free once the MMA released stage s
                     if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err)) {
                         break;
@@ -460,6 +494,14 @@ __global__ void __launch_bounds__(640, 1)
                     const uint32_t ta = tq + t * C::kAStageCols;
                     store16_tmem<THREE>(ta, *reinterpret_cast<const float(*)[16]>(&v[0]));
                     store16_tmem<THREE>(ta + 16, *reinterpret_cast<const float(*)[16]>(&v[16]));
+                    // The raw tile has been read (its values went into the TMEM
+                    // stores); order those generic-proxy reads before the next
+                    // TMA (async-proxy) write into the stage, then release it.
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&empty_a[s]);
+                    }
                     // B landed too, so the MMA issuer waits on t_full alone
                     if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err)) {
                         break;
@@ -516,7 +558,7 @@ __global__ void __launch_bounds__(640, 1)
             rs.kh = 0;
             rs.kw = 0;
             const float* az = p.a + (int64_t)z * p.a_zstride;
-            if constexpr (MODE == kAConvTap || MODE == kAConvGeneric) {
+            if constexpr (MODE == kAConvTap || MODE == kAConvGeneric || MODE == kAConvC4) {
                 const int mm = rs.ok ? rs.m : 0;
                 const int n_img = mm / (int)p.OHW;
                 const int pix = mm - n_img * (int)p.OHW;
@@ -525,7 +567,7 @@ __global__ void __launch_bounds__(640, 1)
                 rs.ih0 = oh * p.sh - p.ph;
                 rs.iw0 = ow * p.sw - p.pw;
                 const float* img = az + (int64_t)n_img * p.img_stride;
-                rs.base = (MODE == kAConvTap) ? img : img + (int64_t)rs.ih0 * p.W + rs.iw0;
+                rs.base = (MODE == kAConvGeneric) ? img + (int64_t)rs.ih0 * p.W + rs.iw0 : img;
             } else if constexpr (MODE == kADenseK) {
                 rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
             } else {
@@ -603,8 +645,8 @@ __global__ void __launch_bounds__(640, 1)
             for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
                 int z, m0, n0;
                 decode(t, z, m0, n0);
-                const int b = i & 1;
-                if (!warp_wait(&acc_full[b], (i >> 1) & 1, abort_flag, p.err)) {
+                const int b = i % C::kAccBufs;
+                if (!warp_wait(&acc_full[b], (i / C::kAccBufs) & 1, abort_flag, p.err)) {
                     break;
                 }
                 tc_fence_after();
@@ -824,8 +866,8 @@ __global__ void __launch_bounds__(640, 1)
             int i = 0;
             bool alive = true;
             for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++i) {
-                const int b = i & 1;
-                if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1, abort_flag, p.err)) {
+                const int b = i % C::kAccBufs;
+                if (!mbar_wait(&acc_empty[b], ((i / C::kAccBufs) & 1) ^ 1, abort_flag, p.err)) {
                     break;
                 }
                 tc_fence_after();
@@ -912,7 +954,8 @@ enum BLayout : int { kBRowsK = 0, kBKRows = 1, kBConvTap = 2 };
 // out[z*rows + row][k] = hi/lo split of B(row, k), zero for k >= K.
 // 32x32 tiles through shared memory so both the read and the write coalesce.
 __global__ void pack_b_kernel(const float* __restrict__ src, int layout, int rows, int K, int Kpad, int64_t ld,
-                              int64_t zstride, int Cg, int KHKW, float* __restrict__ hi, float* __restrict__ lo) {
+                              int64_t zstride, int Cg, int KHKW, int Cpad, float* __restrict__ hi,
+                              float* __restrict__ lo) {
     __shared__ float tile[32][33];
     const int k0 = blockIdx.x * 32;
     const int r0 = blockIdx.y * 32;
@@ -930,9 +973,9 @@ __global__ void pack_b_kernel(const float* __restrict__ src, int layout, int row
             if (k < K && row < rows) {
                 if (layout == kBRowsK) {
                     v = s[(int64_t)row * ld + k];
-                } else { // conv weight [M][Cg][KHKW], k = tap*Cg + cin
-                    const int tap = k / Cg, cin = k - tap * Cg;
-                    v = s[((int64_t)row * Cg + cin) * KHKW + tap];
+                } else { // conv weight [M][Cg][KHKW], k = tap*Cpad + cin (zero for cin >= Cg)
+                    const int tap = k / Cpad, cin = k - tap * Cpad;
+                    v = cin < Cg ? s[((int64_t)row * Cg + cin) * KHKW + tap] : 0.0f;
                 }
             }
             tile[i][tx] = v;
@@ -1023,6 +1066,9 @@ void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi,
     case kAConvNhwc:
         launch_mode<BN, THREE, kAConvNhwc>(dev, a, grid, hi, lo, am);
         break;
+    case kAConvC4:
+        launch_mode<BN, THREE, kAConvC4>(dev, a, grid, hi, lo, am);
+        break;
     default:
         launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo, am);
         break;
@@ -1043,7 +1089,10 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
                  (a.res == nullptr || al16(a.res)) && (a.bias == nullptr || (al16(a.bias) && a.bias_zstride % 4 == 0)))
                     ? 1
                     : 0;
-    a.ktab_smem = (a.mode == kAConvGeneric && kpad * 8 <= 16384) ? 1 : 0;
+    a.ktab_smem = ((a.mode == kAConvGeneric && kpad * 8 <= 16384) || a.mode == kAConvC4) ? 1 : 0;
+    if (a.mode == kAConvC4 && kpad * 8 > 16384) {
+        fail(kStatusUnsupported, "Conv: filter too large for the 4-channel input path");
+    }
     // row-major A with 16-byte rows: TMA it (a zero stride broadcasts one A)
     CUtensorMap am = a_map ? *a_map : hi;
     if (a.mode == kADenseK && a.vec4 && (a.a_zstride % a.lda) == 0) {
@@ -1099,7 +1148,8 @@ void conv_pack(nb2_device* dev, const ConvGeom& g, const float* w, void* packed)
     const dim3 grid(static_cast<unsigned>(kpad / 32), static_cast<unsigned>((g.M + 31) / 32), 1);
     pack_b_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(w, layout, static_cast<int>(g.M), static_cast<int>(K),
                                                         static_cast<int>(kpad), K, 0, static_cast<int>(g.Cg()),
-                                                        static_cast<int>(g.KH * g.KW), hi, lo);
+                                                        static_cast<int>(g.KH * g.KW), static_cast<int>(g.Cpad()),
+                                                        hi, lo);
     check_cuda(cudaGetLastError(), "pack_b launch");
     if (!g.tap_major()) {
         int2* tab = reinterpret_cast<int2*>(lo + g.M * kpad);
@@ -1122,9 +1172,12 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.N = static_cast<int>(g.Mg());
     a.K = static_cast<int>(K);
     a.nkb = static_cast<int>(kpad / 32);
-    a.mode = g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
+    a.mode = g.in_c4 ? kAConvC4 : g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
     if (g.in_nhwc && !g.nhwc_input_ok()) {
         fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 32 == 0 and strides <= 8");
+    }
+    if (g.in_c4 && (!g.c4_input_ok() || g.in_nhwc)) {
+        fail(kStatusUnsupported, "Conv: the 4-channel input form needs group 1 and C <= 4");
     }
     a.a = x;
     a.a_zstride = g.Cg() * g.H * g.W;
@@ -1133,6 +1186,7 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.W = static_cast<int>(g.W);
     a.OH = static_cast<int>(g.OH);
     a.OW = static_cast<int>(g.OW);
+    a.KH = static_cast<int>(g.KH);
     a.KW = static_cast<int>(g.KW);
     a.sh = static_cast<int>(g.sh);
     a.sw = static_cast<int>(g.sw);
@@ -1143,7 +1197,7 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.Cg = static_cast<int>(g.Cg());
     a.HW = g.H * g.W;
     a.OHW = ohw;
-    a.img_stride = g.C * g.H * g.W;
+    a.img_stride = (g.in_c4 ? 4 : g.C) * g.H * g.W;
     const float* hi = static_cast<const float*>(packed);
     a.ktab = g.tap_major() ? nullptr : reinterpret_cast<const int2*>(hi + 2 * g.M * kpad);
     a.b_zrows = static_cast<int>(g.Mg());
@@ -1203,7 +1257,7 @@ void gemm_pack_b(nb2_device* dev, const GemmGeom& g, const float* b, void* packe
     const dim3 grid(static_cast<unsigned>(kpad / 32), static_cast<unsigned>((g.N + 31) / 32),
                     static_cast<unsigned>(g.batch));
     pack_b_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(b, layout, static_cast<int>(g.N), static_cast<int>(g.K),
-                                                        static_cast<int>(kpad), g.ldb, g.b_zstride, 1, 1, hi, lo);
+                                                        static_cast<int>(kpad), g.ldb, g.b_zstride, 1, 1, 1, hi, lo);
     check_cuda(cudaGetLastError(), "pack_b launch");
 }
 

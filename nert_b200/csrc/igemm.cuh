@@ -41,10 +41,15 @@ struct ConvGeom {
     // C ABI and the nert::Device rows are NCHW). An NHWC input needs
     // nhwc_input_ok(): A is then brought in by TMA im2col.
     bool in_nhwc = false, out_nhwc = false;
+    // Input given as x[N][H][W][4] (C <= 4 channels zero-padded to 4, a
+    // stem's image): K is ordered (tap, channel) with 4 channels per tap.
+    bool in_c4 = false;
     int64_t Cg() const { return C / group; }
     int64_t Mg() const { return M / group; }
-    int64_t K() const { return Cg() * KH * KW; }
-    bool tap_major() const { return Cg() % 32 == 0; }
+    int64_t Cpad() const { return in_c4 ? 4 : Cg(); }
+    int64_t K() const { return Cpad() * KH * KW; }
+    bool tap_major() const { return in_c4 || Cg() % 32 == 0; }
+    bool c4_input_ok() const { return group == 1 && C <= 4; }
     int64_t pad_bottom() const { return pb == kPadUnset ? ph : pb; }
     int64_t pad_right() const { return pr == kPadUnset ? pw : pr; }
     // TMA im2col limits for a 4-D map: traversal strides 1..8, box corners in

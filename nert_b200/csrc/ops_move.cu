@@ -264,7 +264,43 @@ unsigned blocks_for(nb2_device* dev, int64_t n) {
     return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, dev->num_sms * 16)));
 }
 
+// One thread per pixel; channel planes are read coalesced along W and the
+// pixel's four channels written as one 16-byte vector.
+__global__ void nchw_to_nhwc4_kernel(const float* __restrict__ x, float4* __restrict__ y, uint32_t C, uint32_t HW,
+                                     uint32_t total) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t n = i / HW, p = i - n * HW;
+        const float* src = x + (size_t)n * C * HW + p;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        v.x = __ldg(src);
+        if (C > 1) {
+            v.y = __ldg(src + HW);
+        }
+        if (C > 2) {
+            v.z = __ldg(src + 2 * (size_t)HW);
+        }
+        if (C > 3) {
+            v.w = __ldg(src + 3 * (size_t)HW);
+        }
+        y[i] = v;
+    }
+}
+
 } // namespace
+
+void nchw_to_nhwc4(nb2_device* dev, const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W) {
+    const int64_t total = N * H * W;
+    if (total <= 0) {
+        return;
+    }
+    if (C < 1 || C > 4 || total >= (int64_t(1) << 31) || H * W >= (int64_t(1) << 31)) {
+        fail(kStatusUnsupported, "nchw_to_nhwc4: needs 1 <= C <= 4 and fewer than 2^31 pixels");
+    }
+    nchw_to_nhwc4_kernel<<<blocks_for(dev, total), 256, 0, dev->stream>>>(
+        x, reinterpret_cast<float4*>(y), static_cast<uint32_t>(C), static_cast<uint32_t>(H * W),
+        static_cast<uint32_t>(total));
+    check_cuda(cudaGetLastError(), "nchw_to_nhwc4 launch");
+}
 
 void segment_copy(nb2_device* dev, const std::vector<CopySeg>& segs) {
     for (size_t base = 0; base < segs.size(); base += kMaxSegs) {

@@ -203,6 +203,59 @@ __global__ void layernorm_warp_kernel(const float* __restrict__ x, const float* 
     }
 }
 
+// Warp per row LayerNorm for D % 128 == 0 (D <= 1024): 16-byte loads and
+// stores, two-pass mean / centred variance in fp32 from registers (the
+// reference's double sums differ from these by rounding far below the fp32
+// output's own precision).
+template <int V4>
+__global__ void layernorm_warp4_kernel(const float4* __restrict__ x, const float4* __restrict__ scale,
+                                       const float4* __restrict__ bias, float4* __restrict__ y,
+                                       float* __restrict__ mean_out, float* __restrict__ inv_out, uint32_t rows,
+                                       float eps) {
+    const uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) {
+        return;
+    }
+    constexpr int D = V4 * 128;
+    const float4* r = x + (size_t)row * (D / 4);
+    float4 v[V4];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        v[i] = __ldg(r + lane + 32 * i);
+        s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    const float mean = warp_sum(s) * (1.0f / D);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / D) + eps);
+    float4* o = y + (size_t)row * (D / 4);
+#pragma unroll
+    for (int i = 0; i < V4; ++i) {
+        const float4 g = __ldg(scale + lane + 32 * i);
+        const float4 b = bias ? __ldg(bias + lane + 32 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 w;
+        w.x = (v[i].x - mean) * inv * g.x + b.x;
+        w.y = (v[i].y - mean) * inv * g.y + b.y;
+        w.z = (v[i].z - mean) * inv * g.z + b.z;
+        w.w = (v[i].w - mean) * inv * g.w + b.w;
+        o[lane + 32 * i] = w;
+    }
+    if (lane == 0) {
+        if (mean_out) {
+            mean_out[row] = mean;
+        }
+        if (inv_out) {
+            inv_out[row] = inv;
+        }
+    }
+}
+
 // Block per row LayerNorm for D > 1024 (row re-read from L1/L2).
 __global__ void layernorm_block_kernel(const float* __restrict__ x, const float* __restrict__ scale,
                                        const float* __restrict__ bias, float* __restrict__ y,
@@ -300,7 +353,42 @@ void layernorm(nb2_device* dev, const float* x, const float* scale, const float*
     if (rows <= 0 || D <= 0) {
         return;
     }
-    if (D <= kWarpRowMax) {
+    const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scale) |
+                      reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (D % 128 == 0 && D <= kWarpRowMax && al && rows < (int64_t(1) << 26)) {
+        const unsigned blocks = static_cast<unsigned>((rows * 32 + 255) / 256);
+        const auto* x4 = reinterpret_cast<const float4*>(x);
+        const auto* s4 = reinterpret_cast<const float4*>(scale);
+        const auto* b4 = reinterpret_cast<const float4*>(bias);
+        auto* y4 = reinterpret_cast<float4*>(y);
+        const auto r = static_cast<uint32_t>(rows);
+        switch (D / 128) {
+        case 1:
+            layernorm_warp4_kernel<1><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 2:
+            layernorm_warp4_kernel<2><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 3:
+            layernorm_warp4_kernel<3><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 4:
+            layernorm_warp4_kernel<4><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 5:
+            layernorm_warp4_kernel<5><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 6:
+            layernorm_warp4_kernel<6><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        case 7:
+            layernorm_warp4_kernel<7><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        default:
+            layernorm_warp4_kernel<8><<<blocks, 256, 0, dev->stream>>>(x4, s4, b4, y4, mean, inv_std, r, eps);
+            break;
+        }
+    } else if (D <= kWarpRowMax) {
         const unsigned blocks = static_cast<unsigned>((rows * 32 + 255) / 256);
         const int d = static_cast<int>(D);
         if (D <= 256) {

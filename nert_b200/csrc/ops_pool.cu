@@ -105,33 +105,37 @@ __global__ void row_mean_block_kernel(const float* __restrict__ x, float* __rest
     }
 }
 
+// 32-bit geometry of a channels-last pool (every extent and index < 2^31).
+struct PoolGeom32 {
+    int C4, H, W, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
+};
+
 // Channels-last max pool: one thread per (output pixel, 4 channels), so a
 // warp reads 512 contiguous bytes of one input pixel per tap (C % 4 == 0).
-__global__ void maxpool2d_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y, PoolGeom g,
-                                       int64_t total) {
-    const int64_t C4 = g.C >> 2;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t c4 = i % C4;
-        int64_t t = i / C4;
-        const int64_t ow = t % g.OW;
+__global__ void maxpool2d_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y, PoolGeom32 g,
+                                       uint32_t total) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t c4 = i % g.C4;
+        uint32_t t = i / g.C4;
+        const int ow = static_cast<int>(t % g.OW);
         t /= g.OW;
-        const int64_t oh = t % g.OH;
-        const int64_t n = t / g.OH;
-        const int64_t h0 = oh * g.sh - g.ph;
-        const int64_t w0 = ow * g.sw - g.pw;
+        const int oh = static_cast<int>(t % g.OH);
+        const uint32_t n = t / g.OH;
+        const int h0 = oh * g.sh - g.ph;
+        const int w0 = ow * g.sw - g.pw;
         float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        for (int64_t kh = 0; kh < g.KH; ++kh) {
-            const int64_t ih = h0 + kh * g.dh;
+        for (int kh = 0; kh < g.KH; ++kh) {
+            const int ih = h0 + kh * g.dh;
             if (ih < 0 || ih >= g.H) {
                 continue;
             }
-            const float4* row = x + ((n * g.H + ih) * g.W) * C4 + c4;
-            for (int64_t kw = 0; kw < g.KW; ++kw) {
-                const int64_t iw = w0 + kw * g.dw;
+            const float4* row = x + ((size_t)(n * g.H + ih) * g.W) * g.C4 + c4;
+            for (int kw = 0; kw < g.KW; ++kw) {
+                const int iw = w0 + kw * g.dw;
                 if (iw < 0 || iw >= g.W) {
                     continue;
                 }
-                const float4 v = __ldg(row + iw * C4);
+                const float4 v = __ldg(row + iw * g.C4);
                 best.x = v.x > best.x ? v.x : best.x;
                 best.y = v.y > best.y ? v.y : best.y;
                 best.z = v.z > best.z ? v.z : best.z;
@@ -206,11 +210,18 @@ void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y
         return;
     }
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
-    if (v4) {
+    if (v4 && total < (int64_t(1) << 31) && g.N * g.H * g.W * g.C < (int64_t(1) << 33)) {
+        const PoolGeom32 g32{static_cast<int>(g.C / 4), static_cast<int>(g.H), static_cast<int>(g.W),
+                             static_cast<int>(g.OH), static_cast<int>(g.OW), static_cast<int>(g.KH),
+                             static_cast<int>(g.KW), static_cast<int>(g.sh), static_cast<int>(g.sw),
+                             static_cast<int>(g.ph), static_cast<int>(g.pw), static_cast<int>(g.dh),
+                             static_cast<int>(g.dw)};
         maxpool2d_nhwc4_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(
-            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), g, total);
+            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), g32, static_cast<uint32_t>(total));
     } else {
-        maxpool2d_nhwc1_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
+        const int64_t total1 = g.N * g.OH * g.OW * g.C;
+        const int64_t blocks1 = std::min<int64_t>((total1 + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
+        maxpool2d_nhwc1_kernel<<<static_cast<unsigned>(blocks1), 256, 0, dev->stream>>>(x, y, g, total1);
     }
     check_cuda(cudaGetLastError(), "maxpool_nhwc launch");
 }

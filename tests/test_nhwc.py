@@ -114,3 +114,45 @@ def test_resnet_channels_last_equals_nchw(cuda, builder, batch, out):
     ref = np_ref.run(g, {"input": x})[out]
     assert rel_err(res[True], ref) <= TOL
     assert rel_err(res[False], ref) <= TOL
+
+
+# (id, N, C, H, W, M, kernel, strides, pads, dilations): narrow-channel convs on an NCHW graph input
+C4_CASES = [
+    ("stem7x7", 2, 3, 224, 224, 64, (7, 7), (2, 2), (3, 3, 3, 3), (1, 1)),
+    ("yolo3x3s2", 2, 3, 64, 80, 16, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1)),
+    ("patch16", 2, 3, 224, 224, 96, (16, 16), (16, 16), (0, 0, 0, 0), (1, 1)),
+    ("c1_dil", 1, 1, 37, 41, 40, (3, 5), (1, 2), (2, 1, 0, 3), (2, 1)),
+    ("c4_odd", 3, 4, 19, 23, 130, (5, 5), (3, 3), (2, 2, 2, 2), (1, 1)),
+]
+
+
+def _c4_graph(case):
+    name, n, c, h, w, m, k, s, p, d = case
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    g = Graph(opset=13)
+    x = g.add_input("x", [n, c, h, w])
+    wt = synth.normal((m, c, k[0], k[1]), (2.0 / (c * k[0] * k[1])) ** 0.5, synth.seed_of("c4", name + "w"))
+    bi = synth.normal((m,), 0.1, synth.seed_of("c4", name + "b"))
+    y = g.op("Relu", [g.op("Conv", [x, g.const("w", wt), g.const("b", bi)], name="conv", kernel_shape=list(k),
+                           strides=list(s), pads=list(p), dilations=list(d))], name="relu")
+    g.add_output(y, None, FLOAT)
+    return g, {"x": synth.uniform((n, c, h, w), -1.0, 1.0, synth.seed_of("c4", name + "x"))}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", C4_CASES, ids=[c[0] for c in C4_CASES])
+def test_narrow_channel_conv_c4_path(cuda, case):
+    g, feed = _c4_graph(case)
+    ref = np_ref.run(g, feed)
+    out_name = g.outputs[0][0]
+    for cl in (True, False):
+        m = model.Model(g, {"x": list(feed["x"].shape)}, channels_last=cl)
+        try:
+            out = m.run(feed)[out_name]
+            labels = [lab for lab, _ in m.profile()]
+        finally:
+            m.close()
+        assert any("[c4]" in lab for lab in labels) == cl, labels
+        assert rel_err(out, ref[out_name]) <= TOL, cl
