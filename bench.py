@@ -257,6 +257,11 @@ def measure_tf32_peak() -> float:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum over the contraction launches of
+# one forward, from the ncu capture summarised in profiles/ (per workload, batch)
+TRAFFIC_BYTES = {("resnet18", 64): int((788.2 + 192.7) * 1e6)}
+
+
 def tensor_peak(precision: str) -> tuple[float, str]:
     """Roofline denominator for the tf32 contraction kernel.
 
@@ -506,7 +511,10 @@ def main():
                          "frac_of_tf32_dense_live": (achieved / tf32) if achieved else None,
                          "flops_per_step": tc_flop, "kernel_ms_per_step": tc_time,
                          "share_of_step": tc_time / total_prof if total_prof else None,
-                         "traffic": None},
+                         "traffic": TRAFFIC_BYTES.get((args.workload, batch)),
+                         "traffic_note": "DRAM bytes read+written by the contraction launches of one step, "
+                                         "from one ncu capture (profiles/resnet18_b64_igemm_dram.md)"
+                         if (args.workload, batch) in TRAFFIC_BYTES else None},
             "top_rows_ms": [[lab, round(ms, 4)] for lab, ms in top_rows],
             "clocks": clk,
             "gpu_launches": int(stats["kernels_per_run"]) * args.steps,
