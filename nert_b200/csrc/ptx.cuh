@@ -53,6 +53,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in hardware (up to `ns`, woken when the phase completes) instead of
+// spinning, so waiting warps leave their sub-partition's issue slots to the
+// working warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on `bar` for the phase with `parity`. Returns false (after
 // recording the timeout and raising the CTA's abort flag) when the bound is
 // hit or another thread of the CTA has already aborted.
@@ -62,7 +78,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
     const long long start = clock64();
     while (true) {
-        if (mbar_try_wait(bar, parity)) {
+        if (mbar_try_wait_sleep(bar, parity, 100000u)) {
             return true;
         }
         if (*abort_flag) {

@@ -4,6 +4,8 @@
     python -m nert_b200.probe gemm M N K [REPS]
     python -m nert_b200.probe maxpool N C H W K STRIDE PAD [REPS]
     python -m nert_b200.probe resnet18 BATCH [REPS]
+    python -m nert_b200.probe engine_conv N C H W M K STRIDE PAD [REPS]
+        (one Conv as an engine graph: C <= 4 takes the 4-channel input path)
     python -m nert_b200.probe chain N C H W M K STRIDE PAD [REPS]
         (engine graph: 1x1 Conv 16->C, the KxK Conv C->M reading and writing
         channels-last, 1x1 Conv M->16; the middle Conv is the second igemm
@@ -61,6 +63,23 @@ def main(argv):
         for _ in range(reps):
             out = m.run({"input": x})
         print("resnet18", out["fc_out"].shape)
+    elif mode == "engine_conv":
+        from .model import Model
+        from .onnx_io import FLOAT, Graph
+
+        n, c, h, w, m_, k, s, p = (int(v) for v in argv[1:9])
+        reps = int(argv[9]) if len(argv) > 9 else 3
+        g = Graph(opset=13)
+        x = g.add_input("x", [n, c, h, w])
+        wt = g.const("w", synth.normal((m_, c, k, k), (2.0 / (c * k * k)) ** 0.5, 2))
+        g.add_output(g.op("Conv", [x, wt], name="conv", kernel_shape=[k, k], strides=[s, s], pads=[p] * 4),
+                     None, FLOAT)
+        m = Model(g, {"x": [n, c, h, w]})
+        feed = {"x": synth.uniform((n, c, h, w), -1.0, 1.0, 1)}
+        for _ in range(reps):
+            out = m.run(feed)
+        m.close()
+        print("engine_conv", next(iter(out.values())).shape)
     elif mode == "chain":
         from . import configs
         from .model import Model
