@@ -680,6 +680,9 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             const float* x = F(n.inputs[0]);
             float* y = F(e.out);
             const int64_t pbytes = static_cast<int64_t>(conv_packed_bytes(geom));
+            // the contraction kernel, plus a reduce launch when it splits K
+            const int conv_k = contraction_launches(dev_, geom.N * geom.OH * geom.OW, geom.Mg(), geom.K(), geom.group);
+            st.launches = conv_k;
             if (packed_conv.count(n.inputs[1])) {
                 // pack once at load from a temporary upload of the raw weight
                 uint8_t* packed = dmalloc(align_up(pbytes));
@@ -697,7 +700,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 if (geom.in_c4) {
                     float* x4 = reinterpret_cast<float*>(dmalloc(align_up(geom.N * geom.H * geom.W * 16)));
                     st.label += "[c4]";
-                    st.launches = 2;
+                    st.launches = conv_k + 1;
                     st.run = [=] {
                         nchw_to_nhwc4(dev, x, x4, geom.N, geom.C, geom.H, geom.W);
                         conv_run(dev, geom, x4, packed, y, ep);
@@ -710,7 +713,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 scratch_need = std::max(scratch_need, pbytes);
                 nb2_device* dev = dev_;
                 void** sp = &scratch_;
-                st.launches = geom.tap_major() ? 2 : 3;
+                st.launches = conv_k + (geom.tap_major() ? 1 : 2);
                 st.run = [=] {
                     conv_pack(dev, geom, w, *sp);
                     conv_run(dev, geom, x, *sp, y, ep);
@@ -805,6 +808,8 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             float* y = F(e.out);
             const int64_t pbytes = static_cast<int64_t>(gemm_packed_bytes(gg));
             nb2_device* dev = dev_;
+            const int gemm_k = contraction_launches(dev_, gg.M, gg.N, gg.K, gg.batch);
+            st.launches = gemm_k;
             if (packed_gemm.count(n.inputs[1])) {
                 uint8_t* packed = dmalloc(align_up(pbytes));
                 gemm_pack_b(dev_, gg, F(n.inputs[1]), packed);
@@ -815,7 +820,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 const float* B = F(n.inputs[1]);
                 scratch_need = std::max(scratch_need, pbytes);
                 void** sp = &scratch_;
-                st.launches = 2;
+                st.launches = gemm_k + 1;
                 st.run = [=] {
                     gemm_pack_b(dev, gg, B, *sp);
                     gemm_run(dev, gg, A, *sp, y, ep);

@@ -49,6 +49,12 @@ enum AMode : int {
 
 struct Args {
     int M, N, K, nkb;
+    // split K: work unit = (tile, K slice); slice ks covers K blocks
+    // [ks*kper, min(nkb, (ks+1)*kper)); with ksplit > 1 the epilogue writes
+    // raw fp32 partial sums to part[((ks*zcount + z)*M + row)*N + col] and a
+    // second kernel reduces them and applies the real epilogue
+    int ksplit, kper;
+    float* part;
     int zcount; // batch / group slices
     int mode;
     const float* a;
@@ -346,7 +352,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
     const int num_m = (p.M + 127) / 128;
     const int num_n = (p.N + BN - 1) / BN;
     const int tiles_per_z = num_m * num_n;
-    const int num_tiles = tiles_per_z * p.zcount;
+    const int num_tiles = tiles_per_z * p.zcount * p.ksplit; // work units
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -396,12 +402,19 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
     const uint32_t tmem = *tmem_slot;
 
     // tile t -> (z, n_tile, m_tile), m fastest
+    // unit t -> (K slice, z, n tile, m tile), m fastest; kb0 / kcnt = the
+    // slice's first K block and block count
     auto decode = [&](int t, int& z, int& m0, int& n0) {
-        z = t / tiles_per_z;
-        const int r = t - z * tiles_per_z;
+        const int u = t % (tiles_per_z * p.zcount);
+        z = u / tiles_per_z;
+        const int r = u - z * tiles_per_z;
         const int nt = r / num_m;
         m0 = (r - nt * num_m) * 128;
         n0 = nt * BN;
+    };
+    auto kslice = [&](int t, int& kb0, int& kcnt) {
+        kb0 = (t / (tiles_per_z * p.zcount)) * p.kper;
+        kcnt = min(nkb - kb0, p.kper);
     };
 
     if (warp >= C::kEpiWarps && warp < C::kEpiWarps + C::kProdWarps) {
@@ -417,9 +430,12 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             // Even ring depth: every use of a stage falls to one group, which
             // waits on its phases in order.
             static_assert(S % 2 == 0, "converter groups need an even ring depth");
-            const uint32_t items = static_cast<uint32_t>(((num_tiles - static_cast<int>(blockIdx.x) +
-                                                           static_cast<int>(gridDim.x) - 1) /
-                                                          static_cast<int>(gridDim.x)) * nkb);
+            uint32_t items = 0;
+            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+                int kb0, kcnt;
+                kslice(t, kb0, kcnt);
+                items += static_cast<uint32_t>(kcnt);
+            }
             const uint32_t tq = tmem + (static_cast<uint32_t>((pw & 3) * 32) << 16) + C::kAccCols;
             for (uint32_t g = static_cast<uint32_t>(pw >> 2); g < items; g += 2) {
                 const int s = static_cast<int>(g % S);
@@ -461,17 +477,24 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         // The (tile, K block) items of this CTA form one stream: the gather
         // cursor runs two items ahead of the stores, across tile boundaries,
         // so short-K layers also keep loads in flight.
-        int ct = blockIdx.x; // cursor tile
+        int ct = blockIdx.x; // cursor unit
         int ckb = 0;         // cursor K block
+        int ckb_end = 0;     // end of the cursor unit's K slice
         RowState rs;
         auto start_tile = [&](int t) {
-            int z, m0, n0;
+            int z, m0, n0, kb0, kcnt;
             decode(t, z, m0, n0);
+            kslice(t, kb0, kcnt);
+            ckb = kb0;
+            ckb_end = kb0 + kcnt;
             rs.m = m0 + r;
             rs.ok = rs.m < p.M;
-            rs.cin = 0;
-            rs.kh = 0;
-            rs.kw = 0;
+            // tap-major running position of the slice's first K block
+            const int k0 = kb0 * 32;
+            const int tap = p.Cg > 0 ? k0 / p.Cg : 0;
+            rs.cin = k0 - tap * p.Cg;
+            rs.kh = p.KW > 0 ? tap / p.KW : 0;
+            rs.kw = tap - rs.kh * p.KW;
             const float* az = p.a + (int64_t)z * p.a_zstride;
             if constexpr (MODE == kAConvTap || MODE == kAConvGeneric || MODE == kAConvC4) {
                 const int mm = rs.ok ? rs.m : 0;
@@ -497,8 +520,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 return false;
             }
             gather16<MODE>(p, rs, ckb, half, ktab, buf);
-            if (++ckb == nkb) {
-                ckb = 0;
+            if (++ckb == ckb_end) {
                 ct += gridDim.x;
                 if (ct < num_tiles) {
                     start_tile(ct);
@@ -580,7 +602,51 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 const float alpha = p.alpha, bsc = p.bias_scale, rsc = p.res_scale;
                 const uint32_t acc0 = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
                                       static_cast<uint32_t>(b * C::kAccs * BN);
-                const bool two = nkb > 1;
+                int kb0, kcnt;
+                kslice(t, kb0, kcnt);
+                const bool two = kcnt > 1;
+                if (p.ksplit > 1) {
+                    // raw partial sums of this K slice, row-major [M][N]
+                    float* prow = p.part + ((int64_t)(kb0 / p.kper) * p.zcount + z) * p.M * p.N + (int64_t)row * p.N;
+#pragma unroll 1
+                    for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
+                        if (n0 + cc >= p.N) {
+                            break;
+                        }
+                        float v[16], v1[16];
+                        tmem_ld16(acc0 + cc, v);
+                        if (two) {
+                            tmem_ld16(acc0 + BN + cc, v1);
+                        }
+                        if (two) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                v[j] += v1[j];
+                            }
+                        }
+                        if (row_ok && (p.N & 3) == 0 && n0 + cc + 16 <= p.N) {
+                            // N % 4 == 0: the partial rows are 16-byte aligned
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4) {
+                                *reinterpret_cast<float4*>(prow + n0 + cc + j) =
+                                    make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                            }
+                        } else if (row_ok) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                if (n0 + cc + j < p.N) {
+                                    prow[n0 + cc + j] = v[j];
+                                }
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&acc_empty[b]);
+                    }
+                    continue;
+                }
 #pragma unroll 1
                 for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
                     if (n0 + cc >= p.N) {
@@ -729,7 +795,9 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     nh0 = oh * p.sh - p.ph;
                     nw0 = (pix - oh * p.OW) * p.sw - p.pw;
                 }
-                for (int kb = 0; kb < nkb; ++kb, ++g) {
+                int kb0, kcnt;
+                kslice(t, kb0, kcnt);
+                for (int kb = kb0; kb < kb0 + kcnt; ++kb, ++g) {
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
                     uint64_t* free_bar = role == 1 ? &empty_a[s] : &empty[s];
@@ -780,8 +848,10 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 }
                 tc_fence_after();
                 const uint32_t d0 = tmem + static_cast<uint32_t>(b * C::kAccs * BN);
-                for (int kb = 0; kb < nkb; ++kb, ++g) {
-                    if ((kb & 1) != par) {
+                int kb0, kcnt;
+                kslice(t, kb0, kcnt);
+                for (int j = 0; j < kcnt; ++j, ++g) { // j = K block within the slice
+                    if ((j & 1) != par) {
                         continue; // the other issuer's K block
                     }
                     const int s = static_cast<int>(g % S); // smem B stage == TMEM A stage
@@ -793,11 +863,11 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = d0 + static_cast<uint32_t>((kb & 1) * BN);
+                    const uint32_t d = d0 + static_cast<uint32_t>((j & 1) * BN);
                     const uint32_t at = tmem + C::kAccCols + static_cast<uint32_t>(s * C::kAStageCols);
                     // a K step of 8 tf32 is 32 bytes: +2 in the descriptor's address field
                     const uint64_t bdh0 = sdesc_k128(smem_u32(b_hi(s))), bdl0 = sdesc_k128(smem_u32(b_lo(s)));
-                    const uint32_t first = kb < 2 ? 0u : 1u;
+                    const uint32_t first = j < 2 ? 0u : 1u;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t acc = kk == 0 ? first : 1u;
@@ -898,6 +968,48 @@ __global__ void conv_ktab_kernel(int2* tab, int K, int Kpad, int KHKW, int KW, i
     tab[k] = make_int2(static_cast<int>(cin * HW + (int64_t)kh * dh * W + (int64_t)kw * dw), ((kh * dh) << 16) | (kw * dw));
 }
 
+__device__ __forceinline__ float act_rt(float v, const Args& p) {
+    switch (p.act) {
+    case kActRelu:
+        return act_of<kActRelu>(v, p);
+    case kActSilu:
+        return act_of<kActSilu>(v, p);
+    case kActSigmoid:
+        return act_of<kActSigmoid>(v, p);
+    case kActGeluErf:
+        return act_of<kActGeluErf>(v, p);
+    default:
+        return v;
+    }
+}
+
+// Split K: sums the K slices' partials in slice order (deterministic) and
+// applies the contraction's epilogue and output layout.
+__global__ void splitk_reduce_kernel(const __grid_constant__ Args p) {
+    const int64_t total = (int64_t)p.zcount * p.M * p.N;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int col = static_cast<int>(i % p.N);
+        const int64_t t = i / p.N;
+        const int row = static_cast<int>(t % p.M);
+        const int z = static_cast<int>(t / p.M);
+        float acc = 0.0f;
+        for (int ks = 0; ks < p.ksplit; ++ks) {
+            acc += p.part[(int64_t)ks * total + i];
+        }
+        int64_t off;
+        if (p.conv_out) {
+            const int n_img = row / (int)p.OHW;
+            const int pix = row - n_img * (int)p.OHW;
+            off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix + (int64_t)col * p.OHW;
+        } else {
+            off = (int64_t)z * p.out_zstride + (int64_t)row * p.ldc + col;
+        }
+        const float bb = p.bias ? p.bias[(int64_t)z * p.bias_zstride + col] : 0.0f;
+        const float rv = p.res ? p.res[off] : 0.0f;
+        p.out[off] = act_rt(fmaf(p.res_scale, rv, fmaf(p.alpha, acc, p.bias_scale * bb)), p);
+    }
+}
+
 // 2-D fp32 map over [rows][inner] (row stride `ld` elements) with 32 x
 // box_rows boxes in the 128-byte swizzle; out-of-range boxes read zeros.
 void make_tmap(CUtensorMap* map, const float* base, int64_t inner, int64_t rows, int box_rows, int64_t ld = -1) {
@@ -960,6 +1072,28 @@ void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi,
     }
 }
 
+} // namespace
+
+int split_k_slices(const nb2_device* dev, int64_t tiles, int nkb, int* kper) {
+    *kper = nkb;
+    if (tiles * 2 > dev->num_sms || nkb < 8) {
+        return 1;
+    }
+    int ks = static_cast<int>(std::min<int64_t>(nkb / 4, (dev->num_sms + tiles - 1) / tiles));
+    *kper = (nkb + ks - 1) / ks;
+    return (nkb + *kper - 1) / *kper;
+}
+
+int contraction_launches(const nb2_device* dev, int64_t M, int64_t n_per_z, int64_t K, int64_t z) {
+    const int nkb = static_cast<int>((K + 31) / 32);
+    const int bn = (n_per_z <= 64 || nkb <= 4) ? 64 : 128;
+    const int64_t tiles = ((M + 127) / 128) * ((n_per_z + bn - 1) / bn) * z;
+    int kper = 0;
+    return split_k_slices(dev, tiles, nkb, &kper) > 1 ? 2 : 1;
+}
+
+namespace {
+
 void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total,
             const CUtensorMap* a_map = nullptr) {
     const int64_t kpad = static_cast<int64_t>(a.nkb) * 32;
@@ -993,13 +1127,35 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     if (tiles >= (1LL << 31)) {
         fail(kStatusUnsupported, "igemm: too many tiles");
     }
+    // Split K when the tiles would leave most SMs idle and K is long: each
+    // (tile, K slice) is a work unit, slices keep >= 4 K blocks.
+    a.ksplit = 1;
+    a.kper = a.nkb;
+    a.part = nullptr;
+    int kper = a.nkb;
+    const int ks = split_k_slices(dev, tiles, a.nkb, &kper);
+    if (ks > 1) {
+        const size_t bytes = static_cast<size_t>(ks) * static_cast<size_t>(z) * a.M * n_per_z * sizeof(float);
+        float* part = static_cast<float*>(dev->split_scratch(bytes));
+        if (part != nullptr) {
+            a.ksplit = ks;
+            a.kper = kper;
+            a.part = part;
+        }
+    }
     // persistent: one CTA per SM (shared memory admits exactly one)
-    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles, dev->num_sms)), 1, 1);
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles * a.ksplit, dev->num_sms)), 1, 1);
     const bool three = dev->precision == kPrec3xTF32;
     if (bn == 64) {
         three ? launch_bn<64, true>(dev, a, grid, hi, lo, am) : launch_bn<64, false>(dev, a, grid, hi, lo, am);
     } else {
         three ? launch_bn<128, true>(dev, a, grid, hi, lo, am) : launch_bn<128, false>(dev, a, grid, hi, lo, am);
+    }
+    if (a.ksplit > 1) {
+        const int64_t total = z * a.M * static_cast<int64_t>(n_per_z);
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, dev->num_sms * 8));
+        splitk_reduce_kernel<<<blocks, 256, 0, dev->stream>>>(a);
+        check_cuda(cudaGetLastError(), "split-K reduce launch");
     }
 }
 

@@ -63,6 +63,14 @@ struct ConvGeom {
 
 int64_t round_up(int64_t v, int64_t m);
 
+// K slices the contraction kernel uses for a problem with `tiles` output
+// tiles and `nkb` 32-wide K blocks (1 = no split; >1 adds a reduce launch);
+// *kper = K blocks per slice.
+int split_k_slices(const nb2_device* dev, int64_t tiles, int nkb, int* kper);
+// Kernel launches of one contraction (1, or 2 with split K): M rows, N
+// columns per z slice, K, z slices.
+int contraction_launches(const nb2_device* dev, int64_t M, int64_t n_per_z, int64_t K, int64_t z);
+
 // Bytes of the packed weight buffer of a Conv: hi and lo planes of
 // [M][Kpad] fp32, then (generic layout only) a Kpad-entry int2 tap table.
 size_t conv_packed_bytes(const ConvGeom& g);

@@ -114,6 +114,26 @@ void* nb2_device::scratch(size_t bytes) {
     return workspace;
 }
 
+void* nb2_device::split_scratch(size_t bytes) {
+    bytes = (bytes + 255) & ~size_t(255);
+    if (bytes <= split_ws_bytes) {
+        return split_ws;
+    }
+    if (capturing) {
+        return nullptr;
+    }
+    nb2::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(split workspace grow)");
+    if (split_ws != nullptr) {
+        nb2::check_cuda(cudaFree(split_ws), "cudaFree(split workspace)");
+        split_ws = nullptr;
+        split_ws_bytes = 0;
+    }
+    const size_t grow = std::max(bytes, split_ws_bytes * 2);
+    nb2::check_cuda(cudaMalloc(&split_ws, grow), "cudaMalloc(split workspace)");
+    split_ws_bytes = grow;
+    return split_ws;
+}
+
 int nb2_device::take_device_error() {
     int code = 0;
     nb2::check_cuda(cudaMemcpyAsync(&code, err_word, sizeof(int), cudaMemcpyDeviceToHost, stream),

@@ -68,6 +68,8 @@ struct nb2_device {
     size_t workspace_bytes = 0;
     void* pinned = nullptr;
     size_t pinned_bytes = 0;
+    void* split_ws = nullptr; // split-K partial sums (grow-only)
+    size_t split_ws_bytes = 0;
     int precision = nb2::kPrec3xTF32;
     int capturing = 0; // inside a CUDA-graph capture: the workspace may not grow
     int num_sms = 148;
@@ -79,6 +81,10 @@ struct nb2_device {
     // synchronises the stream first, so pointers from earlier calls stay
     // valid until the kernels that use them have finished.
     void* scratch(size_t bytes);
+    // Buffer for split-K partial sums of at least `bytes`, or nullptr when it
+    // would have to grow inside a CUDA-graph capture (the caller then runs
+    // without splitting K). Growing synchronises the stream first.
+    void* split_scratch(size_t bytes);
     // Reads and clears the device error word (synchronises the stream).
     int take_device_error();
 };

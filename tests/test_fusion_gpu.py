@@ -119,3 +119,31 @@ def test_fused_matmul_epilogues(cuda, kind):
         finally:
             m.close()
         assert rel_err(out, ref[name]) <= TOL, fuse
+
+
+def test_split_k_epilogue_matches_oracle(cuda):
+    """Few output tiles, long K: the contraction splits K into slices whose
+    partial sums are reduced in order before the fused bias + GELU epilogue."""
+    from nert_b200.model import Model
+
+    g = Graph(opset=13)
+    x = g.add_input("x", [4, 40, 2048])
+    w = synth.normal((2048, 96), 0.05, synth.seed_of("splitk", "w"))
+    b = synth.normal((96,), 0.1, synth.seed_of("splitk", "b"))
+    f = g.op("Add", [g.op("MatMul", [x, g.const("w", w)], name="mm"), g.const("b", b)], name="mm.bias")
+    e = g.op("Erf", [g.op("Div", [f, g.const("s2", np.array(np.sqrt(2.0), np.float32))], name="d")], name="erf")
+    e = g.op("Add", [e, g.const("one", np.array(1.0, np.float32))], name="a1")
+    y = g.op("Mul", [g.op("Mul", [f, e], name="m1"), g.const("h", np.array(0.5, np.float32))], name="m2")
+    g.add_output(y, None, FLOAT)
+    ins = {"x": synth.normal((4, 40, 2048), 1.0, synth.seed_of("splitk", "x"))}
+    ref = np_ref.run(g, ins)[y]
+    m = Model(g, {"x": [4, 40, 2048]})
+    try:
+        out = m.run(ins)[y]
+        again = m.run(ins)[y]
+        launches = m.stats()["kernels_per_run"]
+    finally:
+        m.close()
+    assert rel_err(out, ref) <= TOL
+    np.testing.assert_array_equal(out, again)  # the reduction order is fixed
+    assert launches == 2  # contraction + split-K reduce
