@@ -651,6 +651,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
 
     // ---- steps
     int64_t scratch_need = 0;
+    int64_t xform_need = 0; // shared buffer for NCHW -> NHWC copies of Conv inputs
     std::vector<std::function<void(void*)>> pending; // steps needing the scratch pointer
     for (const auto& e : ex) {
         const Node& n = *e.node;
@@ -697,6 +698,10 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 cudaFree(tmp);
                 weight_bytes_ += pbytes;
                 nb2_device* dev = dev_;
+                // an NCHW input outside the channels-last trunk: a spatial
+                // filter reads it through TMA im2col after one transpose
+                const bool to_nhwc = !geom.in_c4 && !geom.in_nhwc && (flags & kNchwOnly) == 0 &&
+                                     geom.nhwc_input_ok() && geom.KH * geom.KW > 1 && geom.H * geom.W > 1;
                 if (geom.in_c4) {
                     float* x4 = reinterpret_cast<float*>(dmalloc(align_up(geom.N * geom.H * geom.W * 16)));
                     st.label += "[c4]";
@@ -704,6 +709,18 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                     st.run = [=] {
                         nchw_to_nhwc4(dev, x, x4, geom.N, geom.C, geom.H, geom.W);
                         conv_run(dev, geom, x4, packed, y, ep);
+                    };
+                } else if (to_nhwc) {
+                    ConvGeom gt = geom;
+                    gt.in_nhwc = true;
+                    xform_need = std::max(xform_need, geom.N * geom.C * geom.H * geom.W * 4);
+                    void** xp = &xform_;
+                    const std::vector<int64_t> xd = {geom.N, geom.C, geom.H, geom.W};
+                    st.label += "[t>nhwc]";
+                    st.launches = conv_k + 1;
+                    st.run = [=] {
+                        transpose(dev, x, *xp, xd, {0, 2, 3, 1}, 4);
+                        conv_run(dev, gt, static_cast<const float*>(*xp), packed, y, ep);
                     };
                 } else {
                     st.run = [=] { conv_run(dev, geom, x, packed, y, ep); };
@@ -970,6 +987,9 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
         }
         launches_ += st.launches;
         steps_.push_back(std::move(st));
+    }
+    if (xform_need > 0) {
+        xform_ = dmalloc(align_up(xform_need));
     }
     if (scratch_need > 0) {
         scratch_ = dmalloc(align_up(scratch_need));

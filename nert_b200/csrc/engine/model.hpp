@@ -78,6 +78,7 @@ class Model {
     std::vector<IOInfo> inputs_, outputs_;
     std::vector<void*> allocations_;
     void* scratch_ = nullptr;
+    void* xform_ = nullptr; // NHWC copy of an NCHW Conv input (shared by the steps)
     int64_t arena_bytes_ = 0, weight_bytes_ = 0, launches_ = 0, fused_groups_ = 0, nhwc_tensors_ = 0;
     bool use_graph_ = true;
     cudaGraphExec_t exec_ = nullptr;

@@ -156,3 +156,30 @@ def test_narrow_channel_conv_c4_path(cuda, case):
             m.close()
         assert any("[c4]" in lab for lab in labels) == cl, labels
         assert rel_err(out, ref[out_name]) <= TOL, cl
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(2, 64, 30, 26, 48, 3, 1, 1), (1, 96, 17, 17, 130, 5, 2, 2)],
+                         ids=["3x3", "5x5s2"])
+def test_nchw_graph_input_takes_transposed_tma_path(cuda, shape):
+    """A spatial Conv on an NCHW tensor with C % 32 == 0 (a single-op graph)
+    runs on an NHWC copy through TMA im2col; results match the oracle."""
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    n, c, h, w, m, k, s, p = shape
+    g = Graph(opset=13)
+    x = g.add_input("x", [n, c, h, w])
+    wt = synth.normal((m, c, k, k), (1.0 / (c * k * k)) ** 0.5, synth.seed_of("tnhwc", "w"))
+    y = g.op("Conv", [x, g.const("w", wt)], name="conv", kernel_shape=[k, k], strides=[s, s], pads=[p] * 4)
+    g.add_output(y, None, FLOAT)
+    feed = {"x": synth.normal((n, c, h, w), 1.0, synth.seed_of("tnhwc", "x"))}
+    ref = np_ref.run(g, feed)[y]
+    m_ = model.Model(g, {"x": [n, c, h, w]})
+    try:
+        out = m_.run(feed)[y]
+        labels = [lab for lab, _ in m_.profile()]
+    finally:
+        m_.close()
+    assert any("[t>nhwc]" in lab for lab in labels), labels
+    assert rel_err(out, ref) <= TOL
