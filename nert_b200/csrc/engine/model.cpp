@@ -664,12 +664,25 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             ConvGeom geom = conv_geom(n, shapes_.at(n.inputs[0]), shapes_.at(n.inputs[1]), shapes_.at(n.outputs[0]));
             geom.in_nhwc = nhwc.count(n.inputs[0]) > 0;
             geom.out_nhwc = nhwc.count(e.out) > 0;
-            // a narrow NCHW input (an image): convert it to x[N][H][W][4] so
-            // each tap is one 16-byte load (packed weights only)
-            geom.in_c4 = (flags & kNchwOnly) == 0 && !geom.in_nhwc && geom.c4_input_ok() &&
-                         packed_conv.count(n.inputs[1]) > 0;
             if (geom.in_nhwc || geom.out_nhwc) {
                 st.label += geom.in_nhwc ? (geom.out_nhwc ? "[nhwc]" : "[nhwc>nchw]") : "[nchw>nhwc]";
+            }
+            // An NCHW input outside the channels-last trunk (packed weights
+            // only) is converted to NHWC in front of the contraction: up to 16
+            // channels padded to 4, 8 or 16 (each tap one to four 16-byte
+            // loads); a spatial filter over more channels padded to a multiple
+            // of 32 and read through TMA im2col.
+            const bool convertible = (flags & kNchwOnly) == 0 && !geom.in_nhwc &&
+                                     packed_conv.count(n.inputs[1]) > 0 && geom.group == 1;
+            if (convertible && geom.C <= 16) {
+                geom.cvec = geom.C <= 4 ? 4 : (geom.C <= 8 ? 8 : 16);
+            } else if (convertible && geom.KH * geom.KW > 1 && geom.H * geom.W > 1) {
+                ConvGeom gp = geom;
+                gp.cpad = round_up(geom.C, 32);
+                gp.in_nhwc = true;
+                if (gp.nhwc_input_ok()) {
+                    geom = gp;
+                }
             }
             Epilogue ep;
             ep.bias = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;
@@ -698,29 +711,17 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 cudaFree(tmp);
                 weight_bytes_ += pbytes;
                 nb2_device* dev = dev_;
-                // an NCHW input outside the channels-last trunk: a spatial
-                // filter reads it through TMA im2col after one transpose
-                const bool to_nhwc = !geom.in_c4 && !geom.in_nhwc && (flags & kNchwOnly) == 0 &&
-                                     geom.nhwc_input_ok() && geom.KH * geom.KW > 1 && geom.H * geom.W > 1;
-                if (geom.in_c4) {
-                    float* x4 = reinterpret_cast<float*>(dmalloc(align_up(geom.N * geom.H * geom.W * 16)));
-                    st.label += "[c4]";
-                    st.launches = conv_k + 1;
-                    st.run = [=] {
-                        nchw_to_nhwc4(dev, x, x4, geom.N, geom.C, geom.H, geom.W);
-                        conv_run(dev, geom, x4, packed, y, ep);
-                    };
-                } else if (to_nhwc) {
-                    ConvGeom gt = geom;
-                    gt.in_nhwc = true;
-                    xform_need = std::max(xform_need, geom.N * geom.C * geom.H * geom.W * 4);
+                if (geom.cvec || geom.cpad) {
+                    // the converted input lives in the shared transform buffer
+                    const int64_t cp = geom.Cin();
+                    xform_need = std::max(xform_need, geom.N * cp * geom.H * geom.W * 4);
                     void** xp = &xform_;
-                    const std::vector<int64_t> xd = {geom.N, geom.C, geom.H, geom.W};
-                    st.label += "[t>nhwc]";
+                    st.label += geom.cvec == 4 ? "[c4]" : (geom.cvec ? "[c" + std::to_string(geom.cvec) + "]"
+                                                                     : "[t>nhwc]");
                     st.launches = conv_k + 1;
                     st.run = [=] {
-                        transpose(dev, x, *xp, xd, {0, 2, 3, 1}, 4);
-                        conv_run(dev, gt, static_cast<const float*>(*xp), packed, y, ep);
+                        nchw_to_nhwc_pad(dev, x, static_cast<float*>(*xp), geom.N, geom.C, geom.H, geom.W, cp);
+                        conv_run(dev, geom, static_cast<const float*>(*xp), packed, y, ep);
                     };
                 } else {
                     st.run = [=] { conv_run(dev, geom, x, packed, y, ep); };

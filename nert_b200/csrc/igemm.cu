@@ -34,9 +34,9 @@ namespace {
 // fp32 tile into shared memory and the producer warps split it in place.
 // kAConvNhwc: Conv over NHWC activations (C % 32 == 0); TMA im2col brings the
 // raw fp32 tile for one (filter tap, 32-channel block) per K block.
-// kAConvC4: Conv over x[N][H][W][4] (C <= 4 zero-padded to 4, e.g. a stem's
-// RGB input); K ordered (tap, channel), a K half-block is 4 taps, each one
-// 16-byte load.
+// kAConvCvec: Conv over x[N][H][W][cv] with cv = 4, 8 or 16 channels (C <= cv,
+// zero padded; e.g. a stem's RGB image); K ordered (tap, channel), so a
+// thread's 16 K values are 16 / cv taps of 16-byte vector loads.
 enum AMode : int {
     kAConvTap = 0,
     kAConvGeneric = 1,
@@ -44,7 +44,7 @@ enum AMode : int {
     kADenseM = 3,
     kADenseTma = 4,
     kAConvNhwc = 5,
-    kAConvC4 = 6
+    kAConvCvec = 6
 };
 
 struct Args {
@@ -207,16 +207,22 @@ __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, in
                 ++rs.kh;
             }
         }
-    } else if constexpr (MODE == kAConvC4) {
-        // 4 taps x 4 channels; ktab[t] = (kh*dh, kw*dw), y = -1 past the last tap
-        const int t0 = kb * 8 + half * 4;
+    } else if constexpr (MODE == kAConvCvec) {
+        // four 16-byte vectors; ktab[tap] = (kh*dh, kw*dw), y = -1 past the
+        // last tap; p.Cg = cv channels per tap (a power of two)
+        const int sh = 31 - __clz(p.Cg);
+        const int vpp = p.Cg >> 2; // vectors per pixel
+        const int k0 = kb * 32 + half * 16;
         const float4* img = reinterpret_cast<const float4*>(rs.base);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const int2 e = ktab[t0 + q];
+            const int k = k0 + 4 * q;
+            const int tap = k >> sh;
+            const int2 e = ktab[tap];
             const int ih = rs.ih0 + e.x, iw = rs.iw0 + e.y;
             const bool ok = rs.ok & (e.y >= 0) & ((unsigned)ih < (unsigned)p.H) & ((unsigned)iw < (unsigned)p.W);
-            const float4 t = ok ? __ldg(img + (int64_t)ih * p.W + iw) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 t = ok ? __ldg(img + ((int64_t)ih * p.W + iw) * vpp + ((k - (tap << sh)) >> 2))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
             v[4 * q] = t.x;
             v[4 * q + 1] = t.y;
             v[4 * q + 2] = t.z;
@@ -382,11 +388,11 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             }
             ktab = t;
         }
-    } else if constexpr (MODE == kAConvC4) {
-        // per-tap filter offsets, built here (8 taps per K block)
+    } else if constexpr (MODE == kAConvCvec) {
+        // per-tap filter offsets, built here (32 / cv taps per K block)
         int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512 + C::kEpiBytes);
         const int taps = p.KH * p.KW;
-        for (int k = threadIdx.x; k < nkb * 8; k += blockDim.x) {
+        for (int k = threadIdx.x; k < nkb * (32 / p.Cg); k += blockDim.x) {
             const int kh = k / p.KW;
             t[k] = k < taps ? make_int2(kh * p.dh, (k - kh * p.KW) * p.dw) : make_int2(0, -1);
         }
@@ -496,7 +502,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             rs.kh = p.KW > 0 ? tap / p.KW : 0;
             rs.kw = tap - rs.kh * p.KW;
             const float* az = p.a + (int64_t)z * p.a_zstride;
-            if constexpr (MODE == kAConvTap || MODE == kAConvGeneric || MODE == kAConvC4) {
+            if constexpr (MODE == kAConvTap || MODE == kAConvGeneric || MODE == kAConvCvec) {
                 const int mm = rs.ok ? rs.m : 0;
                 const int n_img = mm / (int)p.OHW;
                 const int pix = mm - n_img * (int)p.OHW;
@@ -1063,8 +1069,8 @@ void launch_bn(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi,
     case kAConvNhwc:
         launch_mode<BN, THREE, kAConvNhwc>(dev, a, grid, hi, lo, am);
         break;
-    case kAConvC4:
-        launch_mode<BN, THREE, kAConvC4>(dev, a, grid, hi, lo, am);
+    case kAConvCvec:
+        launch_mode<BN, THREE, kAConvCvec>(dev, a, grid, hi, lo, am);
         break;
     default:
         launch_mode<BN, THREE, kADenseM>(dev, a, grid, hi, lo, am);
@@ -1111,9 +1117,9 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
                  (a.res == nullptr || al16(a.res)) && (a.bias == nullptr || (al16(a.bias) && a.bias_zstride % 4 == 0)))
                     ? 1
                     : 0;
-    a.ktab_smem = ((a.mode == kAConvGeneric && kpad * 8 <= 16384) || a.mode == kAConvC4) ? 1 : 0;
-    if (a.mode == kAConvC4 && kpad * 8 > 16384) {
-        fail(kStatusUnsupported, "Conv: filter too large for the 4-channel input path");
+    a.ktab_smem = ((a.mode == kAConvGeneric && kpad * 8 <= 16384) || a.mode == kAConvCvec) ? 1 : 0;
+    if (a.mode == kAConvCvec && kpad * 8 > 16384) {
+        fail(kStatusUnsupported, "Conv: filter too large for the narrow-channel input path");
     }
     // row-major A with 16-byte rows: TMA it (a zero stride broadcasts one A)
     CUtensorMap am = a_map ? *a_map : hi;
@@ -1216,12 +1222,12 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.N = static_cast<int>(g.Mg());
     a.K = static_cast<int>(K);
     a.nkb = static_cast<int>(kpad / 32);
-    a.mode = g.in_c4 ? kAConvC4 : g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
+    a.mode = g.cvec ? kAConvCvec : g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
     if (g.in_nhwc && !g.nhwc_input_ok()) {
         fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 32 == 0 and strides <= 8");
     }
-    if (g.in_c4 && (!g.c4_input_ok() || g.in_nhwc)) {
-        fail(kStatusUnsupported, "Conv: the 4-channel input form needs group 1 and C <= 4");
+    if (g.cvec && (!g.cvec_input_ok(g.cvec) || g.in_nhwc)) {
+        fail(kStatusUnsupported, "Conv: the narrow-channel input form needs group 1, C <= cv, cv in {4, 8, 16}");
     }
     a.a = x;
     a.a_zstride = g.Cg() * g.H * g.W;
@@ -1238,10 +1244,10 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.pw = static_cast<int>(g.pw);
     a.dh = static_cast<int>(g.dh);
     a.dw = static_cast<int>(g.dw);
-    a.Cg = static_cast<int>(g.Cg());
+    a.Cg = static_cast<int>(g.Cpad()); // channels per tap in the K layout
     a.HW = g.H * g.W;
     a.OHW = ohw;
-    a.img_stride = (g.in_c4 ? 4 : g.C) * g.H * g.W;
+    a.img_stride = g.Cin() * g.H * g.W;
     const float* hi = static_cast<const float*>(packed);
     a.ktab = g.tap_major() ? nullptr : reinterpret_cast<const int2*>(hi + 2 * g.M * kpad);
     a.b_zrows = static_cast<int>(g.Mg());
@@ -1263,10 +1269,11 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
         // start (the upper corner is pad_end - dil*(k-1), relative to the far
         // edge); 128 pixels x 32 channels per load, 128-byte swizzle.
         CUtensorMap am;
-        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(g.C), static_cast<cuuint64_t>(g.W),
+        const int64_t ci = g.Cin(); // channels held by the NHWC input (C, or padded)
+        const cuuint64_t dims[4] = {static_cast<cuuint64_t>(ci), static_cast<cuuint64_t>(g.W),
                                     static_cast<cuuint64_t>(g.H), static_cast<cuuint64_t>(g.N)};
-        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.C * 4), static_cast<cuuint64_t>(g.W * g.C * 4),
-                                       static_cast<cuuint64_t>(g.H * g.W * g.C * 4)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ci * 4), static_cast<cuuint64_t>(g.W * ci * 4),
+                                       static_cast<cuuint64_t>(g.H * g.W * ci * 4)};
         const int64_t pb = g.pad_bottom(), pr = g.pad_right();
         const int lower[2] = {static_cast<int>(-g.pw), static_cast<int>(-g.ph)};
         const int upper[2] = {static_cast<int>(pr - g.dw * (g.KW - 1)), static_cast<int>(pb - g.dh * (g.KH - 1))};

@@ -41,21 +41,27 @@ struct ConvGeom {
     // C ABI and the nert::Device rows are NCHW). An NHWC input needs
     // nhwc_input_ok(): A is then brought in by TMA im2col.
     bool in_nhwc = false, out_nhwc = false;
-    // Input given as x[N][H][W][4] (C <= 4 channels zero-padded to 4, a
-    // stem's image): K is ordered (tap, channel) with 4 channels per tap.
-    bool in_c4 = false;
+    // Narrow input given as x[N][H][W][cvec] (C <= cvec channels zero padded,
+    // cvec = 4, 8 or 16; e.g. a stem's image): K ordered (tap, channel).
+    int64_t cvec = 0;
+    // NHWC input holding cpad >= C channels (zero padded to a multiple of 32
+    // for the TMA im2col form); 0 = exactly C.
+    int64_t cpad = 0;
     int64_t Cg() const { return C / group; }
     int64_t Mg() const { return M / group; }
-    int64_t Cpad() const { return in_c4 ? 4 : Cg(); }
+    // channels per pixel of the input tensor
+    int64_t Cin() const { return cvec ? cvec : (cpad ? cpad : C); }
+    // channels per filter tap in the packed K layout
+    int64_t Cpad() const { return cvec ? cvec : (cpad ? cpad : Cg()); }
     int64_t K() const { return Cpad() * KH * KW; }
-    bool tap_major() const { return in_c4 || Cg() % 32 == 0; }
-    bool c4_input_ok() const { return group == 1 && C <= 4; }
+    bool tap_major() const { return cvec || cpad || Cg() % 32 == 0; }
+    bool cvec_input_ok(int64_t cv) const { return group == 1 && C <= cv && (cv == 4 || cv == 8 || cv == 16); }
     int64_t pad_bottom() const { return pb == kPadUnset ? ph : pb; }
     int64_t pad_right() const { return pr == kPadUnset ? pw : pr; }
     // TMA im2col limits for a 4-D map: traversal strides 1..8, box corners in
     // [-128, 127] and filter offsets in [0, 255] (kept well inside here).
     bool nhwc_input_ok() const {
-        return group == 1 && C % 32 == 0 && sh >= 1 && sh <= 8 && sw >= 1 && sw <= 8 && ph <= 64 && pw <= 64 &&
+        return group == 1 && Cin() % 32 == 0 && sh >= 1 && sh <= 8 && sw >= 1 && sw <= 8 && ph <= 64 && pw <= 64 &&
                pad_bottom() >= -64 && pad_bottom() <= 64 && pad_right() >= -64 && pad_right() <= 64 &&
                dh * (KH - 1) <= 64 && dw * (KW - 1) <= 64;
     }

@@ -45,9 +45,11 @@ void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
 void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
 // y[n][c] = mean over the hw pixels of channels-last x[n][hw][c]
 void mean_nhwc(nb2_device* dev, const float* x, float* y, int64_t n, int64_t hw, int64_t c);
-// x[N][C][H][W] (C <= 4) -> y[N][H][W][4], channels zero-padded to 4: the
-// input form of the 4-channel Conv path.
-void nchw_to_nhwc4(nb2_device* dev, const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W);
+// x[N][C][H][W] -> y[N][H][W][Cp], channels zero padded to Cp (4, 8, 16 or a
+// multiple of 32): the input forms of the narrow-channel and TMA im2col Conv
+// paths for tensors that arrive NCHW.
+void nchw_to_nhwc_pad(nb2_device* dev, const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
+                      int64_t Cp);
 // mean over the trailing `inner` elements of each of `rows` rows
 void row_mean(nb2_device* dev, const float* x, float* y, int64_t rows, int64_t inner);
 

@@ -264,42 +264,81 @@ unsigned blocks_for(nb2_device* dev, int64_t n) {
     return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, dev->num_sms * 16)));
 }
 
-// One thread per pixel; channel planes are read coalesced along W and the
-// pixel's four channels written as one 16-byte vector.
-__global__ void nchw_to_nhwc4_kernel(const float* __restrict__ x, float4* __restrict__ y, uint32_t C, uint32_t HW,
-                                     uint32_t total) {
+// NCHW -> NHWC with the channels zero padded to CP (4, 8 or 16): one thread
+// per pixel; channel planes are read coalesced along the pixels and the
+// pixel's CP channels written as CP/4 16-byte vectors.
+template <int CP>
+__global__ void nchw_to_nhwc_narrow_kernel(const float* __restrict__ x, float4* __restrict__ y, uint32_t C,
+                                           uint32_t HW, uint32_t total) {
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const uint32_t n = i / HW, p = i - n * HW;
         const float* src = x + (size_t)n * C * HW + p;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        v.x = __ldg(src);
-        if (C > 1) {
-            v.y = __ldg(src + HW);
+        float v[CP];
+#pragma unroll
+        for (int c = 0; c < CP; ++c) {
+            v[c] = (uint32_t)c < C ? __ldg(src + (size_t)c * HW) : 0.0f;
         }
-        if (C > 2) {
-            v.z = __ldg(src + 2 * (size_t)HW);
+#pragma unroll
+        for (int q = 0; q < CP / 4; ++q) {
+            y[(size_t)i * (CP / 4) + q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         }
-        if (C > 3) {
-            v.w = __ldg(src + 3 * (size_t)HW);
+    }
+}
+
+// NCHW -> NHWC with the channels zero padded to Cp (a multiple of 32): 32 x 32
+// (channel x pixel) tiles through shared memory, both sides coalesced.
+__global__ void nchw_to_nhwc_tile_kernel(const float* __restrict__ x, float* __restrict__ y, int C, int Cp,
+                                         int64_t HW) {
+    __shared__ float tile[32][33];
+    const int64_t n = blockIdx.z;
+    const int c0 = blockIdx.y * 32;
+    const int64_t p0 = blockIdx.x * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int c = c0 + i;
+        const int64_t p = p0 + threadIdx.x;
+        tile[i][threadIdx.x] = (c < C && p < HW) ? __ldg(x + (n * C + c) * HW + p) : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        const int64_t p = p0 + i;
+        const int c = c0 + threadIdx.x;
+        if (p < HW) {
+            y[(n * HW + p) * Cp + c] = tile[threadIdx.x][i];
         }
-        y[i] = v;
     }
 }
 
 } // namespace
 
-void nchw_to_nhwc4(nb2_device* dev, const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W) {
-    const int64_t total = N * H * W;
+void nchw_to_nhwc_pad(nb2_device* dev, const float* x, float* y, int64_t N, int64_t C, int64_t H, int64_t W,
+                      int64_t Cp) {
+    const int64_t HW = H * W, total = N * HW;
     if (total <= 0) {
         return;
     }
-    if (C < 1 || C > 4 || total >= (int64_t(1) << 31) || H * W >= (int64_t(1) << 31)) {
-        fail(kStatusUnsupported, "nchw_to_nhwc4: needs 1 <= C <= 4 and fewer than 2^31 pixels");
+    if (C < 1 || C > Cp || total >= (int64_t(1) << 31)) {
+        fail(kStatusUnsupported, "nchw_to_nhwc_pad: needs 1 <= C <= Cp and fewer than 2^31 pixels");
     }
-    nchw_to_nhwc4_kernel<<<blocks_for(dev, total), 256, 0, dev->stream>>>(
-        x, reinterpret_cast<float4*>(y), static_cast<uint32_t>(C), static_cast<uint32_t>(H * W),
-        static_cast<uint32_t>(total));
-    check_cuda(cudaGetLastError(), "nchw_to_nhwc4 launch");
+    if (Cp == 4 || Cp == 8 || Cp == 16) {
+        const auto c = static_cast<uint32_t>(C), hw = static_cast<uint32_t>(HW), t = static_cast<uint32_t>(total);
+        auto* y4 = reinterpret_cast<float4*>(y);
+        const unsigned g = blocks_for(dev, total);
+        if (Cp == 4) {
+            nchw_to_nhwc_narrow_kernel<4><<<g, 256, 0, dev->stream>>>(x, y4, c, hw, t);
+        } else if (Cp == 8) {
+            nchw_to_nhwc_narrow_kernel<8><<<g, 256, 0, dev->stream>>>(x, y4, c, hw, t);
+        } else {
+            nchw_to_nhwc_narrow_kernel<16><<<g, 256, 0, dev->stream>>>(x, y4, c, hw, t);
+        }
+    } else if (Cp % 32 == 0 && N <= 65535 && Cp / 32 <= 65535) {
+        const dim3 grid(static_cast<unsigned>((HW + 31) / 32), static_cast<unsigned>(Cp / 32),
+                        static_cast<unsigned>(N));
+        nchw_to_nhwc_tile_kernel<<<grid, dim3(32, 8), 0, dev->stream>>>(x, y, static_cast<int>(C),
+                                                                         static_cast<int>(Cp), HW);
+    } else {
+        fail(kStatusUnsupported, "nchw_to_nhwc_pad: Cp must be 4, 8, 16 or a multiple of 32");
+    }
+    check_cuda(cudaGetLastError(), "nchw_to_nhwc_pad launch");
 }
 
 void segment_copy(nb2_device* dev, const std::vector<CopySeg>& segs) {

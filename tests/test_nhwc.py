@@ -123,7 +123,16 @@ C4_CASES = [
     ("patch16", 2, 3, 224, 224, 96, (16, 16), (16, 16), (0, 0, 0, 0), (1, 1)),
     ("c1_dil", 1, 1, 37, 41, 40, (3, 5), (1, 2), (2, 1, 0, 3), (2, 1)),
     ("c4_odd", 3, 4, 19, 23, 130, (5, 5), (3, 3), (2, 2, 2, 2), (1, 1)),
+    ("c6_3x3", 2, 6, 33, 35, 24, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1)),
+    ("c8_3x3s2", 2, 8, 40, 48, 32, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1)),
+    ("c12_5x5", 1, 12, 29, 31, 70, (5, 5), (1, 1), (2, 2, 2, 2), (1, 1)),
+    ("c16_3x3s2", 2, 16, 64, 80, 32, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1)),
+    ("c16_1x1", 2, 16, 20, 20, 48, (1, 1), (1, 1), (0, 0, 0, 0), (1, 1)),
 ]
+
+
+def _cvec_label(c):
+    return "[c4]" if c <= 4 else ("[c8]" if c <= 8 else "[c16]")
 
 
 def _c4_graph(case):
@@ -144,7 +153,11 @@ def _c4_graph(case):
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", C4_CASES, ids=[c[0] for c in C4_CASES])
 def test_narrow_channel_conv_c4_path(cuda, case):
+    """NCHW inputs with up to 16 channels run on an NHWC copy padded to 4, 8
+    or 16 channels (one to four 16-byte loads per tap); off with
+    channels_last=False."""
     g, feed = _c4_graph(case)
+    tag = _cvec_label(case[2])
     ref = np_ref.run(g, feed)
     out_name = g.outputs[0][0]
     for cl in (True, False):
@@ -154,16 +167,19 @@ def test_narrow_channel_conv_c4_path(cuda, case):
             labels = [lab for lab, _ in m.profile()]
         finally:
             m.close()
-        assert any("[c4]" in lab for lab in labels) == cl, labels
+        assert any(tag in lab for lab in labels) == cl, labels
         assert rel_err(out, ref[out_name]) <= TOL, cl
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", [(2, 64, 30, 26, 48, 3, 1, 1), (1, 96, 17, 17, 130, 5, 2, 2)],
-                         ids=["3x3", "5x5s2"])
+@pytest.mark.parametrize("shape", [(2, 64, 30, 26, 48, 3, 1, 1), (1, 96, 17, 17, 130, 5, 2, 2),
+                                   (2, 48, 21, 27, 40, 3, 1, 1), (1, 80, 18, 22, 64, 3, 2, 1),
+                                   (1, 17, 15, 16, 33, 5, 1, 2)],
+                         ids=["3x3", "5x5s2", "c48_3x3", "c80_3x3s2", "c17_5x5"])
 def test_nchw_graph_input_takes_transposed_tma_path(cuda, shape):
-    """A spatial Conv on an NCHW tensor with C % 32 == 0 (a single-op graph)
-    runs on an NHWC copy through TMA im2col; results match the oracle."""
+    """A spatial Conv on an NCHW tensor with more than 16 channels (a
+    single-op graph) runs on an NHWC copy, channels zero padded to a multiple
+    of 32, through TMA im2col; results match the oracle."""
     from nert_b200 import synth
     from nert_b200.onnx_io import FLOAT, Graph
 
