@@ -110,9 +110,12 @@ struct Cfg {
     // converter once read) and the B hi / lo planes (released by the MMA)
     static constexpr int kStageBytes = kAPlane + kBStageBytes;
     static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
-    // two accumulators per tile (even / odd K blocks) x kAccBufs tiles in
-    // flight: two for BN = 64 (the epilogue overlaps the next tile's MMAs),
-    // one for BN = 128 (the other 256 columns hold the A stages)
+    // two accumulators per tile (even / odd K blocks, one per MMA issuer) x
+    // kAccBufs tiles in flight: two for BN = 64 (the epilogue overlaps the
+    // next tile's MMAs), one for BN = 128 (the other 256 columns hold the A
+    // stages). Measured: one issuer per tile with two 128-wide tiles in
+    // flight is slower wherever an SM gets one or two tiles (the issuer's
+    // wake-ups between K blocks are then exposed).
     static constexpr int kAccs = 2;
     static constexpr int kAccBufs = BN <= 64 ? 2 : 1;
     static constexpr int kAccCols = kAccBufs * kAccs * BN;
@@ -144,7 +147,9 @@ struct Cfg {
     static constexpr int kMma2Warp = kTmaWarp + 4;          // odd K blocks
     static constexpr int kThreads = (kTmaWarp + 5) * 32;
     // epilogue staging: one 32 x 17 fp32 tile per epilogue warp (row-major
-    // outputs whose rows are not 16-byte aligned leave as 64-byte pieces)
+    // outputs whose rows are not 16-byte aligned leave as 64-byte pieces).
+    // Measured: staging 16-byte rows the same way is slower than storing
+    // one 16-byte vector per row directly.
     static constexpr int kEpiTileFloats = 32 * 17;
     static constexpr int kEpiBytes = kEpiWarps * kEpiTileFloats * 4;
     static constexpr int kSmemBytes = kRingBytes + 1024 + 512 + kEpiBytes;
@@ -184,6 +189,33 @@ struct RowState {
     int cin, kh, kw;
 };
 
+// Narrow-channel gather: the half's 16 K values are 16 / CV whole filter
+// taps of CV channels (one to four 16-byte loads per tap). tab[tap] = (kh*dh,
+// kw*dw, 16-byte offset of the tap from the window's top-left pixel); past
+// the last tap x is far out of range, so the bounds test rejects it.
+template <int CV>
+__device__ __forceinline__ void gather_cvec(const Args& p, const RowState& rs, int kb, int half, const int4* tab,
+                                            float (&v)[16]) {
+    constexpr int kTaps = 16 / CV;
+    constexpr int kVec = CV / 4;
+    const int t0 = (kb * 32 + half * 16) / CV;
+    const float4* base = reinterpret_cast<const float4*>(rs.base);
+#pragma unroll
+    for (int t = 0; t < kTaps; ++t) {
+        const int4 e = tab[t0 + t];
+        const bool ok = rs.ok & ((unsigned)(rs.ih0 + e.x) < (unsigned)p.H) & ((unsigned)(rs.iw0 + e.y) < (unsigned)p.W);
+#pragma unroll
+        for (int q = 0; q < kVec; ++q) {
+            const float4 f = ok ? __ldg(base + e.z + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int o = (t * kVec + q) * 4;
+            v[o] = f.x;
+            v[o + 1] = f.y;
+            v[o + 2] = f.z;
+            v[o + 3] = f.w;
+        }
+    }
+}
+
 template <int MODE>
 __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, int half, const int2* ktab,
                                          float (&v)[16]) {
@@ -208,25 +240,13 @@ __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, in
             }
         }
     } else if constexpr (MODE == kAConvCvec) {
-        // four 16-byte vectors; ktab[tap] = (kh*dh, kw*dw), y = -1 past the
-        // last tap; p.Cg = cv channels per tap (a power of two)
-        const int sh = 31 - __clz(p.Cg);
-        const int vpp = p.Cg >> 2; // vectors per pixel
-        const int k0 = kb * 32 + half * 16;
-        const float4* img = reinterpret_cast<const float4*>(rs.base);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int k = k0 + 4 * q;
-            const int tap = k >> sh;
-            const int2 e = ktab[tap];
-            const int ih = rs.ih0 + e.x, iw = rs.iw0 + e.y;
-            const bool ok = rs.ok & (e.y >= 0) & ((unsigned)ih < (unsigned)p.H) & ((unsigned)iw < (unsigned)p.W);
-            const float4 t = ok ? __ldg(img + ((int64_t)ih * p.W + iw) * vpp + ((k - (tap << sh)) >> 2))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-            v[4 * q] = t.x;
-            v[4 * q + 1] = t.y;
-            v[4 * q + 2] = t.z;
-            v[4 * q + 3] = t.w;
+        const int4* tab = reinterpret_cast<const int4*>(ktab);
+        if (p.Cg == 4) {
+            gather_cvec<4>(p, rs, kb, half, tab, v);
+        } else if (p.Cg == 8) {
+            gather_cvec<8>(p, rs, kb, half, tab, v);
+        } else {
+            gather_cvec<16>(p, rs, kb, half, tab, v);
         }
     } else if constexpr (MODE == kAConvGeneric) {
         // per-k tap table (shared memory when it fits); branch-free: an
@@ -390,13 +410,13 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         }
     } else if constexpr (MODE == kAConvCvec) {
         // per-tap filter offsets, built here (32 / cv taps per K block)
-        int2* t = reinterpret_cast<int2*>(smem + C::kRingBytes + 512 + C::kEpiBytes);
+        int4* t = reinterpret_cast<int4*>(smem + C::kRingBytes + 512 + C::kEpiBytes);
         const int taps = p.KH * p.KW;
         for (int k = threadIdx.x; k < nkb * (32 / p.Cg); k += blockDim.x) {
-            const int kh = k / p.KW;
-            t[k] = k < taps ? make_int2(kh * p.dh, (k - kh * p.KW) * p.dw) : make_int2(0, -1);
+            const int kh = k / p.KW, dy = kh * p.dh, dx = (k - kh * p.KW) * p.dw;
+            t[k] = k < taps ? make_int4(dy, dx, (dy * p.W + dx) * (p.Cg >> 2), 0) : make_int4(-(1 << 24), 0, 0, 0);
         }
-        ktab = t;
+        ktab = reinterpret_cast<const int2*>(t);
     }
     if (warp == 0) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -511,7 +531,12 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 rs.ih0 = oh * p.sh - p.ph;
                 rs.iw0 = ow * p.sw - p.pw;
                 const float* img = az + (int64_t)n_img * p.img_stride;
-                rs.base = (MODE == kAConvGeneric) ? img + (int64_t)rs.ih0 * p.W + rs.iw0 : img;
+                // generic: the window's top-left pixel of each channel plane;
+                // narrow channels: that pixel's vector (either may lie
+                // outside the image: only in-window taps are read)
+                rs.base = (MODE == kAConvGeneric) ? img + (int64_t)rs.ih0 * p.W + rs.iw0
+                          : (MODE == kAConvCvec)  ? img + ((int64_t)rs.ih0 * p.W + rs.iw0) * p.Cg
+                                                  : img;
             } else if constexpr (MODE == kADenseK) {
                 rs.base = az + (int64_t)(rs.ok ? rs.m : 0) * p.lda;
             } else {
@@ -610,7 +635,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                                       static_cast<uint32_t>(b * C::kAccs * BN);
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
-                const bool two = kcnt > 1;
+                const bool two = kcnt > 1; // odd-block accumulator in use
                 if (p.ksplit > 1) {
                     // raw partial sums of this K slice, row-major [M][N]
                     float* prow = p.part + ((int64_t)(kb0 / p.kper) * p.zcount + z) * p.M * p.N + (int64_t)row * p.N;
@@ -848,14 +873,14 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             int i = 0;
             bool alive = true;
             for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++i) {
+                int kb0, kcnt;
+                kslice(t, kb0, kcnt);
                 const int b = i % C::kAccBufs;
                 if (!mbar_wait(&acc_empty[b], ((i / C::kAccBufs) & 1) ^ 1, abort_flag, p.err)) {
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d0 = tmem + static_cast<uint32_t>(b * C::kAccs * BN);
-                int kb0, kcnt;
-                kslice(t, kb0, kcnt);
                 for (int j = 0; j < kcnt; ++j, ++g) { // j = K block within the slice
                     if ((j & 1) != par) {
                         continue; // the other issuer's K block
@@ -873,6 +898,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     const uint32_t at = tmem + C::kAccCols + static_cast<uint32_t>(s * C::kAStageCols);
                     // a K step of 8 tf32 is 32 bytes: +2 in the descriptor's address field
                     const uint64_t bdh0 = sdesc_k128(smem_u32(b_hi(s))), bdl0 = sdesc_k128(smem_u32(b_lo(s)));
+                    // the first K block into an accumulator overwrites it
                     const uint32_t first = j < 2 ? 0u : 1u;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
@@ -1222,6 +1248,10 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     a.N = static_cast<int>(g.Mg());
     a.K = static_cast<int>(K);
     a.nkb = static_cast<int>(kpad / 32);
+    // NHWC inputs always take TMA im2col: measured, gathering the same
+    // channels-last rows with 16-byte loads from the producer warps is
+    // 20-50% slower per layer even where one im2col copy per K block
+    // (~850 cycles) bounds the main loop
     a.mode = g.cvec ? kAConvCvec : g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
     if (g.in_nhwc && !g.nhwc_input_ok()) {
         fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 32 == 0 and strides <= 8");
