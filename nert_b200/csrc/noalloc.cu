@@ -80,6 +80,15 @@ extern "C" int nb2_conv2d_noalloc(nb2_device* dev, const nb2_conv_geom* g, const
         }
         dev->make_current();
         void* scratch = scratch_address(dev);
+        // a layer that would split K uses the split workspace only if it
+        // already exists and is large enough; it never grows here, so such
+        // a layer otherwise runs unsplit (same results)
+        struct NoGrow {
+            nb2_device* d;
+            int prev;
+            ~NoGrow() { d->no_grow = prev; }
+        } guard{dev, dev->no_grow};
+        dev->no_grow = 1;
         nb2::conv_pack(dev, geom, w, scratch);
         nb2::Epilogue ep;
         ep.bias = bias;

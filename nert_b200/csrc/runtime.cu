@@ -119,8 +119,8 @@ void* nb2_device::split_scratch(size_t bytes) {
     if (bytes <= split_ws_bytes) {
         return split_ws;
     }
-    if (capturing) {
-        return nullptr;
+    if (capturing || no_grow) {
+        return nullptr; // the caller then runs the contraction unsplit
     }
     nb2::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(split workspace grow)");
     if (split_ws != nullptr) {

@@ -72,6 +72,7 @@ struct nb2_device {
     size_t split_ws_bytes = 0;
     int precision = nb2::kPrec3xTF32;
     int capturing = 0; // inside a CUDA-graph capture: the workspace may not grow
+    int no_grow = 0;   // inside a call that must not allocate: split K runs only in the existing workspace
     int num_sms = 148;
     std::mutex mu;
 

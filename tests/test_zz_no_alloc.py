@@ -71,3 +71,29 @@ def test_noalloc_rejects_weights_above_capacity(cuda):
     st = _call("nb2_conv2d_noalloc", dev, g, x, w, None, y)
     assert st == _lib.ERR_INVALID
     assert "static scratch" in lib.nb2_last_error().decode()
+
+
+def test_noalloc_long_k_layer_matches_conv2d(cuda):
+    """A layer with one output tile and a long K, which nb2_conv2d runs with
+    split K in a growable workspace: the no-alloc call never grows that
+    workspace (it runs unsplit when the workspace is absent or too small),
+    and both orders of the two calls agree with each other."""
+    import torch
+
+    lib = _lib.lib()
+    dev = _lib.device(0)
+    n, c, h, w, m, k = 1, 256, 7, 7, 96, 3
+    x = torch.from_numpy(synth.normal((n, c, h, w), 1.0, 400)).cuda()
+    wt = torch.from_numpy(synth.normal((m, c, k, k), 1.0 / np.sqrt(c * k * k), 401)).cuda()
+    b = torch.from_numpy(synth.normal((m,), 1.0, 402)).cuda()
+    g = conv_geom(tuple(x.shape), tuple(wt.shape), (1, 1), (1, 1, 1, 1))
+    outs = []
+    for name in ("nb2_conv2d_noalloc", "nb2_conv2d", "nb2_conv2d_noalloc"):
+        y = torch.full((g.n, g.m, g.oh, g.ow), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        _lib.check(_call(name, dev, g, x, wt, b, y))
+        _lib.check(lib.nb2_device_synchronize(dev))
+        outs.append(y.cpu().numpy())
+    for got in (outs[0], outs[2]):
+        assert np.isfinite(got).all()
+        assert rel_err(got, outs[1]) <= TOL
