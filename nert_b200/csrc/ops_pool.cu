@@ -146,6 +146,45 @@ __global__ void maxpool2d_nhwc4_kernel(const float4* __restrict__ x, float4* __r
     }
 }
 
+// The same for a fixed KH x KW window without dilation: fully unrolled, so
+// all taps' loads are in flight together (an out-of-image tap reads as
+// -inf, which never wins the same comparison the generic kernel makes).
+template <int KH, int KW>
+__global__ void maxpool2d_nhwc4_fixed_kernel(const float4* __restrict__ x, float4* __restrict__ y, PoolGeom32 g,
+                                             uint32_t total) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const uint32_t c4 = i % g.C4;
+        uint32_t t = i / g.C4;
+        const int ow = static_cast<int>(t % g.OW);
+        t /= g.OW;
+        const int oh = static_cast<int>(t % g.OH);
+        const uint32_t n = t / g.OH;
+        const int h0 = oh * g.sh - g.ph;
+        const int w0 = ow * g.sw - g.pw;
+        const float4* base = x + (size_t)n * g.H * g.W * g.C4 + c4;
+        float4 v[KH * KW];
+#pragma unroll
+        for (int kh = 0; kh < KH; ++kh) {
+#pragma unroll
+            for (int kw = 0; kw < KW; ++kw) {
+                const int ih = h0 + kh, iw = w0 + kw;
+                const bool ok = (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
+                v[kh * KW + kw] = ok ? __ldg(base + ((size_t)ih * g.W + iw) * g.C4)
+                                     : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+        }
+        float4 best = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+#pragma unroll
+        for (int k = 0; k < KH * KW; ++k) {
+            best.x = v[k].x > best.x ? v[k].x : best.x;
+            best.y = v[k].y > best.y ? v[k].y : best.y;
+            best.z = v[k].z > best.z ? v[k].z : best.z;
+            best.w = v[k].w > best.w ? v[k].w : best.w;
+        }
+        y[i] = best;
+    }
+}
+
 __global__ void maxpool2d_nhwc1_kernel(const float* __restrict__ x, float* __restrict__ y, PoolGeom g, int64_t total) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t c = i % g.C;
@@ -216,8 +255,20 @@ void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y
                              static_cast<int>(g.KW), static_cast<int>(g.sh), static_cast<int>(g.sw),
                              static_cast<int>(g.ph), static_cast<int>(g.pw), static_cast<int>(g.dh),
                              static_cast<int>(g.dw)};
-        maxpool2d_nhwc4_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(
-            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), g32, static_cast<uint32_t>(total));
+        const auto* x4 = reinterpret_cast<const float4*>(x);
+        auto* y4 = reinterpret_cast<float4*>(y);
+        const auto tot = static_cast<uint32_t>(total);
+        const auto nb = static_cast<unsigned>(blocks);
+        const bool plain = g.dh == 1 && g.dw == 1;
+        if (plain && g.KH == 3 && g.KW == 3) {
+            maxpool2d_nhwc4_fixed_kernel<3, 3><<<nb, 256, 0, dev->stream>>>(x4, y4, g32, tot);
+        } else if (plain && g.KH == 5 && g.KW == 5) {
+            maxpool2d_nhwc4_fixed_kernel<5, 5><<<nb, 256, 0, dev->stream>>>(x4, y4, g32, tot);
+        } else if (plain && g.KH == 2 && g.KW == 2) {
+            maxpool2d_nhwc4_fixed_kernel<2, 2><<<nb, 256, 0, dev->stream>>>(x4, y4, g32, tot);
+        } else {
+            maxpool2d_nhwc4_kernel<<<nb, 256, 0, dev->stream>>>(x4, y4, g32, tot);
+        }
     } else {
         const int64_t total1 = g.N * g.OH * g.OW * g.C;
         const int64_t blocks1 = std::min<int64_t>((total1 + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
