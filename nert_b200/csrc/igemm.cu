@@ -106,9 +106,13 @@ struct Cfg {
     static constexpr int kBPlane = BN * 128;
     static constexpr int kPlanes = THREE ? 2 : 1;
     static constexpr int kBStageBytes = kBPlane * kPlanes;
-    // shared-memory stage: a raw A tile (TMA_A modes; released by the
-    // converter once read) and the B hi / lo planes (released by the MMA)
-    static constexpr int kStageBytes = kAPlane + kBStageBytes;
+    // shared-memory stage: a raw A tile (TMA_A modes only; released by the
+    // converter once read) and the B hi / lo planes (released by the MMA).
+    // The gather modes take no raw A space: the shared memory they leave
+    // unclaimed stays L1, which holds the overlapping filter windows their
+    // loads re-read.
+    static constexpr int kAStageBytes = TMA_A ? kAPlane : 0;
+    static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
     static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
     // two accumulators per tile (even / odd K blocks, one per MMA issuer) x
     // kAccBufs tiles in flight: two for BN = 64 (the epilogue overlaps the
@@ -367,9 +371,9 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    // the raw A ring (S x 16 KB), then the B ring (S x [B hi][B lo])
+    // the raw A ring (S x 16 KB, TMA_A modes), then the B ring (S x [B hi][B lo])
     auto a_raw = [&](int s) { return smem + s * C::kAPlane; };
-    auto b_hi = [&](int s) { return smem + S * C::kAPlane + s * C::kBStageBytes; };
+    auto b_hi = [&](int s) { return smem + S * C::kAStageBytes + s * C::kBStageBytes; };
     auto b_lo = [&](int s) { return b_hi(s) + C::kBPlane; };
 
     const int warp = threadIdx.x >> 5;
