@@ -39,7 +39,100 @@ struct ExecNode {
     int pos = 0;
     bool alias = false; // output is a view of input 0
     int group = 1;      // nodes in the group
+    // a MatMul whose (Reshape +) Transpose consumer was absorbed: the
+    // contraction writes its result straight into the transposed layout
+    std::vector<int64_t> view, perm;
 };
+
+// Output map of a contraction with z slices of R x C results viewed as
+// `view` (a split of [Z, R, C] into at most two axes each) and permuted by
+// `perm`: each view axis gets its stride in the permuted, contiguous
+// tensor. False when the view does not split Z, R and C that way or a
+// two-axis column split has an inner extent that is not a multiple of 16.
+bool make_out_map(const std::vector<int64_t>& view, const std::vector<int64_t>& perm, int64_t Z, int64_t R,
+                  int64_t C, OutMap* m) {
+    const size_t r = view.size();
+    if (perm.size() != r || r == 0) {
+        return false;
+    }
+    std::vector<int64_t> tstride(r, 1), vstride(r, 0);
+    for (size_t j = r - 1; j > 0; --j) {
+        tstride[j - 1] = tstride[j] * view[static_cast<size_t>(perm[j])];
+    }
+    std::vector<bool> seen(r, false);
+    for (size_t j = 0; j < r; ++j) {
+        if (perm[j] < 0 || perm[j] >= static_cast<int64_t>(r) || seen[static_cast<size_t>(perm[j])]) {
+            return false;
+        }
+        seen[static_cast<size_t>(perm[j])] = true;
+        vstride[static_cast<size_t>(perm[j])] = tstride[j];
+    }
+    // consume view axes (skipping size-1 axes) whose product is `want`,
+    // at most two of them: (outer, inner) -> radix and strides
+    size_t i = 0;
+    auto take = [&](int64_t want, int64_t& x2, int64_t& s1, int64_t& s2, int64_t round) -> bool {
+        std::vector<size_t> ax;
+        int64_t prod = 1;
+        while (i < r && prod < want) {
+            if (view[i] != 1) {
+                ax.push_back(i);
+                prod *= view[i];
+            }
+            ++i;
+        }
+        while (i < r && view[i] == 1 && want == 1) {
+            ++i;
+        }
+        if (prod != want || ax.size() > 2) {
+            return false;
+        }
+        if (ax.empty()) {
+            x2 = 1, s1 = 0, s2 = 0;
+        } else if (ax.size() == 1) {
+            x2 = (want + round - 1) / round * round, s1 = 0, s2 = vstride[ax[0]];
+        } else {
+            x2 = view[ax[1]], s1 = vstride[ax[0]], s2 = vstride[ax[1]];
+        }
+        return true;
+    };
+    OutMap o;
+    o.on = true;
+    if (!take(Z, o.z2, o.zs1, o.zs2, 1) || !take(R, o.r2, o.rs1, o.rs2, 1) || !take(C, o.c2, o.cs1, o.cs2, 16)) {
+        return false;
+    }
+    while (i < r && view[i] == 1) {
+        ++i;
+    }
+    if (i != r || o.c2 % 16 != 0) {
+        return false;
+    }
+    *m = o;
+    return true;
+}
+
+// Z, R, C of a MatMul as the contraction kernel runs it: a B without batch
+// (rank 2, or leading dimensions of 1) folds every leading dimension of A
+// into the rows, else the batch is z.
+void matmul_zrc(const std::vector<int64_t>& out, const std::vector<int64_t>& b, int64_t& Z, int64_t& R, int64_t& C) {
+    C = out.back();
+    Z = 1;
+    R = 1;
+    const size_t r = out.size();
+    int64_t b_count = 1;
+    for (size_t i = 0; i + 2 < b.size(); ++i) {
+        b_count *= b[i];
+    }
+    if (b_count == 1) {
+        for (size_t i = 0; i + 1 < r; ++i) {
+            R *= out[i];
+        }
+    } else {
+        for (size_t i = 0; i + 2 < r; ++i) {
+            Z *= out[i];
+        }
+        R = r >= 2 ? out[r - 2] : 1;
+    }
+}
 
 bool is_alias_op(const std::string& op) {
     return op == "Flatten" || op == "Reshape" || op == "Squeeze" || op == "Unsqueeze" || op == "Identity";
@@ -222,6 +315,41 @@ std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInf
                         e.pos = m;
                         e.group += 2;
                         cur = mul.outputs[0];
+                    }
+                }
+            }
+            if (mm && e.residual.empty()) {
+                // a head split / merge: MatMul -> [Reshape ->] Transpose,
+                // written straight into the transposed layout
+                const int r0 = single(cur);
+                int rs = -1, tr = r0;
+                std::vector<int64_t> view = shapes.at(cur).dims;
+                if (r0 >= 0 && g.nodes[r0].op == "Reshape") {
+                    rs = r0;
+                    view = shapes.at(g.nodes[r0].outputs[0]).dims;
+                    tr = single(g.nodes[r0].outputs[0]);
+                }
+                if (tr >= 0 && g.nodes[tr].op == "Transpose") {
+                    std::vector<int64_t> perm = g.nodes[tr].getints("perm");
+                    if (perm.empty()) {
+                        for (int64_t a = static_cast<int64_t>(view.size()) - 1; a >= 0; --a) {
+                            perm.push_back(a);
+                        }
+                    }
+                    int64_t Z = 1, R = 1, C = 1;
+                    matmul_zrc(shapes.at(cur).dims, shapes.at(n.inputs[1]).dims, Z, R, C);
+                    OutMap om;
+                    if (make_out_map(view, perm, Z, R, C, &om)) {
+                        e.view = view;
+                        e.perm = perm;
+                        if (rs >= 0) {
+                            absorbed[rs] = true;
+                            e.group++;
+                        }
+                        absorbed[tr] = true;
+                        e.group++;
+                        e.pos = tr;
+                        cur = g.nodes[tr].outputs[0];
                     }
                 }
             }
@@ -816,6 +944,13 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 if (!e.residual.empty()) {
                     ep.res = F(e.residual);
                 }
+                if (!e.perm.empty()) {
+                    int64_t Z = 1, R = 1, C = 1;
+                    matmul_zrc(yd, bd, Z, R, C);
+                    if (Z != gg.batch || R != gg.M || C != gg.N || !make_out_map(e.view, e.perm, Z, R, C, &gg.omap)) {
+                        throw LoadError(n.where() + ": transposed output does not match the contraction");
+                    }
+                }
             }
             ep.act = e.act;
             ep.act_a = e.act_a;
@@ -1148,7 +1283,11 @@ std::string analyze_json(const uint8_t* onnx, size_t size, const std::map<std::s
         o += (i ? "," : "") + std::string("{\"op\":") + jstr(e.op) + ",\"name\":" + jstr(e.node->name) +
              ",\"act\":" + std::to_string(e.act) + ",\"group\":" + std::to_string(e.group) +
              ",\"alias\":" + (e.alias ? "true" : "false") + ",\"residual\":" + jstr(e.residual) +
-             ",\"bias\":" + jstr(e.bias) + ",\"ins\":[";
+             ",\"bias\":" + jstr(e.bias) + ",\"perm\":[";
+        for (size_t j = 0; j < e.perm.size(); ++j) {
+            o += (j ? "," : "") + std::to_string(e.perm[j]);
+        }
+        o += "],\"ins\":[";
         for (size_t j = 0; j < e.ins.size(); ++j) {
             o += (j ? "," : "") + jstr(e.ins[j]);
         }

@@ -74,6 +74,12 @@ struct Args {
     int64_t out_zstride, out_img_stride, ldc;
     int conv_out;
     int vec_out; // rows are 16-byte aligned and contiguous in n (and so are bias / res)
+    // permuted output (OutMap): offsets from (z, row, col) by two-level
+    // mixed radices; the epilogue then takes path 0 (lanes over rows) or,
+    // when cs2 == 1, path 1 (16 contiguous columns per chunk)
+    int omap;
+    int oz2, or2, oc2;
+    int64_t ozs1, ozs2, ors1, ors2, ocs1, ocs2;
     const float* bias;
     int bias_zstride;
     float bias_scale;
@@ -621,7 +627,12 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 const bool row_ok = row < p.M;
                 int64_t row_off;
                 int64_t col_stride;
-                if (path == 0) {
+                if (p.omap) {
+                    const int rr = row_ok ? row : 0;
+                    row_off = (int64_t)(z / p.oz2) * p.ozs1 + (int64_t)(z % p.oz2) * p.ozs2 +
+                              (int64_t)(rr / p.or2) * p.ors1 + (int64_t)(rr % p.or2) * p.ors2;
+                    col_stride = p.ocs2; // within one column block (oc2 % 16 == 0)
+                } else if (path == 0) {
                     const int mm = row_ok ? row : 0;
                     const int n_img = mm / (int)p.OHW;
                     const int pix = mm - n_img * (int)p.OHW;
@@ -739,7 +750,8 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     } else if (path == 1) {
                         // 16-byte rows: four vector stores per thread
                         if (row_ok && n0 + cc + 16 <= p.N) {
-                            const int64_t o = row_off + n0 + cc;
+                            const int c0 = n0 + cc;
+                            const int64_t o = row_off + (p.omap ? (int64_t)(c0 / p.oc2) * p.ocs1 + (c0 % p.oc2) : c0);
 #pragma unroll
                             for (int j = 0; j < 16; j += 4) {
                                 float4 bb = make_float4(0.f, 0.f, 0.f, 0.f), rv = bb;
@@ -759,26 +771,32 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                         } else if (row_ok) {
                             for (int j = 0; j < 16 && n0 + cc + j < p.N; ++j) {
                                 const int n = n0 + cc + j;
+                                const int64_t o = row_off + (p.omap ? (int64_t)(n / p.oc2) * p.ocs1 + (n % p.oc2) : n);
                                 const float bb = bias ? __ldg(bias + n) : 0.0f;
-                                const float rv = res ? __ldg(res + row_off + n) : 0.0f;
-                                out[row_off + n] = act_of<ACT>(fmaf(rsc, rv, fmaf(alpha, v[j], bsc * bb)), p);
+                                const float rv = res ? __ldg(res + o) : 0.0f;
+                                out[o] = act_of<ACT>(fmaf(rsc, rv, fmaf(alpha, v[j], bsc * bb)), p);
                             }
                         }
                     } else {
                         // NCHW: a lane's row is a pixel, so each store covers 32
                         // consecutive pixels of one channel
+                        // (a permuted output: the chunk lies in one column
+                        // block, whose columns are col_stride apart)
+                        const int c0 = n0 + cc;
+                        const int64_t cb = row_off + (p.omap ? (int64_t)(c0 / p.oc2) * p.ocs1 + (int64_t)(c0 % p.oc2) * p.ocs2
+                                                              : (int64_t)c0 * col_stride);
                         float rv[16];
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            const int n = n0 + cc + j;
-                            rv[j] = (res && row_ok && n < p.N) ? __ldg(res + row_off + (int64_t)n * col_stride) : 0.0f;
+                            const int n = c0 + j;
+                            rv[j] = (res && row_ok && n < p.N) ? __ldg(res + cb + (int64_t)j * col_stride) : 0.0f;
                         }
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            const int n = n0 + cc + j;
+                            const int n = c0 + j;
                             if (row_ok && n < p.N) {
                                 const float bb = bias ? __ldg(bias + n) : 0.0f;
-                                out[row_off + (int64_t)n * col_stride] =
+                                out[cb + (int64_t)j * col_stride] =
                                     act_of<ACT>(fmaf(rsc, rv[j], fmaf(alpha, v[j], bsc * bb)), p);
                             }
                         }
@@ -1147,6 +1165,15 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
                  (a.res == nullptr || al16(a.res)) && (a.bias == nullptr || (al16(a.bias) && a.bias_zstride % 4 == 0)))
                     ? 1
                     : 0;
+    if (a.omap) {
+        // 16 contiguous columns per chunk when the block stride is 1 and
+        // every offset keeps 16-byte alignment; else lanes over rows
+        const bool v = a.ocs2 == 1 && a.oc2 % 16 == 0 && a.N % 16 == 0 && a.ozs1 % 4 == 0 && a.ozs2 % 4 == 0 &&
+                       a.ors1 % 4 == 0 && a.ors2 % 4 == 0 && a.ocs1 % 4 == 0 && al16(a.out) &&
+                       (a.bias == nullptr || al16(a.bias));
+        a.vec_out = v ? 1 : 0;
+        a.conv_out = v ? 0 : 1;
+    }
     a.ktab_smem = ((a.mode == kAConvGeneric && kpad * 8 <= 16384) || a.mode == kAConvCvec) ? 1 : 0;
     if (a.mode == kAConvCvec && kpad * 8 > 16384) {
         fail(kStatusUnsupported, "Conv: filter too large for the narrow-channel input path");
@@ -1169,7 +1196,7 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     a.kper = a.nkb;
     a.part = nullptr;
     int kper = a.nkb;
-    const int ks = split_k_slices(dev, tiles, a.nkb, &kper);
+    const int ks = a.omap ? 1 : split_k_slices(dev, tiles, a.nkb, &kper); // the reduce writes row-major
     if (ks > 1) {
         const size_t bytes = static_cast<size_t>(ks) * static_cast<size_t>(z) * a.M * n_per_z * sizeof(float);
         float* part = static_cast<float*>(dev->split_scratch(bytes));
@@ -1371,6 +1398,21 @@ void gemm_run(nb2_device* dev, const GemmGeom& g, const float* a_ptr, const void
     a.ldc = g.ldc;
     a.conv_out = 0;
     a.bias_zstride = 0;
+    if (g.omap.on) {
+        if (g.omap.c2 % 16 != 0 || g.omap.z2 < 1 || g.omap.r2 < 1 || ep.res != nullptr) {
+            fail(kStatusUnsupported, "Gemm: permuted output needs column blocks of 16k and no residual");
+        }
+        a.omap = 1;
+        a.oz2 = static_cast<int>(g.omap.z2);
+        a.or2 = static_cast<int>(g.omap.r2);
+        a.oc2 = static_cast<int>(g.omap.c2);
+        a.ozs1 = g.omap.zs1;
+        a.ozs2 = g.omap.zs2;
+        a.ors1 = g.omap.rs1;
+        a.ors2 = g.omap.rs2;
+        a.ocs1 = g.omap.cs1;
+        a.ocs2 = g.omap.cs2;
+    }
     fill_epilogue(a, ep);
     launch(dev, a, g.N, g.batch, static_cast<const float*>(packed_b), g.batch * g.N);
 }

@@ -85,12 +85,26 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
 
 // Dense GEMM: Y[M,N] = op(A)[M,K] * op(B)[K,N]; lda/ldb are the row strides of
 // A and B as stored. B is packed per call into `packed` (see gemm_packed_bytes).
+// Output placement of a contraction written straight into a permuted
+// layout (e.g. a linear layer's [B*T, H*D] result stored as [B, H, T, D]):
+// element (z, row, col) goes to
+//   (z / z2) * zs1 + (z % z2) * zs2 + (row / r2) * rs1 + (row % r2) * rs2
+//   + (col / c2) * cs1 + (col % c2) * cs2,
+// with c2 % 16 == 0. Off (on = false) for plain row-major output.
+struct OutMap {
+    bool on = false;
+    int64_t z2 = 1, zs1 = 0, zs2 = 0;
+    int64_t r2 = 1, rs1 = 0, rs2 = 0;
+    int64_t c2 = 1, cs1 = 0, cs2 = 0;
+};
+
 struct GemmGeom {
     int64_t M, N, K;
     int trans_a, trans_b;
     int64_t lda, ldb, ldc;
     int64_t batch = 1;                  // batched MatMul: z slices
     int64_t a_zstride = 0, b_zstride = 0, c_zstride = 0;
+    OutMap omap;                        // permuted output (no residual, no split K)
 };
 
 size_t gemm_packed_bytes(const GemmGeom& g);

@@ -160,3 +160,37 @@ def test_vit_gelu_and_scale_fusion_plan():
     assert rows["blk0.fc1"]["group"] == 7 and rows["blk0.fc1"]["act"] == 4  # bias + erf-form GELU
     assert rows["blk0.qk"]["group"] == 2  # / sqrt(64) as the epilogue scale
     assert not any(e["op"] in ("Erf", "Div") for e in a["exec"])
+
+
+def test_vit_head_transposes_written_in_place_plan():
+    """The head split (linear -> Reshape -> Transpose) and merge (MatMul ->
+    Transpose) are absorbed: the contraction writes the transposed layout
+    directly, so no Transpose row is left but the patch-embedding one."""
+    from nert_b200 import configs
+
+    g = configs.vit_b16(2, layers=2)
+    a = nbm.analyze(g, {"input": [2, 3, 224, 224]})
+    rows = {e["name"]: e for e in a["exec"]}
+    for b in ("blk0", "blk1"):
+        assert rows[f"{b}.q"]["group"] == 4 and rows[f"{b}.q"]["perm"] == [0, 2, 1, 3]
+        assert rows[f"{b}.k"]["group"] == 4 and rows[f"{b}.k"]["perm"] == [0, 2, 3, 1]
+        assert rows[f"{b}.v"]["group"] == 4 and rows[f"{b}.v"]["perm"] == [0, 2, 1, 3]
+        assert rows[f"{b}.av"]["group"] == 2 and rows[f"{b}.av"]["perm"] == [0, 2, 1, 3]
+    assert [e["name"] for e in a["exec"] if e["op"] == "Transpose"] == ["patch.tokens"]
+
+
+def test_transpose_after_matmul_kept_when_not_a_head_split():
+    """A Transpose whose permutation mixes a row axis into the columns in a
+    way the output map cannot express stays a separate row."""
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    g = Graph(opset=13)
+    x = g.add_input("x", [6, 10, 24])
+    y = g.op("MatMul", [x, g.const("w", synth.normal((24, 20), 0.1, 5))], name="mm")
+    t = g.op("Transpose", [g.op("Reshape", [y, g.const("s", np.array([60, 4, 5], np.int64))], name="rs")],
+             name="tr", perm=[2, 0, 1])
+    g.add_output(t, None, FLOAT)
+    a = nbm.analyze(g, {"x": [6, 10, 24]})
+    # columns 20 = 4 x 5: inner block 5 is not a multiple of 16, so no map
+    assert any(e["op"] == "Transpose" for e in a["exec"])

@@ -147,3 +147,57 @@ def test_split_k_epilogue_matches_oracle(cuda):
     assert rel_err(out, ref) <= TOL
     np.testing.assert_array_equal(out, again)  # the reduction order is fixed
     assert launches == 2  # contraction + split-K reduce
+
+
+def _heads_graph(b, t, heads, d, long_k):
+    """Attention block with the head split / merge as Reshape + Transpose:
+    linear -> [B, T, H, D] -> Transpose to [B, H, T, D] (and [B, H, D, T] for
+    K), attention, Transpose back, Reshape, output linear. long_k makes the
+    output linear's K long enough to split (its input is the merged heads)."""
+    dm = heads * d
+    g = Graph(opset=13)
+    x = g.add_input("x", [b, t, dm])
+
+    def w(name, shape):
+        return g.const(name, synth.normal(shape, 1.0 / np.sqrt(shape[0]), synth.seed_of("heads", name)))
+
+    split = g.const("split", np.array([b, t, heads, d], np.int64))
+    merge = g.const("merge", np.array([b, t, dm], np.int64))
+
+    def proj(name, perm):
+        y = g.op("Add", [g.op("MatMul", [x, w(name + ".w", (dm, dm))], name=name), w(name + ".b", (dm,))],
+                 name=name + ".bias")
+        return g.op("Transpose", [g.op("Reshape", [y, split], name=name + ".r")], name=name + ".t", perm=perm)
+
+    q = proj("q", [0, 2, 1, 3])
+    k = proj("k", [0, 2, 3, 1])
+    v = proj("v", [0, 2, 1, 3])
+    s = g.op("Div", [g.op("MatMul", [q, k], name="qk"), g.const("scale", np.array(np.sqrt(d), np.float32))],
+             name="scaled")
+    a = g.op("Softmax", [s], name="sm", axis=-1)
+    c = g.op("Transpose", [g.op("MatMul", [a, v], name="av")], name="ctx.t", perm=[0, 2, 1, 3])
+    c = g.op("Reshape", [c, merge], name="ctx")
+    g.add_output(g.op("MatMul", [c, w("o.w", (dm, 64 if long_k else dm))], name="o"), None, FLOAT)
+    return g, {"x": synth.normal((b, t, dm), 1.0, synth.seed_of("heads", "x"))}
+
+
+@pytest.mark.parametrize("shape", [(3, 13, 3, 32, False), (2, 197, 12, 64, False), (1, 50, 4, 128, True)],
+                         ids=["t13_h3_d32", "vit_heads", "d128_long_k"])
+def test_head_transposes_written_in_place(cuda, shape):
+    """The projections write [B, H, T, D] / [B, H, D, T] and the attention
+    output writes [B, T, H, D] directly (no Transpose rows); results match
+    the oracle and the unfused graph."""
+    from nert_b200.model import Model, analyze
+
+    g, ins = _heads_graph(*shape)
+    plan = analyze(g, {k: list(v.shape) for k, v in ins.items()})
+    assert [e["name"] for e in plan["exec"] if e["op"] == "Transpose"] == []
+    ref = np_ref.run(g, ins)
+    name = g.outputs[0][0]
+    for fuse in (True, False):
+        m = Model(g, {k: list(v.shape) for k, v in ins.items()}, fuse=fuse)
+        try:
+            out = m.run(ins)[name]
+        finally:
+            m.close()
+        assert rel_err(out, ref[name]) <= TOL, fuse
