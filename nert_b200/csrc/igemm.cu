@@ -77,6 +77,10 @@ struct Args {
     // permuted output (OutMap): offsets from (z, row, col) by two-level
     // mixed radices; the epilogue then takes path 0 (lanes over rows) or,
     // when cs2 == 1, path 1 (16 contiguous columns per chunk)
+    // 128-wide tiles with several tiles per CTA: two tiles in flight with
+    // one accumulator each, the MMA issuers taking alternate tiles (the
+    // epilogue of one tile overlaps the next tile's main loop)
+    int alt;
     int omap;
     int oz2, or2, oc2;
     int64_t ozs1, ozs2, ors1, ors2, ocs1, ocs2;
@@ -374,7 +378,16 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
     uint64_t* acc_full = t_full + ST;  // [2]
     uint64_t* acc_empty = acc_full + 2; // [2]
     uint64_t* mma_done = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    // alternate tiles: the issuer of tile i arrives once it has seen its
+    // last K block ready; the issuer of tile i + 1 waits for that before
+    // its first, so each waits on every A stage's phases in order
+    uint64_t* mma_turn = mma_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_turn + 1);
+    // accumulator buffers: BN = 64: kAccBufs x (even, odd); BN = 128: one
+    // tile x (even, odd), or (alt) two tiles x one
+    const bool alt = BN == 128 && p.alt != 0;
+    const int nbuf = alt ? 2 : C::kAccBufs;
+    auto acc_col = [&](int b) { return static_cast<uint32_t>(alt ? b * BN : b * C::kAccs * BN); };
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     // the raw A ring (S x 16 KB, TMA_A modes), then the B ring (S x [B hi][B lo])
@@ -401,10 +414,11 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             mbar_init(&t_full[t], C::kGroupWarps);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 2); // both MMA issuers commit
+            mbar_init(&acc_full[b], alt ? 1 : 2); // the issuers that feed a tile commit
             mbar_init(&acc_empty[b], C::kEpiWarps);
         }
         mbar_init(mma_done, 2);
+        mbar_init(mma_turn, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -618,8 +632,8 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
                 int z, m0, n0;
                 decode(t, z, m0, n0);
-                const int b = i % C::kAccBufs;
-                if (!warp_wait(&acc_full[b], (i / C::kAccBufs) & 1, abort_flag, p.err)) {
+                const int b = i % nbuf;
+                if (!warp_wait(&acc_full[b], (i / nbuf) & 1, abort_flag, p.err)) {
                     break;
                 }
                 tc_fence_after();
@@ -646,11 +660,10 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 const float* __restrict__ res = p.res;
                 float* __restrict__ out = p.out;
                 const float alpha = p.alpha, bsc = p.bias_scale, rsc = p.res_scale;
-                const uint32_t acc0 = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                      static_cast<uint32_t>(b * C::kAccs * BN);
+                const uint32_t acc0 = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc_col(b);
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
-                const bool two = kcnt > 1; // odd-block accumulator in use
+                const bool two = !alt && kcnt > 1; // odd-block accumulator in use
                 if (p.ksplit > 1) {
                     // raw partial sums of this K slice, row-major [M][N]
                     float* prow = p.part + ((int64_t)(kb0 / p.kper) * p.zcount + z) * p.M * p.N + (int64_t)row * p.N;
@@ -897,14 +910,19 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++i) {
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
-                const int b = i % C::kAccBufs;
-                if (!mbar_wait(&acc_empty[b], ((i / C::kAccBufs) & 1) ^ 1, abort_flag, p.err)) {
+                if (alt && (i & 1) != par) {
+                    g += static_cast<uint32_t>(kcnt); // the other issuer's tile
+                    continue;
+                }
+                const int b = i % nbuf;
+                if (!mbar_wait(&acc_empty[b], ((i / nbuf) & 1) ^ 1, abort_flag, p.err) ||
+                    (alt && i > 0 && !mbar_wait(mma_turn, (i - 1) & 1, abort_flag, p.err))) {
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d0 = tmem + static_cast<uint32_t>(b * C::kAccs * BN);
+                const uint32_t d0 = tmem + acc_col(b);
                 for (int j = 0; j < kcnt; ++j, ++g) { // j = K block within the slice
-                    if ((j & 1) != par) {
+                    if (!alt && (j & 1) != par) {
                         continue; // the other issuer's K block
                     }
                     const int s = static_cast<int>(g % S); // smem B stage == TMEM A stage
@@ -915,13 +933,16 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                         alive = false;
                         break;
                     }
+                    if (alt && j == kcnt - 1) {
+                        mbar_arrive(mma_turn); // the next tile's issuer may start waiting
+                    }
                     tc_fence_after();
-                    const uint32_t d = d0 + static_cast<uint32_t>((j & 1) * BN);
+                    const uint32_t d = d0 + static_cast<uint32_t>(alt ? 0 : (j & 1) * BN);
                     const uint32_t at = tmem + C::kAccCols + static_cast<uint32_t>(s * C::kAStageCols);
                     // a K step of 8 tf32 is 32 bytes: +2 in the descriptor's address field
                     const uint64_t bdh0 = sdesc_k128(smem_u32(b_hi(s))), bdl0 = sdesc_k128(smem_u32(b_lo(s)));
                     // the first K block into an accumulator overwrites it
-                    const uint32_t first = j < 2 ? 0u : 1u;
+                    const uint32_t first = (alt ? j == 0 : j < 2) ? 0u : 1u;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t acc = kk == 0 ? first : 1u;
@@ -1208,6 +1229,10 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     }
     // persistent: one CTA per SM (shared memory admits exactly one)
     const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles * a.ksplit, dev->num_sms)), 1, 1);
+    // two 128-wide tiles in flight once every CTA has several (with one or
+    // two per CTA the single issuer's gaps between K blocks cost more than
+    // the epilogue overlap saves)
+    a.alt = (bn == 128 && a.ksplit == 1 && tiles >= 4 * static_cast<int64_t>(grid.x)) ? 1 : 0;
     const bool three = dev->precision == kPrec3xTF32;
     if (bn == 64) {
         three ? launch_bn<64, true>(dev, a, grid, hi, lo, am) : launch_bn<64, false>(dev, a, grid, hi, lo, am);
