@@ -187,6 +187,21 @@ __global__ void gather_kernel(const T* __restrict__ x, const int64_t* __restrict
     }
 }
 
+// Nearest resize of the last two axes only (every leading axis copied
+// through): y[o][oh][ow] = x[o][lh[oh]][lw[ow]], 32-bit indices, one
+// coalesced store per thread (YOLO's x2 up-sampling).
+template <typename T>
+__global__ void resize_nearest2_kernel(const T* __restrict__ x, T* __restrict__ y, const int64_t* __restrict__ lh,
+                                       const int64_t* __restrict__ lw, uint32_t H, uint32_t W, uint32_t OH,
+                                       uint32_t OW, uint32_t n) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const uint32_t ow = i % OW;
+        const uint32_t t = i / OW;
+        const uint32_t oh = t % OH, o = t / OH;
+        y[i] = x[((size_t)o * H + static_cast<uint32_t>(__ldg(lh + oh))) * W + static_cast<uint32_t>(__ldg(lw + ow))];
+    }
+}
+
 struct ResizeDev {
     int rank;
     int64_t in_dims[8], out_dims[8], in_strides[8], axis_off[8];
@@ -633,7 +648,32 @@ void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, cons
         return;
     }
     const unsigned g = blocks_for(dev, n);
-    if (is_f32) {
+    // nearest, leading axes unchanged: the two-axis gather kernel
+    bool near2 = t.rank >= 2 && n < (int64_t(1) << 31) && st < (int64_t(1) << 31);
+    for (double w : t.weight) {
+        near2 = near2 && w == 0.0;
+    }
+    for (int d = 0; near2 && d + 2 < t.rank; ++d) {
+        near2 = t.in_dims[d] == t.out_dims[d];
+        for (int64_t i = 0; near2 && i < t.out_dims[d]; ++i) {
+            near2 = t.lower[t.axis_off[d] + i] == i;
+        }
+    }
+    if (near2) {
+        const int a = t.rank - 2, b = t.rank - 1;
+        const auto H = static_cast<uint32_t>(t.in_dims[a]), W = static_cast<uint32_t>(t.in_dims[b]);
+        const auto OH = static_cast<uint32_t>(t.out_dims[a]), OW = static_cast<uint32_t>(t.out_dims[b]);
+        const int64_t* lh = r.lower + t.axis_off[a];
+        const int64_t* lw = r.lower + t.axis_off[b];
+        if (is_f32) {
+            resize_nearest2_kernel<float><<<g, 256, 0, dev->stream>>>(
+                static_cast<const float*>(x), static_cast<float*>(y), lh, lw, H, W, OH, OW, static_cast<uint32_t>(n));
+        } else {
+            resize_nearest2_kernel<long long><<<g, 256, 0, dev->stream>>>(static_cast<const long long*>(x),
+                                                                          static_cast<long long*>(y), lh, lw, H, W,
+                                                                          OH, OW, static_cast<uint32_t>(n));
+        }
+    } else if (is_f32) {
         resize_kernel<float><<<g, 256, 0, dev->stream>>>(static_cast<const float*>(x), static_cast<float*>(y), r, n);
     } else {
         resize_kernel<long long><<<g, 256, 0, dev->stream>>>(static_cast<const long long*>(x),

@@ -88,6 +88,14 @@ ROW_CASES = [
     ("gap_r50", "GlobalAveragePool", [(4, 2048, 7, 7)], {}, {}),
     ("resize_up", "Resize", [(2, 256, 20, 20), (0,), (4,)], {"mode": "nearest"},
      {1: np.zeros((0,), np.float32), 2: np.array([1, 1, 2, 2], np.float32)}),
+    # nearest on the last two axes (two-axis gather path): fractional scales,
+    # odd sizes, rank 3; a resized leading axis takes the general kernel
+    ("resize_near_frac", "Resize", [(2, 5, 17, 23), (0,), (4,)], {"mode": "nearest"},
+     {1: np.zeros((0,), np.float32), 2: np.array([1, 1, 1.5, 0.75], np.float32)}),
+    ("resize_near_rank3", "Resize", [(6, 9, 11), (0,), (3,)], {"mode": "nearest"},
+     {1: np.zeros((0,), np.float32), 2: np.array([1, 3, 2], np.float32)}),
+    ("resize_near_lead", "Resize", [(2, 3, 8, 8), (0,), (4,)], {"mode": "nearest"},
+     {1: np.zeros((0,), np.float32), 2: np.array([1, 2, 2, 2], np.float32)}),
     ("resize_linear", "Resize", [(1, 3, 17, 23), (0,), (4,)], {"mode": "linear"},
      {1: np.zeros((0,), np.float32), 2: np.array([1, 1, 1.5, 2.25], np.float32)}),
     ("slice_step", "Slice", [(4, 30, 40), (2,), (2,), (2,), (2,)], {},
