@@ -48,6 +48,39 @@ __global__ void maxpool2d_kernel(const float* __restrict__ x, float* __restrict_
     }
 }
 
+// NCHW max pool over a fixed KH x KW window without dilation (YOLO's SPPF
+// 5x5/1): 32-bit indices, all taps' loads issued together (an out-of-image
+// tap reads as -inf, which never wins the comparison the generic kernel
+// makes); neighbouring threads share their windows through L1.
+template <int KH, int KW>
+__global__ void maxpool2d_fixed_kernel(const float* __restrict__ x, float* __restrict__ y, int H, int W, int OH,
+                                       int OW, int sh, int sw, int ph, int pw, uint32_t total) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int ow = static_cast<int>(i % OW);
+        const uint32_t t = i / OW;
+        const int oh = static_cast<int>(t % OH);
+        const float* plane = x + (size_t)(t / OH) * H * W;
+        const int h0 = oh * sh - ph, w0 = ow * sw - pw;
+        float v[KH * KW];
+#pragma unroll
+        for (int kh = 0; kh < KH; ++kh) {
+#pragma unroll
+            for (int kw = 0; kw < KW; ++kw) {
+                const int ih = h0 + kh, iw = w0 + kw;
+                v[kh * KW + kw] = ((unsigned)ih < (unsigned)H && (unsigned)iw < (unsigned)W)
+                                      ? __ldg(plane + ih * W + iw)
+                                      : -INFINITY;
+            }
+        }
+        float best = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < KH * KW; ++k) {
+            best = v[k] > best ? v[k] : best;
+        }
+        y[i] = best;
+    }
+}
+
 // Warp per row, double accumulation, for short rows (e.g. 7x7 = 49).
 __global__ void row_mean_warp_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows, int64_t inner) {
     const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -295,7 +328,22 @@ void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {
         return;
     }
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
-    maxpool2d_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
+    const bool small = total < (int64_t(1) << 31) && g.N * g.C * g.H * g.W < (int64_t(1) << 31);
+    const bool plain = small && g.dh == 1 && g.dw == 1;
+    const auto nb = static_cast<unsigned>(blocks);
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W), OH = static_cast<int>(g.OH),
+              OW = static_cast<int>(g.OW), sh = static_cast<int>(g.sh), sw = static_cast<int>(g.sw),
+              ph = static_cast<int>(g.ph), pw = static_cast<int>(g.pw);
+    const auto tot = static_cast<uint32_t>(total);
+    if (plain && g.KH == 5 && g.KW == 5) {
+        maxpool2d_fixed_kernel<5, 5><<<nb, 256, 0, dev->stream>>>(x, y, H, W, OH, OW, sh, sw, ph, pw, tot);
+    } else if (plain && g.KH == 3 && g.KW == 3) {
+        maxpool2d_fixed_kernel<3, 3><<<nb, 256, 0, dev->stream>>>(x, y, H, W, OH, OW, sh, sw, ph, pw, tot);
+    } else if (plain && g.KH == 2 && g.KW == 2) {
+        maxpool2d_fixed_kernel<2, 2><<<nb, 256, 0, dev->stream>>>(x, y, H, W, OH, OW, sh, sw, ph, pw, tot);
+    } else {
+        maxpool2d_kernel<<<nb, 256, 0, dev->stream>>>(x, y, g, total);
+    }
     check_cuda(cudaGetLastError(), "maxpool launch");
 }
 

@@ -83,6 +83,9 @@ ROW_CASES = [
     ("concat_c", "Concat", [(2, 16, 80, 80), (2, 16, 80, 80), (2, 32, 80, 80)], {"axis": 1}, {}),
     ("concat_last", "Concat", [(2, 144, 6400), (2, 144, 1600), (2, 144, 400)], {"axis": 2}, {}),
     ("maxpool_sppf", "MaxPool", [(2, 128, 20, 20)], {"kernel_shape": [5, 5], "strides": [1, 1], "pads": [2] * 4}, {}),
+    ("maxpool_2x2", "MaxPool", [(3, 5, 17, 21)], {"kernel_shape": [2, 2], "strides": [2, 2]}, {}),
+    ("maxpool_dil", "MaxPool", [(2, 4, 13, 14)],
+     {"kernel_shape": [3, 3], "strides": [1, 1], "pads": [2, 2, 2, 2], "dilations": [2, 2]}, {}),
     ("maxpool_ceil", "MaxPool", [(2, 8, 15, 15)],
      {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [0, 0, 1, 1], "ceil_mode": 1}, {}),
     ("gap_r50", "GlobalAveragePool", [(4, 2048, 7, 7)], {}, {}),
