@@ -270,15 +270,28 @@ __global__ void __launch_bounds__(512) topk_hist_kernel(const float* __restrict_
     const float* r = x + row * L;
     const int64_t begin = static_cast<int64_t>(blockIdx.x) * kChunk;
     const int64_t end = min(begin + kChunk, L);
-    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
-        const uint32_t key = key_of(__ldg(r + i));
-        if ((key & mask) == prefix) {
-            const uint32_t bin = (key >> sh) & dm;
-            // warp-aggregated increment: one atomic per distinct bin in the warp
-            const unsigned active = __activemask();
-            const unsigned peers = __match_any_sync(active, bin);
-            if ((__ffs(peers) - 1) == static_cast<int>(threadIdx.x & 31)) {
-                atomicAdd(&h[bin], static_cast<uint32_t>(__popc(peers)));
+    // four loads in flight per thread (coalesced across the block), then
+    // their histogram updates
+    const int64_t step = blockDim.x;
+    for (int64_t i0 = begin + threadIdx.x; i0 < end; i0 += 4 * step) {
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u * step;
+            v[u] = i < end ? __ldg(r + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool in = i0 + u * step < end;
+            const uint32_t key = key_of(v[u]);
+            if (in && (key & mask) == prefix) {
+                const uint32_t bin = (key >> sh) & dm;
+                // warp-aggregated increment: one atomic per distinct bin in the warp
+                const unsigned active = __activemask();
+                const unsigned peers = __match_any_sync(active, bin);
+                if ((__ffs(peers) - 1) == static_cast<int>(threadIdx.x & 31)) {
+                    atomicAdd(&h[bin], static_cast<uint32_t>(__popc(peers)));
+                }
             }
         }
     }
@@ -307,8 +320,13 @@ __global__ void __launch_bounds__(512) topk_eqcount_kernel(const float* __restri
     const int64_t begin = static_cast<int64_t>(blockIdx.x) * kChunk;
     const int64_t end = min(begin + kChunk, L);
     int c = 0;
-    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
-        c += key_of(__ldg(r + i)) == T;
+    const int64_t step = blockDim.x;
+    for (int64_t i0 = begin + threadIdx.x; i0 < end; i0 += 4 * step) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u * step;
+            c += (i < end && key_of(__ldg(r + i)) == T) ? 1 : 0;
+        }
     }
     c = __reduce_add_sync(0xffffffffu, c);
     if ((threadIdx.x & 31) == 0 && c) {

@@ -169,10 +169,11 @@ def test_topk_bit_exact(cuda, rows, length, k):
         np.testing.assert_array_equal(got[name], ref[name])
 
 
-def test_topk_ties_take_smallest_index(cuda):
-    x = np.zeros((2, 4096), np.float32)
+@pytest.mark.parametrize("length", [4096, 300001], ids=["row_kernel", "split_passes"])
+def test_topk_ties_take_smallest_index(cuda, length):
+    x = np.zeros((2, length), np.float32)
     x[:, ::3] = 1.0  # many exact ties
-    g, _ = one("TopK", [(2, 4096), (1,)], {"axis": -1}, {1: np.array([100], np.int64)}, n_out=2)
+    g, _ = one("TopK", [(2, length), (1,)], {"axis": -1}, {1: np.array([100], np.int64)}, n_out=2)
     ref = np_ref.run(g, {"in0": x})
     got = run_engine(g, {"in0": x})
     for name in ref:
