@@ -1159,9 +1159,25 @@ int split_k_slices(const nb2_device* dev, int64_t tiles, int nkb, int* kper) {
     return (nkb + *kper - 1) / *kper;
 }
 
+// Tile width: 64 for narrow outputs; for short K (<= 4 blocks) 64 as well,
+// since a 64-wide tile's double-buffered accumulator lets the epilogue
+// overlap the next tile (measured 10-12% faster on 1x1 convs with K = 64,
+// 128), unless every CTA gets at least four 128-wide tiles, which then keep
+// two tiles in flight too.
+int tile_width(const nb2_device* dev, int64_t M, int64_t n_per_z, int nkb, int64_t z) {
+    if (n_per_z <= 64) {
+        return 64;
+    }
+    if (nkb > 4) {
+        return 128;
+    }
+    const int64_t t128 = ((M + 127) / 128) * ((n_per_z + 127) / 128) * z;
+    return t128 >= 4 * static_cast<int64_t>(dev->num_sms) ? 128 : 64;
+}
+
 int contraction_launches(const nb2_device* dev, int64_t M, int64_t n_per_z, int64_t K, int64_t z) {
     const int nkb = static_cast<int>((K + 31) / 32);
-    const int bn = (n_per_z <= 64 || nkb <= 4) ? 64 : 128;
+    const int bn = tile_width(dev, M, n_per_z, nkb, z);
     const int64_t tiles = ((M + 127) / 128) * ((n_per_z + bn - 1) / bn) * z;
     int kper = 0;
     return split_k_slices(dev, tiles, nkb, &kper) > 1 ? 2 : 1;
@@ -1172,10 +1188,7 @@ namespace {
 void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* packed, int64_t rows_total,
             const CUtensorMap* a_map = nullptr) {
     const int64_t kpad = static_cast<int64_t>(a.nkb) * 32;
-    // 64-wide tiles for narrow outputs, and for short K (<= 4 blocks), where a
-    // 64-wide tile's double-buffered accumulator lets the epilogue overlap
-    // the next tile (measured 10-12% faster on 1x1 convs with K = 64, 128)
-    const int bn = (n_per_z <= 64 || a.nkb <= 4) ? 64 : 128;
+    const int bn = tile_width(dev, a.M, n_per_z, a.nkb, z);
     CUtensorMap hi, lo;
     make_tmap(&hi, packed, kpad, rows_total, bn);
     make_tmap(&lo, packed + rows_total * kpad, kpad, rows_total, bn);
