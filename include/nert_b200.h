@@ -93,6 +93,21 @@ int nb2_device_set_precision(nb2_device* dev, int precision);
 int nb2_device_get_precision(const nb2_device* dev);
 /* Wait for the device's stream; NB2_ERR_DEVICE if a kernel recorded an error. */
 int nb2_device_synchronize(nb2_device* dev);
+/* Bound, in SM clock ticks, after which a tensor-core kernel's pipeline wait
+ * gives up, records a device error (NB2_ERR_DEVICE, "bounded wait expired",
+ * at the next synchronisation) and unwinds instead of hanging; cycles <= 0
+ * restores the default (about one second). No counterpart in the reference,
+ * whose CUDA rows synchronise after every launch (src/cuda/relu.cu:68). */
+int nb2_device_set_wait_bound(nb2_device* dev, int64_t cycles);
+int64_t nb2_device_get_wait_bound(const nb2_device* dev);
+/* Schedule the host chose for the most recent Conv/Gemm/MatMul launch on this
+ * device: output tile width (64 or 128), whether two tiles were kept in flight
+ * (MMA issuers on alternate tiles), the number of K slices (1 = unsplit), the
+ * A-operand mode and the number of output tiles. Any pointer may be null.
+ * Diagnostics for tests and tuning; the reference has no counterpart (cuDNN
+ * and cuBLAS pick their algorithms internally, src/cuda/conv.cu:230-530). */
+int nb2_device_last_contraction(const nb2_device* dev, int* tile_n, int* two_in_flight, int* k_slices, int* a_mode,
+                                int64_t* tiles);
 
 /* Device memory (replaces CudaAllocator, src/cuda_device.cpp:30-51):
  * 256-byte aligned, null on bytes <= 0. */
@@ -126,9 +141,11 @@ int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* 
  * reference). Same semantics and validation as nb2_conv2d, but the weight is
  * packed into a fixed 8 MiB static device array (per GPU, held until exit)
  * instead of the growable workspace, so the call performs no cudaMalloc,
- * cudaFree or other allocation: for code recording a CUDA graph, or running
- * inside a framework that owns all device memory. Weights whose packed form
- * exceeds nb2_conv2d_noalloc_capacity() bytes are rejected (NB2_ERR_INVALID).
+ * cudaFree or other allocation: for a plug-in inside a host framework that
+ * owns all device memory, or a service on a fixed memory budget. It never splits K (the
+ * split-K buffer is shared and growable), so it launches one contraction
+ * kernel whatever the layer. Weights whose packed form exceeds
+ * nb2_conv2d_noalloc_capacity() bytes are rejected (NB2_ERR_INVALID).
  * The first call on a device resolves the array's device address, so make it
  * before any stream capture. All calls share the array and leave their data
  * in it; calls whose kernels overlap on one GPU would race on it. */

@@ -44,6 +44,11 @@ _SIGS = {
     "nb2_device_set_precision": (ctypes.c_int, [vp, ctypes.c_int]),
     "nb2_device_get_precision": (ctypes.c_int, [vp]),
     "nb2_device_synchronize": (ctypes.c_int, [vp]),
+    "nb2_device_set_wait_bound": (ctypes.c_int, [vp, ctypes.c_int64]),
+    "nb2_device_get_wait_bound": (ctypes.c_int64, [vp]),
+    "nb2_device_last_contraction": (ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                                   ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                                   c_i64p]),
     "nb2_device_malloc": (ctypes.c_int, [vp, ctypes.c_int64, ctypes.POINTER(vp)]),
     "nb2_device_free": (ctypes.c_int, [vp, vp]),
     "nb2_memcpy_h2d": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64]),
@@ -106,6 +111,16 @@ def check(status: int) -> None:
 def i64s(vals) -> ctypes.Array:
     vals = [int(v) for v in vals]
     return (ctypes.c_int64 * max(1, len(vals)))(*vals)
+
+
+def last_contraction(ordinal: int = 0) -> dict:
+    """Schedule of the most recent Conv/Gemm/MatMul launch on the GPU."""
+    tn, alt, ks, mode = (ctypes.c_int() for _ in range(4))
+    tiles = ctypes.c_int64()
+    check(lib().nb2_device_last_contraction(device(ordinal), ctypes.byref(tn), ctypes.byref(alt), ctypes.byref(ks),
+                                            ctypes.byref(mode), ctypes.byref(tiles)))
+    return {"tile_n": tn.value, "two_in_flight": alt.value, "k_slices": ks.value, "a_mode": mode.value,
+            "tiles": tiles.value}
 
 
 def device(ordinal: int = 0) -> int:

@@ -5,7 +5,8 @@
   sm_100a only (``-gencode arch=compute_100a,code=sm_100a``).
 * ``nert_b200/lib/libnert_b200_device.so`` — the ``nert::Device`` plug-in
   (``device/b200_device.cpp``), compiled against the NERT public headers when
-  they are available (``NERT_INCLUDE`` or the reference checkout).
+  they are available (``NERT_INCLUDE``, else the ``include/`` of the reference
+  checkout named by ``NERT_REFERENCE`` or lying beside this repository).
 
 Objects are rebuilt only when a source or header is newer than the object.
 """
@@ -34,7 +35,8 @@ DEVICE_LIB = os.path.join(LIB_DIR, "libnert_b200_device.so")
 
 
 def nert_include() -> str | None:
-    for cand in (os.environ.get("NERT_INCLUDE"), "/root/reference/include"):
+    ref = os.environ.get("NERT_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
+    for cand in (os.environ.get("NERT_INCLUDE"), os.path.join(ref, "include")):
         if cand and os.path.exists(os.path.join(cand, "nert", "device.hpp")):
             return cand
     return None

@@ -53,12 +53,17 @@ def resnet18(batch: int = 1, config: str = "resnet18") -> Graph:
     return _resnet(batch, config, bottleneck=False, blocks=(2, 2, 2, 2))
 
 
-def resnet50(batch: int = 1, config: str = "resnet50", softmax: bool = True) -> Graph:
-    """torchvision-style ResNet-50 (Bottleneck 3/4/6/3, widths 64-2048) + Softmax."""
-    return _resnet(batch, config, bottleneck=True, blocks=(3, 4, 6, 3), softmax=softmax)
+def resnet50(batch: int = 1, config: str = "resnet50", softmax: bool = True, expose_logits: bool = False) -> Graph:
+    """torchvision-style ResNet-50 (Bottleneck 3/4/6/3, widths 64-2048) + Softmax.
+
+    With random Kaiming weights the logits spread over hundreds, so the
+    softmax is nearly one-hot; ``expose_logits`` adds the Gemm output
+    ``fc_out`` as a second graph output so parity checks see every logit."""
+    return _resnet(batch, config, bottleneck=True, blocks=(3, 4, 6, 3), softmax=softmax, expose_logits=expose_logits)
 
 
-def _resnet(batch: int, config: str, bottleneck: bool, blocks, softmax: bool = False) -> Graph:
+def _resnet(batch: int, config: str, bottleneck: bool, blocks, softmax: bool = False,
+            expose_logits: bool = False) -> Graph:
     b = _Builder(config)
     g = b.g
     x = g.add_input("input", [batch, 3, 224, 224])
@@ -92,9 +97,12 @@ def _resnet(batch: int, config: str, bottleneck: bool, blocks, softmax: bool = F
     bound = 1.0 / math.sqrt(cin)
     bfc = synth.uniform((1000,), -bound, bound, b.seed("fc.b"))
     y = g.op("Gemm", [y, g.const("fc.weight", wfc), g.const("fc.bias", bfc)], name="fc", transB=1)
+    logits = y
     if softmax:
         y = g.op("Softmax", [y], name="softmax", axis=-1)
     g.add_output(y, None, FLOAT)
+    if softmax and expose_logits:
+        g.add_output(logits, None, FLOAT)
     return g
 
 
@@ -188,7 +196,8 @@ def vit_input(batch: int, config: str = "vit_b16") -> np.ndarray:
 # TopK boundary is not a pile of near-ties.
 CLS_HEAD_SCALE = 90.0
 
-def yolov8n(batch: int = 1, config: str = "yolov8n", size: int = 640, classes: int = 80, topk: int = 300) -> Graph:
+def yolov8n(batch: int = 1, config: str = "yolov8n", size: int = 640, classes: int = 80, topk: int = 300,
+            expose_scores: bool = False) -> Graph:
     """YOLOv8n-style detector at opset 13.
 
     CSP backbone of Conv + SiLU (Sigmoid * Mul), C2f blocks built from Split /
@@ -198,7 +207,12 @@ def yolov8n(batch: int = 1, config: str = "yolov8n", size: int = 640, classes: i
     bins + 1x1 Conv with weights 0..15; boxes decoded from anchor points and
     strides; TopK k=300 over the 8400*80 sigmoid scores; Gather of the chosen
     boxes (anchor = index // 80, class = index - 80 * anchor, int64).
-    Kaiming weights; the class-head output conv is scaled so logits are O(1)."""
+    Kaiming weights; the class-head output conv is scaled so logits are O(1).
+    ``expose_scores`` adds three more graph outputs, the flattened pre-TopK
+    scores ``scores.flat_out`` [B, 8400*80], the decoded boxes ``boxes_out``
+    [B, 4, 8400] and the TopK indices ``topk_out1`` [B, k] (int64), so the
+    selection can be checked against the scores and boxes the same run
+    computed."""
     b = _Builder(config)
     g = b.g
 
@@ -309,6 +323,10 @@ def yolov8n(batch: int = 1, config: str = "yolov8n", size: int = 640, classes: i
     g.add_output(top_v, None, FLOAT)
     g.add_output(sel, None, FLOAT)
     g.add_output(class_i, None, 7)
+    if expose_scores:
+        g.add_output(flat, None, FLOAT)
+        g.add_output(boxes, None, FLOAT)
+        g.add_output(top_i, None, 7)
     return g
 
 

@@ -142,6 +142,38 @@ int nb2_device_set_precision(nb2_device* dev, int precision) {
 
 int nb2_device_get_precision(const nb2_device* dev) { return dev ? dev->precision : -1; }
 
+int nb2_device_set_wait_bound(nb2_device* dev, int64_t cycles) {
+    return guard([&] {
+        need(dev != nullptr, "null device");
+        dev->wait_bound = cycles > 0 ? static_cast<long long>(cycles) : kDefaultWaitBoundCycles;
+    });
+}
+
+int64_t nb2_device_get_wait_bound(const nb2_device* dev) { return dev ? dev->wait_bound : -1; }
+
+int nb2_device_last_contraction(const nb2_device* dev, int* tile_n, int* two_in_flight, int* k_slices, int* a_mode,
+                                int64_t* tiles) {
+    return guard([&] {
+        need(dev != nullptr, "null device");
+        const nb2_device::Schedule& s = dev->last_sched;
+        if (tile_n) {
+            *tile_n = s.tile_n;
+        }
+        if (two_in_flight) {
+            *two_in_flight = s.alt;
+        }
+        if (k_slices) {
+            *k_slices = s.ksplit;
+        }
+        if (a_mode) {
+            *a_mode = s.a_mode;
+        }
+        if (tiles) {
+            *tiles = s.tiles;
+        }
+    });
+}
+
 int nb2_device_synchronize(nb2_device* dev) {
     return guard([&] {
         bind(dev);

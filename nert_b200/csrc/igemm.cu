@@ -93,6 +93,7 @@ struct Args {
     int act;
     float act_a, act_b, act_c; // GELU (erf form) constants
     int* err;
+    long long wait_bound; // clock64 ticks before a pipeline wait gives up
 };
 
 constexpr int pow2_at_least(int v) {
@@ -309,8 +310,9 @@ __device__ __forceinline__ void gather16(const Args& p, RowState& rs, int kb, in
 }
 
 // All 32 lanes wait; the outcome is made warp-uniform.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
-    const bool ok = mbar_wait(bar, parity, abort_flag, err);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          long long bound) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, err, bound);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -490,7 +492,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             for (uint32_t g = static_cast<uint32_t>(pw >> 2); g < items; g += 2) {
                 const int s = static_cast<int>(g % S);
                 const int t = static_cast<int>(g % ST);
-                if (!warp_wait(&full_a[s], (g / S) & 1u, abort_flag, p.err)) {
+                if (!warp_wait(&full_a[s], (g / S) & 1u, abort_flag, p.err, p.wait_bound)) {
                     break;
                 }
                 const uint32_t row = smem_u32(a_raw(s)) + r * 128;
@@ -503,7 +505,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                                  : "memory");
                 }
                 // TMEM stage t == s is free once the MMA released stage s
-                if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err)) {
+                if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err, p.wait_bound)) {
                     break;
                 }
                 const uint32_t ta = tq + t * C::kAStageCols;
@@ -518,7 +520,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     mbar_arrive(&empty_a[s]);
                 }
                 // B landed too, so the MMA issuer waits on t_full alone
-                if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err)) {
+                if (!warp_wait(&full_b[s], (g / S) & 1u, abort_flag, p.err, p.wait_bound)) {
                     break;
                 }
                 publish_tmem(&t_full[t], lane);
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         const uint32_t tq = tmem + (static_cast<uint32_t>((pw & 3) * 32) << 16) + C::kAccCols + half * 16;
         auto produce = [&](const float (&v)[16]) -> bool {
             const int t = static_cast<int>(g % ST);
-            if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err)) {
+            if (!warp_wait(&empty[t], ((g / ST) & 1u) ^ 1u, abort_flag, p.err, p.wait_bound)) {
                 return false;
             }
             store16_tmem<THREE>(tq + t * C::kAStageCols, v);
@@ -633,7 +635,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 int z, m0, n0;
                 decode(t, z, m0, n0);
                 const int b = i % nbuf;
-                if (!warp_wait(&acc_full[b], (i / nbuf) & 1, abort_flag, p.err)) {
+                if (!warp_wait(&acc_full[b], (i / nbuf) & 1, abort_flag, p.err, p.wait_bound)) {
                     break;
                 }
                 tc_fence_after();
@@ -867,7 +869,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     const int s = static_cast<int>(g % S);
                     const uint32_t ph = (g / S) & 1u;
                     uint64_t* free_bar = role == 1 ? &empty_a[s] : &empty[s];
-                    if (!mbar_wait(free_bar, ph ^ 1u, abort_flag, p.err)) {
+                    if (!mbar_wait(free_bar, ph ^ 1u, abort_flag, p.err, p.wait_bound)) {
                         alive = false;
                         break;
                     }
@@ -915,8 +917,8 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     continue;
                 }
                 const int b = i % nbuf;
-                if (!mbar_wait(&acc_empty[b], ((i / nbuf) & 1) ^ 1, abort_flag, p.err) ||
-                    (alt && i > 0 && !mbar_wait(mma_turn, (i - 1) & 1, abort_flag, p.err))) {
+                if (!mbar_wait(&acc_empty[b], ((i / nbuf) & 1) ^ 1, abort_flag, p.err, p.wait_bound) ||
+                    (alt && i > 0 && !mbar_wait(mma_turn, (i - 1) & 1, abort_flag, p.err, p.wait_bound))) {
                     break;
                 }
                 tc_fence_after();
@@ -928,8 +930,8 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                     const int s = static_cast<int>(g % S); // smem B stage == TMEM A stage
                     const uint32_t ph = (g / S) & 1u;
                     // TMA-fed A: the converter publishes only after B landed
-                    if (!mbar_wait(&t_full[s], ph, abort_flag, p.err) ||
-                        (!kTmaA && !mbar_wait(&full_b[s], ph, abort_flag, p.err))) {
+                    if (!mbar_wait(&t_full[s], ph, abort_flag, p.err, p.wait_bound) ||
+                        (!kTmaA && !mbar_wait(&full_b[s], ph, abort_flag, p.err, p.wait_bound))) {
                         alive = false;
                         break;
                     }
@@ -1193,6 +1195,7 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     make_tmap(&hi, packed, kpad, rows_total, bn);
     make_tmap(&lo, packed + rows_total * kpad, kpad, rows_total, bn);
     a.err = dev->err_word;
+    a.wait_bound = dev->wait_bound;
     a.zcount = static_cast<int>(z);
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     a.vec_out = (!a.conv_out && a.ldc % 4 == 0 && a.out_zstride % 4 == 0 && al16(a.out) &&
@@ -1247,6 +1250,12 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     // gaps between K blocks cost more than the epilogue overlap saves:
     // measured 10-15% slower on 4096^3)
     a.alt = (bn == 128 && a.ksplit == 1 && a.nkb <= 32 && tiles >= 4 * static_cast<int64_t>(grid.x)) ? 1 : 0;
+    dev->last_sched.tile_n = bn;
+    dev->last_sched.alt = a.alt;
+    dev->last_sched.ksplit = a.ksplit;
+    dev->last_sched.a_mode = a.mode;
+    dev->last_sched.grid = static_cast<int>(grid.x);
+    dev->last_sched.tiles = tiles;
     const bool three = dev->precision == kPrec3xTF32;
     if (bn == 64) {
         three ? launch_bn<64, true>(dev, a, grid, hi, lo, am) : launch_bn<64, false>(dev, a, grid, hi, lo, am);

@@ -2,10 +2,9 @@
 //
 // nb2_conv2d packs (splits and reorders) the weight into the device
 // workspace, which grows with cudaMalloc on first use of a larger layer.
-// Some callers cannot allow that: code recording into a CUDA graph (cudaMalloc
-// is not capturable and synchronises the device), or a host framework that
-// owns all device memory and forbids allocation once it is running (a plug-in
-// executed from a framework's enqueue callback, a memory-budgeted service).
+// Some callers cannot allow that: a host framework that owns all device
+// memory and forbids allocation once it is running (a plug-in executed from
+// a framework's enqueue callback), or a service held to a fixed memory budget.
 // This entry point keeps its scratch in one file-scope __device__ array of a
 // fixed size instead, so a call allocates nothing; the caller still provides
 // every input and output buffer.
@@ -31,6 +30,7 @@
 #include "runtime.hpp"
 
 #include <mutex>
+#include <new>
 #include <string>
 
 namespace nb2 {
@@ -80,9 +80,9 @@ extern "C" int nb2_conv2d_noalloc(nb2_device* dev, const nb2_conv_geom* g, const
         }
         dev->make_current();
         void* scratch = scratch_address(dev);
-        // a layer that would split K uses the split workspace only if it
-        // already exists and is large enough; it never grows here, so such
-        // a layer otherwise runs unsplit (same results)
+        // no split K here: the split-K workspace is shared, growable and
+        // freed by nothing this call controls, so a layer that would split K
+        // runs unsplit (same results, one kernel)
         struct NoGrow {
             nb2_device* d;
             int prev;
@@ -99,6 +99,9 @@ extern "C" int nb2_conv2d_noalloc(nb2_device* dev, const nb2_conv_geom* g, const
     } catch (const nb2::Error& e) {
         nb2::set_last_error(e.what());
         return e.code;
+    } catch (const std::bad_alloc&) {
+        nb2::set_last_error("out of host memory");
+        return NB2_ERR_NOMEM;
     } catch (const std::exception& e) {
         nb2::set_last_error(e.what());
         return NB2_ERR_INVALID;

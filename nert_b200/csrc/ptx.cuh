@@ -16,8 +16,11 @@ enum DeviceError : int {
     kDevIndexOutOfRange = 2, // a Gather/TopK index outside the axis
 };
 
-// About one second at the B200's SM clock: every spin-wait gives up after
-// this many clock64 ticks, records kDevWaitTimeout and lets the CTA unwind.
+// About one second at the B200's SM clock. Waits on the pipeline take their
+// bound from the launch (the device's run-time setting, this value by
+// default); the drains at the end of a CTA (its own bulk copies and MMAs in
+// flight, which complete on their own) always allow this many clock64 ticks,
+// so a short run-time bound never lets a CTA exit before its copies land.
 constexpr long long kWaitBoundCycles = 2000000000LL;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -70,9 +73,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Bounded wait on `bar` for the phase with `parity`. Returns false (after
-// recording the timeout and raising the CTA's abort flag) when the bound is
-// hit or another thread of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+// recording the timeout and raising the CTA's abort flag) when `bound`
+// clock64 ticks pass or another thread of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          long long bound) {
     if (mbar_try_wait(bar, parity)) {
         return true;
     }
@@ -84,7 +88,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         if (*abort_flag) {
             return false;
         }
-        if (clock64() - start > kWaitBoundCycles) {
+        if (clock64() - start > bound) {
             *abort_flag = 1;
             atomicExch(err, kDevWaitTimeout);
             return false;

@@ -92,6 +92,8 @@ nb2_device* device(int ordinal) {
 
 } // namespace nb2
 
+nb2_device::nb2_device() : wait_bound(nb2::kDefaultWaitBoundCycles) {}
+
 void nb2_device::make_current() const { nb2::check_cuda(cudaSetDevice(ordinal), "cudaSetDevice"); }
 
 void* nb2_device::scratch(size_t bytes) {
@@ -116,20 +118,22 @@ void* nb2_device::scratch(size_t bytes) {
 
 void* nb2_device::split_scratch(size_t bytes) {
     bytes = (bytes + 255) & ~size_t(255);
+    if (no_grow) {
+        return nullptr; // a no-allocation call never depends on this shared buffer
+    }
     if (bytes <= split_ws_bytes) {
         return split_ws;
     }
-    if (capturing || no_grow) {
+    if (capturing) {
         return nullptr; // the caller then runs the contraction unsplit
     }
-    nb2::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize(split workspace grow)");
-    if (split_ws != nullptr) {
-        nb2::check_cuda(cudaFree(split_ws), "cudaFree(split workspace)");
-        split_ws = nullptr;
-        split_ws_bytes = 0;
-    }
     const size_t grow = std::max(bytes, split_ws_bytes * 2);
-    nb2::check_cuda(cudaMalloc(&split_ws, grow), "cudaMalloc(split workspace)");
+    void* fresh = nullptr;
+    nb2::check_cuda(cudaMalloc(&fresh, grow), "cudaMalloc(split workspace)");
+    if (split_ws != nullptr) {
+        retired_split.push_back(split_ws);
+    }
+    split_ws = fresh;
     split_ws_bytes = grow;
     return split_ws;
 }

@@ -17,7 +17,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_ref", "libnert_ref.so")
-REFERENCE_SRC = os.environ.get("NERT_REFERENCE_SRC", "/root/reference")
+# the reference checkout: NERT_REFERENCE, else a sibling of this repository
+REFERENCE_SRC = os.environ.get("NERT_REFERENCE",
+                               os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 _lib = None
 _NP = {0: np.float32, 1: np.int64, 2: np.bool_}

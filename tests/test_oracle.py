@@ -11,6 +11,7 @@ two oracles and the golden values agree with one another.
 import numpy as np
 import pytest
 
+from conftest import rel_err
 from golden.known_answers import CASES, CASES2
 from helpers import case2_graph, check_outputs
 from nert_b200 import configs, onnx_io, synth
@@ -128,3 +129,27 @@ def test_onnx_roundtrip():
     for k, v in g.initializers.items():
         np.testing.assert_array_equal(g2.initializers[k], v)
     assert onnx_io.to_onnx_bytes(g2) == b
+
+
+@pytest.mark.parametrize("config", ["resnet18", "resnet50", "vit_b16", "yolov8n"])
+def test_np_ref_matches_bench_config_fixtures(config):
+    """The numpy restatement reproduces the reference library's golden
+    outputs on the pinned images of each benchmarked batch."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_model_fixtures as mmf
+
+    z = np.load(os.path.join(mmf.OUT, f"{config}.npz"))
+    batch = int(z["batch"])
+    g, name, x = mmf.graph_and_input(config, batch)
+    for i in mmf.images(batch):
+        got = np_ref.run(g, {name: x[i:i + 1]})
+        for out_name in {k.rsplit("/", 1)[0] for k in z.files if "/" in k}:
+            want = z[f"{out_name}/{i}"]
+            have = mmf.subsample(config, out_name, got[out_name])
+            if want.dtype == np.int64:
+                np.testing.assert_array_equal(have, want, err_msg=f"{config} {out_name} {i}")
+            else:
+                assert rel_err(have, want) <= 1e-5, (config, out_name, i)
