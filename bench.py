@@ -16,8 +16,14 @@ timings are combined as the max over ranks.
 * e2e:    the same through Model.run_async (pinned host input -> H2D -> run ->
           D2H of every output) per step.
 * roofline: the tensor-core Conv/Gemm/MatMul kernel's algorithmic FLOP/s
-          (from an eager pass with an event between rows) against the
-          pool's measured bf16 GEMM peak / 2 (tf32) / 3 (3xTF32-effective).
+          over its time inside the timed replay (ms_per_step x its share of
+          an eager pass with an event between rows) against the pool's
+          measured bf16 GEMM peak / 2 (tf32) / 3 (3xTF32-effective).
+* bandwidth_rows: every HBM-bound row at its largest config geometry,
+          algorithmic bytes / CUDA-event time, against the measured HBM copy
+          bandwidth (1 GPU only).
+* --gpus N under torchrun: rank r runs its slice of one seeded global batch
+          (weak scaling: --batch per GPU; strong: --global-batch fixed).
 * cpu_baseline: the reference NERT CpuDevice (oracle/_ref, compiled from the
           reference sources) on the host cores, one image per process.
 
@@ -52,7 +58,11 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--workload", default="resnet18", choices=list(DEFAULT_BATCH))
-    p.add_argument("--batch", type=int, default=None)
+    p.add_argument("--batch", type=int, default=None,
+                   help="images per GPU (weak scaling: the global batch grows with the GPU count)")
+    p.add_argument("--global-batch", type=int, default=None,
+                   help="fixed global batch split over the GPUs by the library's shard plan (strong scaling)")
+    p.add_argument("--no-rows", action="store_true", help="skip the bandwidth-row table")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "1xtf32"])
     a = p.parse_args()
@@ -75,18 +85,21 @@ def metric_for(workload: str, batch: int) -> str:
             "sweep": "single-op sweep fp32 TFLOP/s per op (config 1)"}[workload]
 
 
-def build_workload(workload: str, batch: int):
-    """(graph, feeds) of one benchmark config."""
+def build_workload(workload: str, batch: int, rows: slice | None = None):
+    """(graph, feeds) of one benchmark config; with ``rows`` the graph is
+    built for that slice of a seeded batch of ``batch`` images and fed it."""
     from nert_b200 import configs
 
+    n = batch if rows is None else rows.stop - rows.start
+    sl = rows if rows is not None else slice(0, batch)
     if workload == "resnet18":
-        return configs.resnet18(batch), {"input": configs.resnet_input(batch)}
+        return configs.resnet18(n), {"input": configs.resnet_input(batch)[sl]}
     if workload == "resnet50":
-        return configs.resnet50(batch), {"input": configs.resnet_input(batch, "resnet50")}
+        return configs.resnet50(n), {"input": configs.resnet_input(batch, "resnet50")[sl]}
     if workload == "vit_b16":
-        return configs.vit_b16(batch), {"input": configs.vit_input(batch)}
+        return configs.vit_b16(n), {"input": configs.vit_input(batch)[sl]}
     if workload == "yolov8n":
-        return configs.yolov8n(batch), {"images": configs.yolo_input(batch)}
+        return configs.yolov8n(n), {"images": configs.yolo_input(batch)[sl]}
     raise ValueError(workload)
 
 
@@ -311,6 +324,139 @@ def contraction_flops(graph, analysis) -> dict:
     return out
 
 
+def hbm_peak() -> tuple[float, str]:
+    """Measured HBM copy bandwidth of this pool (MEASURED_PEAKS.json), else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "of measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "of fallback"
+
+
+def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
+    """Every HBM-bound row at the largest config geometry that uses it,
+    launched through the C ABI on the layer's stream and timed with CUDA
+    events around each launch (L2 flushed by a 256 MB write before each).
+    bytes = the row's algorithmic bytes (read once + write once)."""
+    import ctypes
+
+    import torch
+
+    from nert_b200 import _lib
+    from nert_b200._lib import i64s
+
+    L = _lib.lib()
+    dev = _lib.device(local)
+    stream = torch.cuda.ExternalStream(L.nb2_device_stream(dev), device=torch.device("cuda", local))
+    cuda = torch.device("cuda", local)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=cuda)
+    g = torch.Generator(device=cuda)
+    g.manual_seed(7)
+
+    def rnd(*shape):
+        return torch.rand(shape, device=cuda, generator=g) * 2 - 1
+
+    rows = []
+
+    def add(name, shape, nbytes, fn):
+        rows.append((name, shape, nbytes, fn))
+
+    p = lambda t: t.data_ptr()
+    # MaxPool: ResNet bs64 stem pool and YOLO b16 SPPF
+    x = rnd(64, 64, 112, 112)
+    y = torch.empty(64, 64, 56, 56, device=cuda)
+    add("MaxPool 3x3/s2 ResNet bs64", [64, 64, 112, 112], 4 * (x.numel() + y.numel()),
+        lambda x=x, y=y: L.nb2_maxpool2d(dev, p(x), i64s(x.shape), p(y), i64s(y.shape), i64s([3, 3]), i64s([2, 2]),
+                                         i64s([1, 1, 1, 1]), i64s([1, 1])))
+    x2 = rnd(16, 128, 20, 20)
+    y2 = torch.empty_like(x2)
+    add("MaxPool 5x5/s1 SPPF YOLO b16", [16, 128, 20, 20], 8 * x2.numel(),
+        lambda x=x2, y=y2: L.nb2_maxpool2d(dev, p(x), i64s(x.shape), p(y), i64s(y.shape), i64s([5, 5]),
+                                           i64s([1, 1]), i64s([2, 2, 2, 2]), i64s([1, 1])))
+    # GlobalAveragePool: ResNet-50 b32
+    x3 = rnd(32, 2048, 7, 7)
+    y3 = torch.empty(32 * 2048, device=cuda)
+    add("GlobalAveragePool ResNet-50 b32", [32, 2048, 7, 7], 4 * (x3.numel() + y3.numel()),
+        lambda x=x3, y=y3: L.nb2_row_mean(dev, p(x), 32 * 2048, 49, p(y)))
+    # Softmax: ViT attention rows, YOLO DFL bins (axis 1 of [16, 16, 33600])
+    x4 = rnd(32, 12, 197, 197)
+    y4 = torch.empty_like(x4)
+    add("Softmax ViT b32 [32,12,197,197]", list(x4.shape), 8 * x4.numel(),
+        lambda x=x4, y=y4: L.nb2_softmax(dev, p(x), p(y), 32 * 12 * 197, 197, 1))
+    x5 = rnd(16, 16, 33600)
+    y5 = torch.empty_like(x5)
+    add("Softmax DFL YOLO b16 (axis of 16)", list(x5.shape), 8 * x5.numel(),
+        lambda x=x5, y=y5: L.nb2_softmax(dev, p(x), p(y), 16, 16, 33600))
+    # LayerNormalization: ViT b32
+    x6 = rnd(32 * 197, 768)
+    y6 = torch.empty_like(x6)
+    sc, bi = rnd(768), rnd(768)
+    add("LayerNormalization ViT b32", [32, 197, 768], 8 * x6.numel() + 8 * 768,
+        lambda x=x6, y=y6, s=sc, b=bi: L.nb2_layernorm(dev, p(x), p(s), p(b), p(y), None, None, 32 * 197, 768,
+                                                         ctypes.c_float(1e-6)))
+    # TopK and the box Gather: YOLO b16
+    x7 = torch.rand(16, 672000, device=cuda, generator=g)
+    v7 = torch.empty(16, 300, device=cuda)
+    i7 = torch.empty(16, 300, dtype=torch.int64, device=cuda)
+    add("TopK k=300 YOLO b16 [16,672000]", [16, 672000], 4 * x7.numel() + 12 * 16 * 300,
+        lambda x=x7, v=v7, i=i7: L.nb2_topk(dev, p(x), p(v), p(i), 16, 672000, 300))
+    x8 = rnd(16 * 8400, 4)
+    idx8 = torch.randint(0, 16 * 8400, (16 * 300,), device=cuda, generator=g)
+    y8 = torch.empty(16 * 300, 4, device=cuda)
+    add("Gather boxes YOLO b16", [16 * 8400, 4], 8 * y8.numel() + 8 * idx8.numel(),
+        lambda x=x8, i=idx8, y=y8: L.nb2_gather(dev, p(x), p(i), p(y), 1, 16 * 8400, 4, 16 * 300, 4))
+    # Resize nearest x2: YOLO b16 PAN up-sampling
+    x9 = rnd(16, 256, 20, 20)
+    y9 = torch.empty(16, 256, 40, 40, device=cuda)
+    sc9 = (ctypes.c_double * 4)(1.0, 1.0, 2.0, 2.0)
+    add("Resize nearest x2 YOLO b16", [16, 256, 20, 20], 4 * (x9.numel() + y9.numel()),
+        lambda x=x9, y=y9: L.nb2_resize(dev, p(x), p(y), i64s(x.shape), i64s(y.shape), sc9, 4, 0, 0, 0, 0))
+    # Transpose ViT patch tokens, Concat of the YOLO head levels
+    x10 = rnd(32, 768, 196)
+    y10 = torch.empty(32, 196, 768, device=cuda)
+    add("Transpose ViT b32 [32,768,196]->[32,196,768]", [32, 768, 196], 8 * x10.numel(),
+        lambda x=x10, y=y10: L.nb2_transpose(dev, p(x), p(y), i64s(x.shape), i64s([0, 2, 1]), 3, 4))
+    parts = [rnd(16, 144, n) for n in (6400, 1600, 400)]
+    whole = torch.empty(16, 144, 8400, device=cuda)
+    c_parts = (ctypes.c_void_p * 3)(*[t.data_ptr() for t in parts])
+    add("Concat YOLO head b16 [16,144,8400]", [16, 144, 8400], 8 * whole.numel(),
+        lambda w=whole: L.nb2_concat_split(dev, 1, p(w), c_parts, i64s([6400, 1600, 400]), 3, 16 * 144, 1, 4))
+    # elementwise: residual Add, score Sigmoid
+    a11, b11 = rnd(64, 128, 28, 28), rnd(64, 128, 28, 28)
+    y11 = torch.empty_like(a11)
+    add("Add ResNet bs64 [64,128,28,28]", list(a11.shape), 12 * a11.numel(),
+        lambda a=a11, b=b11, y=y11: L.nb2_binary(dev, 0, 0, p(a), i64s(a.shape), 4, p(b), i64s(b.shape), 4, p(y),
+                                                 i64s(y.shape), 4))
+    x12 = rnd(16, 80, 8400)
+    y12 = torch.empty_like(x12)
+    add("Sigmoid YOLO b16 scores", list(x12.shape), 8 * x12.numel(),
+        lambda x=x12, y=y12: L.nb2_unary(dev, 1, p(x), p(y), x.numel()))
+
+    peak, src = hbm_peak()
+    out = []
+    torch.cuda.synchronize()
+    for name, shape, nbytes, fn in rows:
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                _lib.check(fn())
+            evs = []
+            for _ in range(reps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                _lib.check(fn())
+                e.record(stream)
+                evs.append((s, e))
+        _lib.check(L.nb2_device_synchronize(dev))
+        torch.cuda.synchronize()
+        us = 1000.0 * sum(s.elapsed_time(e) for s, e in evs) / reps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out.append({"row": name, "shape": shape, "bytes": int(nbytes), "us": round(us, 2), "gbs": round(gbs, 1),
+                    "frac": round(gbs / peak, 3), "peak_gbs": peak, "peak_note": src})
+    del flush
+    return out
+
+
 # ---- B200 leg ------------------------------------------------------------------------
 
 def run_sweep(args, local):
@@ -403,8 +549,15 @@ def main():
 
     from nert_b200 import model as nbm
 
-    batch = args.batch
-    graph, feeds = build_workload(args.workload, batch)
+    # this rank's slice of one seeded global batch, by the library's shard
+    # plan (weak scaling: batch per GPU fixed; strong: the global batch fixed)
+    from nert_b200.sharding import rank_slice
+
+    strong = args.global_batch is not None
+    global_batch = args.global_batch if strong else args.batch * world
+    my_rows = rank_slice(global_batch, rank, world)
+    batch = my_rows.stop - my_rows.start
+    graph, feeds = build_workload(args.workload, global_batch, my_rows)
     dims = {k: list(v.shape) for k, v in feeds.items()}
     m = nbm.Model(graph, dims, device=local)
     stats = m.stats()
@@ -471,11 +624,16 @@ def main():
     for _ in range(reps):
         for label, ms in m.profile():
             sums[label] = sums.get(label, 0.0) + ms / reps
-    tc_time = sum(ms for lab, ms in sums.items() if row_name(lab) in flops)
+    tc_eager = sum(ms for lab, ms in sums.items() if row_name(lab) in flops)
     tc_flop = sum(flops.values())
     total_prof = sum(sums.values())
+    # the contraction rows' share of the eager pass applied to the timed
+    # CUDA-graph replay: the kernel's time inside the step that `value` times
+    share = tc_eager / total_prof if total_prof else 0.0
+    tc_time = mean_dev * share
     achieved = tc_flop / (tc_time * 1e-3) / 1e12 if tc_time > 0 else None
     top_rows = sorted(sums.items(), key=lambda kv: -kv[1])[:5]
+    rows_table = bandwidth_rows(local) if (rank == 0 and world == 1 and not args.no_rows) else None
 
     line = None
     if rank == 0:
@@ -483,24 +641,25 @@ def main():
         peak, peak_note = tensor_peak(args.precision)
         line = {
             "metric": metric_for(args.workload, batch),
-            "value": world * batch / (mean_dev * 1e-3),
+            "value": global_batch / (mean_dev * 1e-3),
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": mean_dev,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core contractions, fp32 accumulate)" if args.precision == "3xtf32"
             else "f32 (1xTF32 contractions, opt-in)",
             "data": "synthetic (seeded inputs, Kaiming / N(0,0.02) weights, BN folded)",
             "config": {"workload": args.workload, "model": args.workload, "per_gpu_batch": batch,
-                       "global_batch": batch * world, "parallelism": f"replicas{world}",
+                       "global_batch": global_batch, "parallelism": f"batch-sharded x{world} (no collective)",
+                       "shard": "rank r runs its slice of one seeded global batch (library shard plan)",
                        "l2": "flushed (256 MB write) between timed steps, outside the step events",
                        "precision": args.precision, "cuda_graph": True,
                        "fused_groups": stats["fused_groups"], "rows_per_run": stats["exec_nodes"]},
-            "e2e": {"value": world * batch / (mean_e2e * 1e-3), "unit": UNIT,
+            "e2e": {"value": global_batch / (mean_e2e * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": int(sum(b.nbytes for b in h_in)),
                     "d2h_bytes_per_step": int(sum(b.nbytes for b in h_out)), "ms_per_step": mean_e2e},
             "roofline": {"bound": "tensor", "kernel": "igemm_kernel (tcgen05 implicit-GEMM Conv/Gemm/MatMul)",
@@ -510,14 +669,18 @@ def main():
                          "tf32_dense_live": tf32,
                          "frac_of_tf32_dense_live": (achieved / tf32) if achieved else None,
                          "flops_per_step": tc_flop, "kernel_ms_per_step": tc_time,
-                         "share_of_step": tc_time / total_prof if total_prof else None,
+                         "share_of_step": share,
+                         "kernel_ms_note": "ms_per_step (timed CUDA-graph replay) x the contraction rows' share "
+                                           "of an eager pass with an event between rows",
+                         "kernel_ms_eager": tc_eager,
                          "traffic": TRAFFIC_BYTES.get((args.workload, batch)),
                          "traffic_note": "DRAM bytes read+written by the contraction launches of one step, "
                                          "from one ncu capture (profiles/resnet18_b64_igemm_dram.md)"
                          if (args.workload, batch) in TRAFFIC_BYTES else None},
             "top_rows_ms": [[lab, round(ms, 4)] for lab, ms in top_rows],
+            "bandwidth_rows": rows_table,
             "clocks": clk,
-            "gpu_launches": int(stats["kernels_per_run"]) * args.steps,
+            "gpu_launches": int(stats["kernels_per_run"]) * args.steps * world,
         }
     del flush
     m.close()

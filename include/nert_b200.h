@@ -259,6 +259,36 @@ int nb2_model_stats(const nb2_model* m, int64_t* kernels_per_run, int64_t* arena
 int nb2_model_profile(nb2_model* m, int max_steps, char* labels, int label_len, float* ms, int* count);
 int nb2_model_stream(const nb2_model* m, void** stream);
 
+/* ---- batch sharding over several GPUs ----------------------------------- */
+
+/* Contiguous slices of `batch` images over `n_shards` GPUs: shard i takes
+ * counts[i] images starting at offsets[i]; the first batch % n_shards shards
+ * take one image more. Host only. */
+int nb2_shard_plan(int64_t batch, int n_shards, int64_t* offsets, int64_t* counts);
+
+/* One graph run batch-sharded over several GPUs: a plan per GPU for its slice
+ * of the batch (every input leads with the same batch dimension; the graph
+ * must be valid at each slice's batch and every output must lead with the
+ * batch dimension), one host thread and stream per shard, the slices copied
+ * from and into the caller's host buffers at offset first-image x bytes per
+ * image. `ordinals[i]` is the GPU of shard i; shards may share a GPU (then
+ * CUDA-graph replay is required). No data crosses between GPUs: every op on
+ * the path is per image once BatchNormalization is folded. The reference
+ * binds one Model to one process-wide device (src/cuda_device.cpp:98-102,
+ * src/executor.cpp:202-225); this has no counterpart there. */
+typedef struct nb2_sharded nb2_sharded;
+int nb2_sharded_create(const void* onnx, int64_t size, int n_inputs, const char* const* input_names,
+                       const int64_t* dims_flat, const int* ranks, const int* ordinals, int n_shards, int flags,
+                       nb2_sharded** out);
+int nb2_sharded_destroy(nb2_sharded* s);
+int nb2_sharded_num_io(const nb2_sharded* s, int* n_inputs, int* n_outputs);
+/* name / dtype / global dims (up to 8) of input or output i */
+int nb2_sharded_io(const nb2_sharded* s, int is_output, int i, const char** name, int* dtype, int* rank,
+                   int64_t* dims8);
+int nb2_sharded_shard(const nb2_sharded* s, int i, int* ordinal, int64_t* batch_offset, int64_t* batch_count);
+/* Scatter, run every shard concurrently, gather; returns when all are done. */
+int nb2_sharded_run(nb2_sharded* s, const void* const* host_inputs, void* const* host_outputs);
+
 /* Host-only planning (no GPU needed): shapes, fused row list and arena plan
  * of a graph as JSON; *needed is the byte size including the terminator. */
 int nb2_graph_analyze(const void* onnx, int64_t size, int n_inputs, const char* const* input_names,

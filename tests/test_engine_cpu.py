@@ -20,6 +20,7 @@ import pytest
 
 from nert_b200 import _lib, configs, onnx_io
 from nert_b200 import model as nbm
+from nert_b200 import sharding  # noqa: F401  (binds the nb2_shard* entry points)
 from nert_b200.onnx_io import FLOAT, Graph
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
