@@ -48,7 +48,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-18 fp32 images/s bs64 at 1/2/4/8 B200; Conv/GEMM % of TF32 tensor peak"
 UNIT = "images/s"
-DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32}
+DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32, "conv": 64}
 
 
 def parse():
@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--global-batch", type=int, default=None,
                    help="fixed global batch split over the GPUs by the library's shard plan (strong scaling)")
     p.add_argument("--no-rows", action="store_true", help="skip the bandwidth-row table")
+    p.add_argument("--conv", default="3,224,224,64,7,2,3",
+                   help="--workload conv: C,H,W,M,K,S,P of one Conv+Relu on an NCHW input of --batch images")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--precision", default="3xtf32", choices=["3xtf32", "1xtf32"])
     a = p.parse_args()
@@ -82,7 +84,8 @@ def metric_for(workload: str, batch: int) -> str:
     return {"resnet50": f"ResNet-50 fp32 images/s bs{batch} per B200",
             "vit_b16": f"ViT-B/16 fp32 images/s bs{batch} per B200",
             "yolov8n": f"YOLOv8n-style fp32 images/s bs{batch} per B200 (640x640, TopK 300)",
-            "sweep": "single-op sweep fp32 TFLOP/s per op (config 1)"}[workload]
+            "sweep": "single-op sweep fp32 TFLOP/s per op (config 1)",
+            "conv": "one Conv+Relu through the engine, fp32 TFLOP/s"}[workload]
 
 
 def build_workload(workload: str, batch: int, rows: slice | None = None):
@@ -170,8 +173,8 @@ def run_reference(args):
     if not ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnert_ref.so was not built"}))
         return 0
-    if args.workload == "sweep":
-        print(json.dumps({"impl": "reference", "unavailable": "the sweep has no reference CPU arm"}))
+    if args.workload in ("sweep", "conv"):
+        print(json.dumps({"impl": "reference", "unavailable": "the single-op workloads have no reference CPU arm"}))
         return 0
     cores = ref_cores()
     pool = RefPool(cores, args.workload)
@@ -459,6 +462,61 @@ def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
 
 # ---- B200 leg ------------------------------------------------------------------------
 
+def run_conv(args, local):
+    """One Conv(+Relu) of the given geometry as an engine graph, timed like
+    the sweep: CUDA-graph replays, L2 flushed between them (also the target
+    for the committed ncu captures of single contraction launches)."""
+    import math
+
+    import torch
+
+    from nert_b200 import model as nbm
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    c, h, w, m, k, st, pd = (int(v) for v in args.conv.split(","))
+    n = args.batch
+    g = Graph(opset=13)
+    x = g.add_input("x", [n, c, h, w])
+    wt = synth.normal((m, c, k, k), math.sqrt(2.0 / (c * k * k)), synth.seed_of("bench_conv", "w"))
+    bi = synth.normal((m,), 0.1, synth.seed_of("bench_conv", "b"))
+    y = g.op("Relu", [g.op("Conv", [x, g.const("w", wt), g.const("b", bi)], name="conv", kernel_shape=[k, k],
+                           strides=[st, st], pads=[pd] * 4)], name="relu")
+    g.add_output(y, None, FLOAT)
+    feed = {"x": synth.uniform((n, c, h, w), -1.0, 1.0, synth.seed_of("bench_conv", "x"))}
+    mdl = nbm.Model(g, {"x": [n, c, h, w]}, device=local)
+    mdl.run(feed)
+    flops = sum(contraction_flops(g, nbm.analyze(g, {"x": [n, c, h, w]})).values())
+    stream = torch.cuda.ExternalStream(mdl.stream(), device=torch.device("cuda", local))
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    evs = []
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            mdl.launch()
+        for _ in range(args.steps):
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            mdl.launch()
+            e0.record(stream)
+            evs.append((s0, e0))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    rows = {lab: t for lab, t in mdl.profile()}
+    kpr = mdl.stats()["kernels_per_run"]
+    mdl.close()
+    peak, note = tensor_peak(args.precision)
+    print(json.dumps({"metric": metric_for("conv", n), "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32)",
+                      "data": "synthetic", "config": {"workload": "conv", "batch": n, "conv": args.conv,
+                                                      "l2": "flushed between timed steps"},
+                      "rows_ms": rows, "roofline": {"bound": "tensor", "peak": peak, "peak_note": note,
+                                                    "frac": flops / (ms * 1e-3) / 1e12 / peak},
+                      "gpu_launches": kpr * args.steps}), flush=True)
+    return 0
+
+
 def run_sweep(args, local):
     """Config 1: every Conv shape at batch 32 and every Gemm shape, one row each."""
     import torch
@@ -524,7 +582,7 @@ def main():
     rank, world, local = dist_env()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "sweep":
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv"):
         from oracle import ref
 
         if ref.available():
@@ -546,6 +604,8 @@ def main():
 
     if args.workload == "sweep":
         return run_sweep(args, local)
+    if args.workload == "conv":
+        return run_conv(args, local)
 
     from nert_b200 import model as nbm
 
