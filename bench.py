@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--global-batch", type=int, default=None,
                    help="fixed global batch split over the GPUs by the library's shard plan (strong scaling)")
     p.add_argument("--no-rows", action="store_true", help="skip the bandwidth-row table")
+    p.add_argument("--api", default="engine", choices=["engine", "seam"],
+                   help="seam: the reference's own loader and executor (oracle/_ref) on nert::b200::Device")
     p.add_argument("--conv", default="3,224,224,64,7,2,3",
                    help="--workload conv: C,H,W,M,K,S,P of one Conv+Relu on an NCHW input of --batch images")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -517,6 +519,72 @@ def run_conv(args, local):
     return 0
 
 
+def run_seam(args, local):
+    """The workload through the drop-in boundary: the reference's unmodified
+    LoadGraphFromFile -> nert::Model -> Run (compiled from its sources into
+    oracle/_ref) on nert::b200::Device(local). Every Run stages the input from
+    host memory, runs node by node through the seam rows and copies the output
+    back; timed with CUDA events on the device's stream around each Run."""
+    import ctypes
+
+    import torch
+
+    from nert_b200 import _lib, onnx_io
+    from oracle import ref
+
+    if not ref.available() or not os.path.exists(_lib.DEVICE_LIB_PATH):
+        print(json.dumps({"metric": metric_for(args.workload, args.batch), "unavailable":
+                          "the reference library or the device plug-in was not built"}))
+        return 0
+    ref.lib()
+    L = _lib.lib()
+    dl = ctypes.CDLL(_lib.DEVICE_LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+    dl.nb2_nert_device.restype = ctypes.c_void_p
+    dl.nb2_nert_device.argtypes = [ctypes.c_int]
+    handle = dl.nb2_nert_device(local)
+    graph, feeds = build_workload(args.workload, args.batch)
+    tmp = tempfile.TemporaryDirectory()
+    path = onnx_io.save(graph, os.path.join(tmp.name, "model.onnx"))
+    m = ref.RefModel(path, {k: list(v.shape) for k, v in feeds.items()}, handle)
+    stream = torch.cuda.ExternalStream(L.nb2_device_stream(_lib.device(local)), device=torch.device("cuda", local))
+    for _ in range(max(3, args.warmup)):
+        m.run(feeds)
+    evs, walls, runs = [], [], []
+    for _ in range(args.steps):
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        t0 = time.perf_counter()
+        out = m.run(feeds)
+        walls.append(time.perf_counter() - t0)
+        runs.append(m.last_ms)  # nert::Model::RunTyped alone (inputs already in its HostTensorMap)
+        e0.record(stream)
+        evs.append((s0, e0))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    wall_ms = 1000.0 * sum(walls) / len(walls)
+    run_ms = sum(runs) / len(runs)
+    m.close()
+    tmp.cleanup()
+    v = args.batch / (run_ms * 1e-3)
+    print(json.dumps({
+        "metric": metric_for(args.workload, args.batch), "value": v, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": run_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core contractions)",
+        "timing": "value = batch / the wall time of nert::Model::RunTyped (host input -> staged upload -> rows -> "
+                  "host output); event_ms_per_step brackets the whole call including the C shim's copy of the "
+                  "input into the reference's HostTensorMap",
+        "event_ms_per_step": ms,
+        "data": "synthetic (seeded inputs, Kaiming / N(0,0.02) weights, BN folded)",
+        "config": {"workload": args.workload, "per_gpu_batch": args.batch, "api": "seam",
+                   "path": "reference LoadGraphFromFile -> nert::Model -> Run on nert::b200::Device (one row per "
+                           "node, no fusion, no graph replay)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": int(sum(a.nbytes for a in feeds.values())),
+                "d2h_bytes_per_step": int(sum(a.nbytes for a in out.values())), "ms_per_step": run_ms,
+                "wall_ms_per_step": wall_ms},
+        "gpu_launches": None}), flush=True)
+    return 0
+
+
 def run_sweep(args, local):
     """Config 1: every Conv shape at batch 32 and every Gemm shape, one row each."""
     import torch
@@ -582,7 +650,8 @@ def main():
     rank, world, local = dist_env()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv"):
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv")
+            and args.api == "engine"):
         from oracle import ref
 
         if ref.available():
@@ -606,6 +675,8 @@ def main():
         return run_sweep(args, local)
     if args.workload == "conv":
         return run_conv(args, local)
+    if args.api == "seam":
+        return run_seam(args, local)
 
     from nert_b200 import model as nbm
 

@@ -160,6 +160,16 @@ int64_t nb2_conv2d_noalloc_capacity(void);
 int nb2_gemm(nb2_device* dev, const float* a, const float* b, const float* c, int c_rank, float* y, int64_t m,
              int64_t n, int64_t k, int trans_a, int trans_b, float alpha, float beta, int act);
 
+/* Packed-B form of the Gemm row for callers that keep B resident (a weight):
+ * pack op(B) ([k,n], or [n,k] stored when trans_b) once into
+ * nb2_gemm_packed_size bytes of device memory, then run many times with the
+ * same semantics as nb2_gemm. A MatMul with a rank-2 B is the same
+ * contraction with m = the product of A's leading dimensions. */
+int nb2_gemm_packed_size(int64_t n, int64_t k, int64_t* bytes);
+int nb2_gemm_pack(nb2_device* dev, const float* b, int64_t n, int64_t k, int trans_b, void* packed);
+int nb2_gemm_run_packed(nb2_device* dev, const float* a, const void* packed_b, const float* c, int c_rank, float* y,
+                        int64_t m, int64_t n, int64_t k, int trans_a, float alpha, float beta, int act);
+
 /* MatMul row: src/kernels/mat_mul.cpp:79-169 — NumPy matmul with 1-D
  * promotion. Batch dims must match the output's or be all ones/absent. */
 int nb2_matmul(nb2_device* dev, const float* a, const int64_t* a_dims, int a_rank, const float* b,

@@ -62,6 +62,11 @@ _SIGS = {
     "nb2_conv2d_run_packed": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp, vp, vp, ctypes.c_int, vp]),
     "nb2_gemm": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                 ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int]),
+    "nb2_gemm_packed_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, c_i64p]),
+    "nb2_gemm_pack": (ctypes.c_int, [vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, vp]),
+    "nb2_gemm_run_packed": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                           ctypes.c_int]),
     "nb2_matmul": (ctypes.c_int, [vp, vp, c_i64p, ctypes.c_int, vp, c_i64p, ctypes.c_int, vp]),
     "nb2_unary": (ctypes.c_int, [vp, ctypes.c_int, vp, vp, ctypes.c_int64]),
     "nb2_binary": (ctypes.c_int, [vp, ctypes.c_int, ctypes.c_int, vp, c_i64p, ctypes.c_int, vp, c_i64p, ctypes.c_int,

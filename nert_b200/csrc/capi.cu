@@ -111,6 +111,28 @@ struct HostStage {
 
 } // namespace
 
+namespace {
+
+// Bytes of the NHWC copy a converted NCHW input needs (0 when none).
+size_t nhwc_copy_bytes(const ConvGeom& g) {
+    return (g.cvec || g.cpad) ? static_cast<size_t>(g.N * g.Cin() * g.H * g.W * 4) : 0;
+}
+
+// A Conv whose input arrives NCHW: converted to NHWC first when its layout
+// asks for it (into `xbuf`, or the device workspace when null), then run.
+void run_nchw_conv(nb2_device* dev, const ConvGeom& g, const float* x, const void* packed, float* y,
+                   const Epilogue& ep, void* xbuf) {
+    if (g.cvec || g.cpad) {
+        float* xp = static_cast<float*>(xbuf != nullptr ? xbuf : dev->scratch(nhwc_copy_bytes(g)));
+        nchw_to_nhwc_pad(dev, x, xp, g.N, g.C, g.H, g.W, g.Cin());
+        conv_run(dev, g, xp, packed, y, ep);
+        return;
+    }
+    conv_run(dev, g, x, packed, y, ep);
+}
+
+} // namespace
+
 namespace nb2 {
 // The validated geometry of a C-ABI Conv description (shared by every Conv
 // entry point).
@@ -220,8 +242,21 @@ int nb2_memcpy_h2d(nb2_device* dev, void* dst, const void* src, int64_t bytes) {
         need(bytes > 0 && dst != nullptr && src != nullptr, "h2d: bad arguments");
         bind(dev);
         std::lock_guard<std::mutex> lock(dev->mu);
-        // Chunked through the pinned buffer so the caller may free `src`
-        // as soon as we return, while the copy stays ordered on the stream.
+        cudaPointerAttributes attr{};
+        const bool known = cudaPointerGetAttributes(&attr, src) == cudaSuccess;
+        if (!known) {
+            cudaGetLastError();
+        }
+        if (!known || attr.type == cudaMemoryTypeUnregistered) {
+            // pageable memory: the driver stages it through its own pinned
+            // buffers, pipelined, and returns once `src` has been read
+            check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyHostToDevice, dev->stream),
+                       "cudaMemcpyAsync(H2D)");
+            return;
+        }
+        // Pinned (or device-visible) memory would be read asynchronously:
+        // chunked through our pinned buffer so the caller may free `src` as
+        // soon as we return, while the copy stays ordered on the stream.
         const size_t chunk = 64u << 20;
         const auto* s = static_cast<const uint8_t*>(src);
         auto* d = static_cast<uint8_t*>(dst);
@@ -267,13 +302,13 @@ int nb2_memcpy_d2d(nb2_device* dev, void* dst, const void* src, int64_t bytes) {
 int nb2_conv2d_packed_size(const nb2_conv_geom* g, int64_t* bytes) {
     return guard([&] {
         need(bytes != nullptr, "null output pointer");
-        *bytes = static_cast<int64_t>(conv_packed_bytes(to_geom(g)));
+        *bytes = static_cast<int64_t>(conv_packed_bytes(nchw_input_layout(to_geom(g))));
     });
 }
 
 int nb2_conv2d_pack(nb2_device* dev, const nb2_conv_geom* g, const float* w, void* packed) {
     return guard([&] {
-        const ConvGeom geom = to_geom(g);
+        const ConvGeom geom = nchw_input_layout(to_geom(g));
         need(w != nullptr && packed != nullptr, "Conv: null buffer");
         bind(dev);
         conv_pack(dev, geom, w, packed);
@@ -283,30 +318,31 @@ int nb2_conv2d_pack(nb2_device* dev, const nb2_conv_geom* g, const float* w, voi
 int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* x, const void* packed,
                           const float* bias, const float* residual, int act, float* y) {
     return guard([&] {
-        const ConvGeom geom = to_geom(g);
+        const ConvGeom geom = nchw_input_layout(to_geom(g));
         need(x != nullptr && packed != nullptr && y != nullptr, "Conv: null buffer");
         bind(dev);
         Epilogue ep;
         ep.bias = bias;
         ep.res = residual;
         ep.act = act;
-        conv_run(dev, geom, x, packed, y, ep);
+        run_nchw_conv(dev, geom, x, packed, y, ep, nullptr);
     });
 }
 
 int nb2_conv2d(nb2_device* dev, const nb2_conv_geom* g, const float* x, const float* w, const float* bias,
                const float* residual, int act, float* y) {
     return guard([&] {
-        const ConvGeom geom = to_geom(g);
+        const ConvGeom geom = nchw_input_layout(to_geom(g));
         need(x != nullptr && w != nullptr && y != nullptr, "Conv: null buffer");
         bind(dev);
-        void* packed = dev->scratch(conv_packed_bytes(geom));
-        conv_pack(dev, geom, w, packed);
+        const size_t pbytes = (conv_packed_bytes(geom) + 255) & ~size_t(255);
+        uint8_t* ws = static_cast<uint8_t*>(dev->scratch(pbytes + nhwc_copy_bytes(geom)));
+        conv_pack(dev, geom, w, ws);
         Epilogue ep;
         ep.bias = bias;
         ep.res = residual;
         ep.act = act;
-        conv_run(dev, geom, x, packed, y, ep);
+        run_nchw_conv(dev, geom, x, ws, y, ep, ws + pbytes);
     });
 }
 
@@ -340,6 +376,62 @@ int nb2_gemm(nb2_device* dev, const float* a, const float* b, const float* c, in
         }
         ep.act = act;
         gemm_run(dev, g, a, packed, y, ep);
+    });
+}
+
+int nb2_gemm_packed_size(int64_t n, int64_t k, int64_t* bytes) {
+    return guard([&] {
+        need(n > 0 && k > 0 && bytes != nullptr, "Gemm: bad packed-size arguments");
+        GemmGeom g{};
+        g.N = n;
+        g.K = k;
+        g.batch = 1;
+        *bytes = static_cast<int64_t>(gemm_packed_bytes(g));
+    });
+}
+
+int nb2_gemm_pack(nb2_device* dev, const float* b, int64_t n, int64_t k, int trans_b, void* packed) {
+    return guard([&] {
+        need(n > 0 && k > 0, "Gemm: non-positive dimension");
+        need(b != nullptr && packed != nullptr, "Gemm: null buffer");
+        bind(dev);
+        GemmGeom g{};
+        g.N = n;
+        g.K = k;
+        g.batch = 1;
+        g.trans_b = trans_b;
+        g.ldb = trans_b ? k : n;
+        gemm_pack_b(dev, g, b, packed);
+    });
+}
+
+int nb2_gemm_run_packed(nb2_device* dev, const float* a, const void* packed_b, const float* c, int c_rank, float* y,
+                        int64_t m, int64_t n, int64_t k, int trans_a, float alpha, float beta, int act) {
+    return guard([&] {
+        need(m > 0 && n > 0 && k > 0, "Gemm: non-positive dimension");
+        need(a != nullptr && packed_b != nullptr && y != nullptr, "Gemm: null buffer");
+        need(c_rank >= 0 && c_rank <= 2, "Gemm: bias shape must be [N] or [M,N]");
+        need(c_rank == 0 || c != nullptr, "Gemm: null buffer");
+        bind(dev);
+        GemmGeom g{};
+        g.M = m;
+        g.N = n;
+        g.K = k;
+        g.batch = 1;
+        g.trans_a = trans_a;
+        g.lda = trans_a ? m : k;
+        g.ldc = n;
+        Epilogue ep;
+        ep.alpha = alpha;
+        if (c_rank == 1) {
+            ep.bias = c;
+            ep.bias_scale = beta;
+        } else if (c_rank == 2) {
+            ep.res = c;
+            ep.res_scale = beta;
+        }
+        ep.act = act;
+        gemm_run(dev, g, a, packed_b, y, ep);
     });
 }
 

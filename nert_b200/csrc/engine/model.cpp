@@ -802,15 +802,8 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             // of 32 and read through TMA im2col.
             const bool convertible = (flags & kNchwOnly) == 0 && !geom.in_nhwc &&
                                      packed_conv.count(n.inputs[1]) > 0 && geom.group == 1;
-            if (convertible && geom.C <= 16) {
-                geom.cvec = geom.C <= 4 ? 4 : (geom.C <= 8 ? 8 : 16);
-            } else if (convertible && geom.KH * geom.KW > 1 && geom.H * geom.W > 1) {
-                ConvGeom gp = geom;
-                gp.cpad = round_up(geom.C, 32);
-                gp.in_nhwc = true;
-                if (gp.nhwc_input_ok()) {
-                    geom = gp;
-                }
+            if (convertible) {
+                geom = nchw_input_layout(geom);
             }
             Epilogue ep;
             ep.bias = n.inputs.size() > 2 ? F(n.inputs[2]) : nullptr;

@@ -1286,6 +1286,25 @@ void fill_epilogue(Args& a, const Epilogue& ep) {
 
 // ---- Conv ------------------------------------------------------------------
 
+ConvGeom nchw_input_layout(const ConvGeom& g) {
+    if (g.group != 1 || g.in_nhwc || g.cvec || g.cpad) {
+        return g;
+    }
+    ConvGeom r = g;
+    if (g.C <= 16) {
+        r.cvec = g.C <= 4 ? 4 : (g.C <= 8 ? 8 : 16);
+        return r;
+    }
+    if (g.KH * g.KW > 1 && g.H * g.W > 1) {
+        r.cpad = round_up(g.C, 32);
+        r.in_nhwc = true;
+        if (r.nhwc_input_ok()) {
+            return r;
+        }
+    }
+    return g;
+}
+
 size_t conv_packed_bytes(const ConvGeom& g) {
     const int64_t kpad = round_up(g.K(), 32);
     size_t bytes = static_cast<size_t>(2 * g.M * kpad * 4);

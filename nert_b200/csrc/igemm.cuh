@@ -69,6 +69,13 @@ struct ConvGeom {
 
 int64_t round_up(int64_t v, int64_t m);
 
+// The layout a Conv over an NCHW input runs in once that input is converted
+// to NHWC in front of the contraction (group 1 only): up to 16 channels
+// padded to 4, 8 or 16 (each filter tap one to four 16-byte loads); a spatial
+// filter over more channels padded to a multiple of 32 and read through TMA
+// im2col; otherwise the geometry unchanged (gathered straight from NCHW).
+ConvGeom nchw_input_layout(const ConvGeom& g);
+
 // K slices the contraction kernel uses for a problem with `tiles` output
 // tiles and `nkb` 32-wide K blocks (1 = no split; >1 adds a reduce launch);
 // *kper = K blocks per slice.

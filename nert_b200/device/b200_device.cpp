@@ -34,6 +34,7 @@
 #include <array>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -50,6 +51,15 @@ namespace {
 
 thread_local nb2_device* tl_device = nullptr;
 thread_local std::map<const void*, std::vector<uint8_t>>* tl_mirror = nullptr;
+struct DeviceState;
+thread_local DeviceState* tl_state = nullptr;
+
+// The tensor-core layout of a resident weight, packed on first use and kept
+// until the weight's memory is released or written again (defined with the
+// seam objects below). Returns null when `w` is not a resident upload (then
+// the caller packs per call).
+const void* cached_pack(const void* w, int64_t w_bytes, const std::string& key, int64_t packed_bytes,
+                        const std::function<int(void*)>& pack, const std::string& ctx);
 
 [[noreturn]] void fail(const std::string& ctx, const std::string& msg) { throw InferenceException(ctx + ": " + msg); }
 
@@ -329,9 +339,27 @@ void Conv(const Node& node, const std::vector<TensorView>& in, const std::vector
     g.dil_h = one ? 1 : d[0];
     g.dil_w = one ? d[0] : d[1];
     g.group = group;
-    check(nb2_conv2d(current(ctx), &g, static_cast<const float*>(x.data), static_cast<const float*>(w.data),
-                     has_bias ? static_cast<const float*>(in[2].data) : nullptr, nullptr, NB2_ACT_NONE,
-                     static_cast<float*>(y.data)),
+    nb2_device* dev = current(ctx);
+    const float* bias = has_bias ? static_cast<const float*>(in[2].data) : nullptr;
+    int64_t pbytes = 0;
+    check(nb2_conv2d_packed_size(&g, &pbytes), ctx);
+    // the weights of a loaded graph are resident uploads: split and reorder
+    // them for the tensor cores once, not on every Run
+    const std::string key = "conv:" + std::to_string(g.c) + "," + std::to_string(g.h) + "," + std::to_string(g.w) +
+                            "," + std::to_string(g.m) + "," + std::to_string(g.kh) + "," + std::to_string(g.kw) +
+                            "," + std::to_string(g.dil_h) + "," + std::to_string(g.dil_w) + "," +
+                            std::to_string(g.group);
+    const void* packed = cached_pack(
+        w.data, count_of(w.dims) * 4, key, pbytes,
+        [&](void* dst) { return nb2_conv2d_pack(dev, &g, static_cast<const float*>(w.data), dst); }, ctx);
+    if (packed != nullptr) {
+        check(nb2_conv2d_run_packed(dev, &g, static_cast<const float*>(x.data), packed, bias, nullptr, NB2_ACT_NONE,
+                                    static_cast<float*>(y.data)),
+              ctx);
+        return;
+    }
+    check(nb2_conv2d(dev, &g, static_cast<const float*>(x.data), static_cast<const float*>(w.data), bias, nullptr,
+                     NB2_ACT_NONE, static_cast<float*>(y.data)),
           ctx);
 }
 
@@ -368,7 +396,22 @@ void Gemm(const Node& node, const std::vector<TensorView>& in, const std::vector
         }
         c = static_cast<const float*>(cv.data);
     }
-    check(nb2_gemm(current(ctx), static_cast<const float*>(a.data), static_cast<const float*>(b.data), c, c_rank,
+    nb2_device* dev = current(ctx);
+    int64_t pbytes = 0;
+    check(nb2_gemm_packed_size(n, k, &pbytes), ctx);
+    const void* packed = cached_pack(
+        b.data, count_of(b.dims) * 4, "gemm:" + std::to_string(n) + "," + std::to_string(k) + "," + std::to_string(tb),
+        pbytes,
+        [&](void* dst) { return nb2_gemm_pack(dev, static_cast<const float*>(b.data), n, k, static_cast<int>(tb), dst); },
+        ctx);
+    if (packed != nullptr) {
+        check(nb2_gemm_run_packed(dev, static_cast<const float*>(a.data), packed, c, c_rank,
+                                  static_cast<float*>(y.data), m, n, k, static_cast<int>(ta), alpha, beta,
+                                  NB2_ACT_NONE),
+              ctx);
+        return;
+    }
+    check(nb2_gemm(dev, static_cast<const float*>(a.data), static_cast<const float*>(b.data), c, c_rank,
                    static_cast<float*>(y.data), m, n, k, static_cast<int>(ta), static_cast<int>(tb), alpha, beta,
                    NB2_ACT_NONE),
           ctx);
@@ -379,6 +422,29 @@ void MatMul(const Node& node, const std::vector<TensorView>& in, const std::vect
     expect_io(node, in, out, 2, 2, 1);
     expect_f32(node, in[0]);
     expect_f32(node, in[1]);
+    const TensorView &a = in[0], &b = in[1];
+    if (b.dims.size() == 2 && a.dims.size() >= 2 && a.dims.back() == b.dims[0]) {
+        // a rank-2 B (a linear layer's weight) shared by every batch: one
+        // contraction over all of A's rows with B packed once
+        nb2_device* dev = current(ctx);
+        const int64_t k = b.dims[0], n = b.dims[1], m = count_of(a.dims) / k;
+        std::vector<int64_t> want(a.dims.begin(), a.dims.end() - 1);
+        want.push_back(n);
+        if (out[0].dims != want) {
+            fail(ctx, "output shape does not match the operands");
+        }
+        int64_t pbytes = 0;
+        check(nb2_gemm_packed_size(n, k, &pbytes), ctx);
+        const void* packed = cached_pack(
+            b.data, count_of(b.dims) * 4, "gemm:" + std::to_string(n) + "," + std::to_string(k) + ",0", pbytes,
+            [&](void* dst) { return nb2_gemm_pack(dev, static_cast<const float*>(b.data), n, k, 0, dst); }, ctx);
+        if (packed != nullptr && m > 0) {
+            check(nb2_gemm_run_packed(dev, static_cast<const float*>(a.data), packed, nullptr, 0,
+                                      static_cast<float*>(out[0].data), m, n, k, 0, 1.0f, 1.0f, NB2_ACT_NONE),
+                  ctx);
+            return;
+        }
+    }
     check(nb2_matmul(current(ctx), static_cast<const float*>(in[0].data), in[0].dims.data(),
                      static_cast<int>(in[0].dims.size()), static_cast<const float*>(in[1].data), in[1].dims.data(),
                      static_cast<int>(in[1].dims.size()), static_cast<float*>(out[0].data)),
@@ -810,8 +876,63 @@ struct DeviceState {
     std::map<const void*, std::vector<uint8_t>> mirror;
     std::multimap<int64_t, void*> pool; // released buffers kept for reuse, by size
     std::unordered_map<void*, int64_t> sizes;
+    // bytes written by host_to_device at each destination since it was last
+    // (re)allocated: the executor uploads every initializer into a buffer of
+    // its own once per Model (src/executor.cpp:390-413)
+    std::map<const void*, int64_t> uploads;
+    // packed tensor-core layouts of resident weights, by weight address
+    struct Packed {
+        std::string key;
+        void* buf = nullptr;
+    };
+    std::map<const void*, Packed> packs;
     std::mutex mu;
+
+    // Drops uploads and packs whose address lies in [lo, lo + bytes); the
+    // caller holds `mu`.
+    void forget(const void* lo, int64_t bytes) {
+        const auto* b = static_cast<const uint8_t*>(lo);
+        for (auto it = packs.lower_bound(lo); it != packs.end() && static_cast<const uint8_t*>(it->first) < b + bytes;) {
+            nb2_device_free(dev, it->second.buf);
+            it = packs.erase(it);
+        }
+        for (auto it = uploads.lower_bound(lo);
+             it != uploads.end() && static_cast<const uint8_t*>(it->first) < b + bytes;) {
+            it = uploads.erase(it);
+        }
+    }
 };
+
+const void* cached_pack(const void* w, int64_t w_bytes, const std::string& key, int64_t packed_bytes,
+                        const std::function<int(void*)>& pack, const std::string& ctx) {
+    DeviceState* st = tl_state;
+    if (st == nullptr || w == nullptr) {
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(st->mu);
+    auto up = st->uploads.find(w);
+    if (up == st->uploads.end() || up->second < w_bytes) {
+        return nullptr; // not a resident upload (an activation, or a partial write)
+    }
+    auto it = st->packs.find(w);
+    if (it != st->packs.end()) {
+        if (it->second.key == key) {
+            return it->second.buf;
+        }
+        nb2_device_free(st->dev, it->second.buf); // the same weight seen with another geometry
+        st->packs.erase(it);
+    }
+    void* buf = nullptr;
+    if (nb2_device_malloc(st->dev, packed_bytes, &buf) != NB2_OK || buf == nullptr) {
+        return nullptr; // no room: pack per call in the workspace instead
+    }
+    if (pack(buf) != NB2_OK) {
+        nb2_device_free(st->dev, buf);
+        fail(ctx, nb2_last_error());
+    }
+    st->packs[w] = DeviceState::Packed{key, buf};
+    return buf;
+}
 
 class B200Allocator final : public Allocator {
   public:
@@ -848,6 +969,7 @@ class B200Allocator final : public Allocator {
         if (it == s_->sizes.end()) {
             return;
         }
+        s_->forget(buffer, it->second);
         // queued work may still read the buffer: wait before it is reused
         nb2_device_synchronize(s_->dev);
         s_->pool.emplace(it->second, buffer);
@@ -864,13 +986,17 @@ class B200Transfer final : public Transfer {
         if (bytes == 0) {
             return;
         }
-        if (bytes <= 4096) {
+        {
             std::lock_guard<std::mutex> lock(s_->mu);
-            const auto* b = static_cast<const uint8_t*>(src);
-            s_->mirror[dst].assign(b, b + bytes);
-        } else {
-            std::lock_guard<std::mutex> lock(s_->mu);
-            s_->mirror.erase(dst);
+            if (bytes <= 4096) {
+                const auto* b = static_cast<const uint8_t*>(src);
+                s_->mirror[dst].assign(b, b + bytes);
+            } else {
+                s_->mirror.erase(dst);
+            }
+            // new contents: any packed layout of these bytes is stale
+            s_->forget(dst, bytes);
+            s_->uploads[dst] = bytes;
         }
         if (nb2_memcpy_h2d(s_->dev, dst, src, bytes) != NB2_OK) {
             throw InferenceException(std::string("B200 transfer: ") + nb2_last_error());
@@ -932,6 +1058,7 @@ class B200Table final : public KernelTable {
     KernelFn find(const std::string& op_type) const override {
         tl_device = s_->dev;
         tl_mirror = &s_->mirror;
+        tl_state = s_;
         auto it = rows_.find(op_type);
         return it == rows_.end() ? nullptr : it->second;
     }
