@@ -341,7 +341,8 @@ def hbm_peak() -> tuple[float, str]:
 def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
     """Every HBM-bound row at the largest config geometry that uses it,
     launched through the C ABI on the layer's stream and timed with CUDA
-    events around each launch (L2 flushed by a 256 MB write before each).
+    events around each launch (L2 flushed before each by a 256 MB write and a
+    read of the same buffer).
     bytes = the row's algorithmic bytes (read once + write once)."""
     import ctypes
 
@@ -355,6 +356,7 @@ def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
     stream = torch.cuda.ExternalStream(L.nb2_device_stream(dev), device=torch.device("cuda", local))
     cuda = torch.device("cuda", local)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=cuda)
+    flush_sum = torch.empty((), dtype=torch.float32, device=cuda)
     g = torch.Generator(device=cuda)
     g.manual_seed(7)
 
@@ -446,7 +448,10 @@ def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
                 _lib.check(fn())
             evs = []
             for _ in range(reps):
+                # flush L2: write 256 MB, then read it back so the lines the
+                # row's reads evict are clean (no write-back inside its time)
                 flush.zero_()
+                flush_sum.copy_(flush.sum())
                 s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 s.record(stream)
                 _lib.check(fn())

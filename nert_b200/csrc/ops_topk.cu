@@ -15,10 +15,14 @@
 // shared memory.
 //
 // Short rows (L < kSplitMin) use one 1024-thread CTA per row. Long rows (the
-// detector's 8400*80 scores) are split over many CTAs per row: each digit pass
-// is a grid-wide histogram with warp-aggregated shared-memory atomics, and the
-// digit selection is recomputed from the histograms by every CTA of the next
-// pass, so no separate selection launch is needed.
+// detector's 8400*80 scores) first take the sampled-threshold path: one read
+// of the row keeps every key at or above a threshold drawn from a sample, and
+// the few thousand survivors are ranked exactly. A row for which that cannot
+// be exact (fewer than k survivors, or more than the candidate list holds,
+// e.g. a flood of equal values) is redone by the radix passes: each digit
+// pass is a grid-wide histogram with warp-aggregated shared-memory atomics,
+// and the digit selection is recomputed from the histograms by every CTA of
+// the next pass, so no separate selection launch is needed.
 
 #include "ops_move.cuh"
 
@@ -255,9 +259,12 @@ __device__ void select_prefix(const uint32_t* __restrict__ hist_row, int pass, i
 // grid (chunks, rows): histogram of digit `pass` over keys matching the
 // prefix chosen by the earlier passes.
 __global__ void __launch_bounds__(512) topk_hist_kernel(const float* __restrict__ x, int64_t L, int k, int pass,
-                                                         uint32_t* __restrict__ hist) {
+                                                         uint32_t* __restrict__ hist, const int* __restrict__ done) {
     __shared__ uint32_t h[kBins];
     const int64_t row = blockIdx.y;
+    if (done != nullptr && done[row]) {
+        return; // finished by the sampled-threshold path
+    }
     uint32_t* hist_row = hist + row * 3 * kBins;
     for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
         h[i] = 0;
@@ -306,9 +313,13 @@ __global__ void __launch_bounds__(512) topk_hist_kernel(const float* __restrict_
 // grid (chunks, rows): how many keys of each chunk equal T.
 __global__ void __launch_bounds__(512) topk_eqcount_kernel(const float* __restrict__ x, int64_t L, int k,
                                                             const uint32_t* __restrict__ hist,
-                                                            int* __restrict__ eq_counts, int chunks) {
+                                                            int* __restrict__ eq_counts, int chunks,
+                                                            const int* __restrict__ done) {
     __shared__ int s_count;
     const int64_t row = blockIdx.y;
+    if (done != nullptr && done[row]) {
+        return;
+    }
     uint32_t T, mask;
     int need;
     select_prefix(hist + row * 3 * kBins, 3, k, T, mask, need);
@@ -344,10 +355,14 @@ __global__ void __launch_bounds__(512) topk_collect_kernel(const float* __restri
                                                             const uint32_t* __restrict__ hist,
                                                             const int* __restrict__ eq_counts, int chunks,
                                                             int* __restrict__ gt_count, uint32_t* __restrict__ cand_key,
-                                                            int64_t* __restrict__ cand_idx) {
+                                                            int64_t* __restrict__ cand_idx,
+                                                            const int* __restrict__ done) {
     __shared__ int warp_counts[16];
     __shared__ int s_base;
     const int64_t row = blockIdx.y;
+    if (done != nullptr && done[row]) {
+        return;
+    }
     uint32_t T, mask;
     int need;
     select_prefix(hist + row * 3 * kBins, 3, k, T, mask, need);
@@ -407,10 +422,14 @@ __global__ void __launch_bounds__(kThreads) topk_sort_kernel(const float* __rest
                                                               int sort_n, const uint32_t* __restrict__ cand_key,
                                                               const int64_t* __restrict__ cand_idx,
                                                               float* __restrict__ values,
-                                                              int64_t* __restrict__ indices) {
+                                                              int64_t* __restrict__ indices,
+                                                              const int* __restrict__ done) {
     __shared__ uint32_t sk[kMaxK];
     __shared__ int64_t si[kMaxK];
     const int64_t row = blockIdx.x;
+    if (done != nullptr && done[row]) {
+        return;
+    }
     for (int i = threadIdx.x; i < sort_n; i += blockDim.x) {
         sk[i] = i < k ? cand_key[row * k + i] : 0u;
         si[i] = i < k ? cand_idx[row * k + i] : INT64_MAX;
@@ -423,18 +442,334 @@ __global__ void __launch_bounds__(kThreads) topk_sort_kernel(const float* __rest
     }
 }
 
+
+// ---- sampled-threshold path for long rows --------------------------------------
+//
+// One read of the row instead of five: a threshold t is taken from a sample
+// of the row (kSampleBlocks contiguous blocks spread over it) as its j-th
+// largest key, with j sized so that about 4k keys of the full row reach t;
+// every key >= t is appended to a candidate list; the candidates are sorted
+// by (key desc, index asc) and the first k written. Exact whenever at least k
+// keys reach t (then the k-th largest key T >= t, so every key >= T, ties
+// included, is a candidate) and the list did not overflow; a row for which
+// either fails is flagged and redone by the radix passes above.
+
+constexpr int kSampleBlocks = 32;
+constexpr int kSampleBlock = 1024;
+constexpr int kSample = kSampleBlocks * kSampleBlock;
+constexpr int kCandCap = 2048;
+constexpr int kSampledMaxK = 384; // largest k the sampled path takes
+constexpr int kFilterChunk = 16384;
+
+__device__ __forceinline__ int64_t sample_pos(int64_t L, int i) {
+    const int b = i / kSampleBlock;
+    const int64_t start = (L - kSampleBlock) * b / (kSampleBlocks - 1);
+    return start + (i - b * kSampleBlock);
+}
+
+// Exact key of rank j (1 = largest) among keys[0..n) in shared memory, by
+// three digit passes over a 2048-bin histogram (warp-aggregated atomics).
+// Every thread of the block calls it; returns the key and how many keys
+// greater than it there are.
+__device__ uint32_t block_kth_key(const uint32_t* keys, int n, int j, uint32_t* hist, int* n_greater) {
+    __shared__ uint32_t s_prefix, s_mask;
+    __shared__ int s_need;
+    __shared__ uint32_t lane_tot[32];
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        s_prefix = 0;
+        s_mask = 0;
+        s_need = j;
+    }
+    for (int pass = 0; pass < 3; ++pass) {
+        for (int i = tid; i < kBins; i += blockDim.x) {
+            hist[i] = 0;
+        }
+        __syncthreads();
+        const uint32_t prefix = s_prefix, mask = s_mask;
+        const int sh = digit_shift(pass);
+        const uint32_t dm = digit_mask(pass);
+        for (int base = 0; base < n; base += blockDim.x) {
+            const int i = base + tid;
+            const bool in = i < n && (keys[i] & mask) == prefix;
+            const uint32_t bin = in ? (keys[i] >> sh) & dm : 0xFFFFFFFFu;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (in && (__ffs(peers) - 1) == (tid & 31)) {
+                atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+            }
+        }
+        __syncthreads();
+        if (tid < 32) {
+            uint32_t mine = 0;
+            for (int b = 0; b < 64; ++b) {
+                mine += hist[tid * 64 + ((b + tid) & 63)]; // skewed: lanes on distinct banks
+            }
+            lane_tot[tid] = mine;
+            __syncwarp();
+            if (tid == 0) {
+                const int need = s_need;
+                uint32_t above = 0;
+                int sel = 0;
+                for (int l = 31; l >= 0; --l) {
+                    if (above + lane_tot[l] >= static_cast<uint32_t>(need)) {
+                        for (int b = l * 64 + 63; b >= l * 64; --b) {
+                            if (above + hist[b] >= static_cast<uint32_t>(need)) {
+                                sel = b;
+                                break;
+                            }
+                            above += hist[b];
+                        }
+                        break;
+                    }
+                    above += lane_tot[l];
+                }
+                s_need = need - static_cast<int>(above);
+                s_prefix |= static_cast<uint32_t>(sel) << sh;
+                s_mask |= dm << sh;
+            }
+        }
+        __syncthreads();
+    }
+    *n_greater = j - s_need;
+    return s_prefix;
+}
+
+// grid rows, 1024 threads: thread i takes the i-th element of every sample
+// block (kSampleBlocks values spread over the row) and keeps their largest
+// key; thresh[row] = the j-th largest of those 1024 maxima. At least j
+// sampled keys reach it, and a sampled key seldom shares its thread with
+// another top one, so about j * L / kSample keys of the row reach it.
+__global__ void __launch_bounds__(kThreads) topk_sample_kernel(const float* __restrict__ x, int64_t L, int j,
+                                                                uint32_t* __restrict__ thresh) {
+    __shared__ uint32_t keys[kThreads];
+    __shared__ uint32_t hist[kBins];
+    const float* r = x + blockIdx.x * L;
+    const int tid = threadIdx.x;
+    uint32_t best = 0;
+#pragma unroll 8
+    for (int q = 0; q < kSampleBlocks; ++q) {
+        best = max(best, key_of(__ldg(r + sample_pos(L, q * kThreads + tid))));
+    }
+    keys[tid] = best;
+    __syncthreads();
+    int greater = 0;
+    const uint32_t t = block_kth_key(keys, kThreads, j, hist, &greater);
+    if (tid == 0) {
+        thresh[blockIdx.x] = t;
+    }
+}
+
+// grid (chunks, rows), 256 threads: append every key >= thresh[row] with its
+// index (one atomic per warp and load round).
+__global__ void __launch_bounds__(256) topk_filter_kernel(const float* __restrict__ x, int64_t L,
+                                                           const uint32_t* __restrict__ thresh,
+                                                           int* __restrict__ count, uint32_t* __restrict__ cand_key,
+                                                           int64_t* __restrict__ cand_idx, int vec4) {
+    const int64_t row = blockIdx.y;
+    const uint32_t t = thresh[row];
+    const float* r = x + row * L;
+    const int64_t begin = static_cast<int64_t>(blockIdx.x) * kFilterChunk;
+    const int64_t end = min(begin + kFilterChunk, L);
+    const int lane = threadIdx.x & 31;
+    uint32_t* ck = cand_key + row * kCandCap;
+    int64_t* ci = cand_idx + row * kCandCap;
+    auto emit = [&](bool hit, uint32_t key, int64_t i) {
+        const unsigned ballot = __ballot_sync(0xffffffffu, hit);
+        if (ballot == 0u) {
+            return;
+        }
+        int base = 0;
+        if (lane == 0) {
+            base = atomicAdd(&count[row], __popc(ballot));
+        }
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (hit) {
+            const int slot = base + __popc(ballot & ((1u << lane) - 1u));
+            if (slot < kCandCap) {
+                ck[slot] = key;
+                ci[slot] = i;
+            }
+        }
+    };
+    if (vec4) {
+        const float4* r4 = reinterpret_cast<const float4*>(r);
+        // four float4 per thread in flight per round
+        for (int64_t q0 = begin / 4 + threadIdx.x; q0 * 4 < end; q0 += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t q = q0 + u * blockDim.x;
+                v[u] = q * 4 < end ? __ldg(r4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t q = q0 + u * blockDim.x;
+                const bool in = q * 4 < end;
+                const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                const bool any = in && (key_of(f[0]) >= t || key_of(f[1]) >= t || key_of(f[2]) >= t ||
+                                        key_of(f[3]) >= t);
+                if (__ballot_sync(0xffffffffu, any) == 0u) {
+                    continue; // nearly every round: nothing in this warp reaches t
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t key = key_of(f[c]);
+                    emit(in && key >= t, key, q * 4 + c);
+                }
+            }
+        }
+    } else {
+        for (int64_t i0 = begin + threadIdx.x; i0 < end; i0 += blockDim.x) {
+            const uint32_t key = key_of(__ldg(r + i0));
+            emit(key >= t, key, i0);
+        }
+    }
+}
+
+// grid rows: the first k candidates in (key desc, index asc) order; flags rows
+// whose list is short of k or overflowed (done[row] = 0) for the radix passes.
+// T = the k-th largest candidate key; every key > T is taken, and of the keys
+// == T the ones with the smallest indices; the k taken are placed by counting
+// how many of them precede each.
+__global__ void __launch_bounds__(kThreads) topk_final_kernel(const float* __restrict__ x, int64_t L, int k,
+                                                               const int* __restrict__ count,
+                                                               const uint32_t* __restrict__ cand_key,
+                                                               const int64_t* __restrict__ cand_idx,
+                                                               float* __restrict__ values,
+                                                               int64_t* __restrict__ indices, int* __restrict__ done) {
+    __shared__ uint32_t sk[kCandCap];
+    __shared__ int64_t si[kCandCap];
+    __shared__ uint32_t hist[kBins];
+    __shared__ uint32_t tk[kSampledMaxK];
+    __shared__ int64_t ti[kSampledMaxK];
+    __shared__ int s_taken, s_ties;
+    __shared__ int tie_pos[kCandCap]; // positions in sk / si of the keys == T
+    const int64_t row = blockIdx.x;
+    const int n = count[row];
+    if (n < k || n > kCandCap) {
+        if (threadIdx.x == 0) {
+            done[row] = 0;
+        }
+        return;
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        sk[i] = cand_key[row * kCandCap + i];
+        si[i] = cand_idx[row * kCandCap + i];
+    }
+    if (threadIdx.x == 0) {
+        s_taken = 0;
+        s_ties = 0;
+    }
+    __syncthreads();
+    int greater = 0;
+    const uint32_t T = block_kth_key(sk, n, k, hist, &greater);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        if (sk[i] > T) {
+            const int slot = atomicAdd(&s_taken, 1);
+            tk[slot] = sk[i];
+            ti[slot] = si[i];
+        } else if (sk[i] == T) {
+            tie_pos[atomicAdd(&s_ties, 1)] = i;
+        }
+    }
+    __syncthreads();
+    const int ties = s_ties;
+    const int need = k - greater;
+    for (int i = threadIdx.x; i < ties; i += blockDim.x) {
+        const int64_t me = si[tie_pos[i]];
+        int r = 0;
+        for (int q = 0; q < ties; ++q) {
+            r += si[tie_pos[q]] < me ? 1 : 0;
+        }
+        if (r < need) {
+            tk[greater + r] = T;
+            ti[greater + r] = me;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const uint32_t ki = tk[i];
+        const int64_t ii = ti[i];
+        int rank = 0;
+        for (int q = 0; q < k; ++q) {
+            rank += (tk[q] > ki || (tk[q] == ki && ti[q] < ii)) ? 1 : 0;
+        }
+        values[row * k + rank] = x[row * L + ii];
+        indices[row * k + rank] = ii;
+    }
+    if (threadIdx.x == 0) {
+        done[row] = 1;
+    }
+}
+
+} // namespace
+
+// Sizes of the sampled-threshold path's sample and of its j (see above), or
+// 0 when a row is too short or k too large for it (radix passes only).
+static int sample_rank(int64_t L, int64_t k) {
+    if (L < 65536 || k > kSampledMaxK) {
+        return 0;
+    }
+    const int64_t j = (4 * k * kSample + L - 1) / L;
+    return (j >= 32 && j <= kThreads / 4) ? static_cast<int>(j) : 0;
+}
+
+namespace {
+struct TopkScratch {
+    uint32_t* hist;
+    int* eq_counts;
+    int* gt_count;
+    int64_t* cand_idx;
+    uint32_t* cand_key;
+    uint32_t* thresh;
+    int* count;
+    int* done;
+    uint32_t* fkey;
+    int64_t* fidx;
+    size_t head;  // bytes cleared before the radix passes
+    size_t fhead; // bytes cleared before the filter (thresh, count, done)
+    size_t total;
+};
+
+TopkScratch topk_layout(void* base, int64_t rows, int64_t L, int64_t k) {
+    auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+    const int64_t chunks = (L + kChunk - 1) / kChunk;
+    TopkScratch t{};
+    uint8_t* p = static_cast<uint8_t*>(base);
+    size_t at = 0;
+    t.hist = reinterpret_cast<uint32_t*>(p + at);
+    t.eq_counts = reinterpret_cast<int*>(p + at + static_cast<size_t>(rows) * 3 * kBins * 4);
+    t.gt_count = t.eq_counts + rows * chunks;
+    t.head = al(static_cast<size_t>(rows) * 3 * kBins * 4 + static_cast<size_t>(rows * chunks) * 4 +
+                static_cast<size_t>(rows) * 4);
+    at += t.head;
+    t.cand_idx = reinterpret_cast<int64_t*>(p + at);
+    at += al(static_cast<size_t>(rows * k) * 8);
+    t.cand_key = reinterpret_cast<uint32_t*>(p + at);
+    at += al(static_cast<size_t>(rows * k) * 4);
+    t.thresh = reinterpret_cast<uint32_t*>(p + at);
+    t.count = reinterpret_cast<int*>(p + at + rows * 4);
+    t.done = t.count + rows;
+    t.fhead = al(static_cast<size_t>(rows) * 12);
+    const size_t fat = at;
+    at += t.fhead;
+    if (sample_rank(L, k) > 0) {
+        t.fkey = reinterpret_cast<uint32_t*>(p + at);
+        at += al(static_cast<size_t>(rows) * kCandCap * 4);
+        t.fidx = reinterpret_cast<int64_t*>(p + at);
+        at += al(static_cast<size_t>(rows) * kCandCap * 8);
+    }
+    (void)fat;
+    t.total = at;
+    return t;
+}
 } // namespace
 
 size_t topk_scratch_bytes(int64_t rows, int64_t L, int64_t k) {
     if (L < kSplitMin) {
         return 0;
     }
-    const int64_t chunks = (L + kChunk - 1) / kChunk;
-    const size_t hist = static_cast<size_t>(rows) * 3 * kBins * 4;
-    const size_t eq = static_cast<size_t>(rows * chunks) * 4;
-    const size_t gt = static_cast<size_t>(rows) * 4;
-    const size_t cand = static_cast<size_t>(rows * k) * 12;
-    return ((hist + eq + gt + 255) / 256) * 256 + cand + 256;
+    return topk_layout(nullptr, rows, L, k).total;
 }
 
 void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t L, int64_t k,
@@ -464,25 +799,33 @@ void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int6
     if (scratch == nullptr) {
         fail(kStatusInvalid, "TopK: long rows need scratch memory");
     }
+    const TopkScratch t = topk_layout(scratch, rows, L, k);
     const int chunks = static_cast<int>((L + kChunk - 1) / kChunk);
-    auto* hist = static_cast<uint32_t*>(scratch);
-    int* eq_counts = reinterpret_cast<int*>(hist + rows * 3 * kBins);
-    int* gt_count = eq_counts + rows * chunks;
-    const size_t head = ((static_cast<size_t>(rows) * 3 * kBins * 4 + static_cast<size_t>(rows * chunks) * 4 +
-                          static_cast<size_t>(rows) * 4 + 255) / 256) * 256;
-    auto* cand_idx = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(scratch) + head);
-    auto* cand_key = reinterpret_cast<uint32_t*>(cand_idx + rows * k);
-    check_cuda(cudaMemsetAsync(scratch, 0, head, dev->stream), "topk scratch clear");
-    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(rows));
     const int ki = static_cast<int>(k);
-    for (int pass = 0; pass < 3; ++pass) {
-        topk_hist_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, pass, hist);
+    const int j = sample_rank(L, k);
+    const int* done = nullptr;
+    if (j > 0) {
+        check_cuda(cudaMemsetAsync(t.thresh, 0, t.fhead, dev->stream), "topk scratch clear");
+        topk_sample_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, j, t.thresh);
+        const int vec4 = (L % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) ? 1 : 0;
+        const dim3 fgrid(static_cast<unsigned>((L + kFilterChunk - 1) / kFilterChunk), static_cast<unsigned>(rows));
+        topk_filter_kernel<<<fgrid, 256, 0, dev->stream>>>(x, L, t.thresh, t.count, t.fkey, t.fidx, vec4);
+        topk_final_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, ki, t.count, t.fkey, t.fidx,
+                                                                                    values, indices, t.done);
+        done = t.done;
     }
-    topk_eqcount_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, hist, eq_counts, chunks);
-    topk_collect_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, hist, eq_counts, chunks, gt_count, cand_key,
-                                                       cand_idx);
-    topk_sort_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, ki, sort_n, cand_key,
-                                                                                cand_idx, values, indices);
+    // radix passes: every row when the sampled path does not apply, else
+    // only the rows it flagged (the others return at once)
+    check_cuda(cudaMemsetAsync(scratch, 0, t.head, dev->stream), "topk scratch clear");
+    const dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>(rows));
+    for (int pass = 0; pass < 3; ++pass) {
+        topk_hist_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, pass, t.hist, done);
+    }
+    topk_eqcount_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, t.hist, t.eq_counts, chunks, done);
+    topk_collect_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, t.hist, t.eq_counts, chunks, t.gt_count, t.cand_key,
+                                                       t.cand_idx, done);
+    topk_sort_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, ki, sort_n, t.cand_key,
+                                                                                t.cand_idx, values, indices, done);
     check_cuda(cudaGetLastError(), "topk launch");
 }
 

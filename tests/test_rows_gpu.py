@@ -205,3 +205,22 @@ def test_gather_out_of_range_reports_device_error(cuda):
     # the context stays usable after the reported error
     out = run_engine(g, {"x": np.ones((10, 4), np.float32), "idx": np.array([1, 9, -10], np.int64)})
     assert np.all(list(out.values())[0] == 1.0)
+
+
+def test_topk_long_rows_mixed_ties(cuda):
+    """Long rows take a sampled threshold, one filtering read and an exact sort
+    of the survivors; a row whose survivors overflow (here 200,000 exact ties
+    at the top) is redone by the radix passes while the other rows keep the
+    fast result. Row 0: distinct values; row 1: 500 exact ties of the largest
+    value among distinct ones (resolved by index); row 2: the overflow row."""
+    L = 672000
+    base = np.argsort(synth.uniform((3 * L,), 0, 1, 21), kind="stable").astype(np.float64)
+    x = ((base / (3 * L)) * 2 - 1).astype(np.float32).reshape(3, L)
+    pos = (synth.uniform((500,), 0, 1, 22) * L).astype(np.int64)
+    x[1, pos] = 2.0
+    x[2, ::3] = 3.0
+    g, _ = one("TopK", [(3, L), (1,)], {"axis": -1}, {1: np.array([300], np.int64)}, n_out=2)
+    ref = np_ref.run(g, {"in0": x})
+    got = run_engine(g, {"in0": x})
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
