@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--global-batch", type=int, default=None,
                    help="fixed global batch split over the GPUs by the library's shard plan (strong scaling)")
     p.add_argument("--no-rows", action="store_true", help="skip the bandwidth-row table")
+    p.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
+                   help="--impl reference: the reference CpuDevice (the driver's arm) or its own CudaDevice "
+                        "(cuDNN Conv, cuBLAS Gemm/MatMul; the GPU baseline)")
     p.add_argument("--api", default="engine", choices=["engine", "seam"],
                    help="seam: the reference's own loader and executor (oracle/_ref) on nert::b200::Device")
     p.add_argument("--conv", default="3,224,224,64,7,2,3",
@@ -166,10 +169,74 @@ def ref_cores() -> int:
     return max(1, min(os.cpu_count() or 1, 8))
 
 
+def run_reference_cuda(args):
+    """The reference's unmodified loader and executor on its own CudaDevice
+    (src/cuda_device.cpp: cuDNN Conv src/cuda/conv.cu:230-530, cuBLAS
+    Gemm/MatMul src/cuda/gemm.cu:84-166, mat_mul.cu:94-198, a synchronise after
+    every row), built by oracle/Makefile: the GPU baseline. Times
+    nert::Model::RunTyped (host input -> output) per step."""
+    from oracle import ref
+
+    from nert_b200 import onnx_io
+
+    if not ref.available(cuda=True):
+        print(json.dumps({"impl": "reference", "device": "cuda",
+                          "unavailable": "oracle/_ref/libnert_ref_cuda.so was not built (needs nvcc and cuDNN)"}))
+        return 0
+    cases = []
+    if args.workload == "sweep":
+        from nert_b200 import configs
+
+        cases = [(n, *configs.sweep_conv(n, args.batch)) for n, *_ in configs.SWEEP_CONVS]
+        cases += [(f"gemm_{m}x{n}x{k}", *configs.sweep_gemm(m, n, k)) for m, n, k in configs.SWEEP_GEMMS]
+    else:
+        g, feeds = build_workload(args.workload, args.batch)
+        cases = [(args.workload, g, feeds)]
+    rows = []
+    with tempfile.TemporaryDirectory() as d:
+        for name, g, feeds in cases:
+            path = onnx_io.save(g, os.path.join(d, f"{name}.onnx"))
+            m = ref.RefModel(path, {k: list(v.shape) for k, v in feeds.items()}, cuda=True)
+            try:
+                for _ in range(max(1, args.warmup)):
+                    m.run(feeds)
+                ms = []
+                for _ in range(args.steps):
+                    m.run(feeds)
+                    ms.append(m.last_ms)
+            finally:
+                m.close()
+            from nert_b200 import model as nbm
+
+            flops = sum(contraction_flops(g, nbm.analyze(g, {k: list(v.shape) for k, v in feeds.items()})).values())
+            t = sum(ms) / len(ms)
+            rows.append({"case": name, "ms": t, "tflops": flops / (t * 1e-3) / 1e12})
+    if args.workload == "sweep":
+        total_ms = sum(r["ms"] for r in rows)
+        line = {"impl": "reference", "device": "reference CudaDevice (cuDNN, cuBLAS) on B200",
+                "metric": metric_for("sweep", args.batch), "value": sum(r["tflops"] * r["ms"] for r in rows) / total_ms,
+                "unit": "TFLOP/s", "ms_per_step": total_ms, "ops": rows}
+    else:
+        t = rows[0]["ms"]
+        line = {"impl": "reference", "device": "reference CudaDevice (cuDNN, cuBLAS) on B200",
+                "metric": metric_for(args.workload, args.batch), "value": args.batch / (t * 1e-3), "unit": UNIT,
+                "ms_per_step": t, "contraction_tflops": rows[0]["tflops"]}
+    line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                 "scaling": "weak", "vs_baseline": None, "dtype": "f32 (cuDNN / cuBLAS FP32)",
+                 "data": "synthetic (seeded inputs and weights, BN folded)",
+                 "config": {"workload": args.workload, "per_gpu_batch": args.batch},
+                 "timing": "nert::Model::RunTyped wall time (host input to host output, a device synchronise "
+                           "after every row, as the reference does)"})
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    if args.ref_device == "cuda":
+        return run_reference_cuda(args)
     from oracle import ref
 
     if not ref.available():

@@ -628,7 +628,8 @@ void gather(nb2_device* dev, const void* x, const int64_t* idx, void* y, int64_t
     check_cuda(cudaGetLastError(), "gather launch");
 }
 
-void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, const void* dev_tables, bool is_f32) {
+void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, const void* dev_tables, bool is_f32,
+            int near2_hint) {
     ResizeDev r{};
     r.rank = t.rank;
     int64_t st = 1, n = 1;
@@ -650,13 +651,17 @@ void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, cons
     const unsigned g = blocks_for(dev, n);
     // nearest, leading axes unchanged: the two-axis gather kernel
     bool near2 = t.rank >= 2 && n < (int64_t(1) << 31) && st < (int64_t(1) << 31);
-    for (double w : t.weight) {
-        near2 = near2 && w == 0.0;
-    }
-    for (int d = 0; near2 && d + 2 < t.rank; ++d) {
-        near2 = t.in_dims[d] == t.out_dims[d];
-        for (int64_t i = 0; near2 && i < t.out_dims[d]; ++i) {
-            near2 = t.lower[t.axis_off[d] + i] == i;
+    if (near2_hint >= 0) {
+        near2 = near2 && near2_hint == 1;
+    } else {
+        for (double w : t.weight) {
+            near2 = near2 && w == 0.0;
+        }
+        for (int d = 0; near2 && d + 2 < t.rank; ++d) {
+            near2 = t.in_dims[d] == t.out_dims[d];
+            for (int64_t i = 0; near2 && i < t.out_dims[d]; ++i) {
+                near2 = t.lower[t.axis_off[d] + i] == i;
+            }
         }
     }
     if (near2) {
@@ -787,7 +792,14 @@ void resize_on_device_tables(nb2_device* dev, const void* x, void* y, const std:
     resize_tables_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, dev->stream>>>(
         a, lower, lower + total, reinterpret_cast<double*>(lower + 2 * total));
     check_cuda(cudaGetLastError(), "resize tables launch");
-    resize(dev, x, y, t, scratch, is_f32);
+    // a nearest resize whose leading axes keep their length at scale 1 maps
+    // them to themselves under every coordinate transform and rounding (an
+    // integer source coordinate rounds to itself): the two-axis kernel
+    int near2 = linear == 0 ? 1 : 0;
+    for (int d = 0; near2 && d + 2 < rank; ++d) {
+        near2 = (in_dims[d] == out_dims[d] && scales[d] == 1.0) ? 1 : 0;
+    }
+    resize(dev, x, y, t, scratch, is_f32, near2);
 }
 
 void cast(nb2_device* dev, const void* x, int from, void* y, int to, int64_t n) {

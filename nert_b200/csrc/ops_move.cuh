@@ -44,7 +44,11 @@ struct ResizeTables {
     std::vector<double> weight;
     std::vector<int64_t> axis_off;     // start of each axis in the tables
 };
-void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, const void* dev_tables, bool is_f32);
+// near2: 1 / 0 when the caller knows whether this is a nearest resize of the
+// last two axes only (every leading axis the identity); -1 = decide from the
+// host copy of the tables in `t`.
+void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, const void* dev_tables, bool is_f32,
+            int near2 = -1);
 
 // Resize with the per-axis tables built on the device into `scratch`
 // (resize_table_bytes(out_dims) bytes) — for callers without host tables.

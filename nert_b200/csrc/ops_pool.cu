@@ -102,6 +102,52 @@ __global__ void row_mean_warp_kernel(const float* __restrict__ x, float* __restr
     }
 }
 
+// Short rows (inner <= 64, e.g. 7x7 = 49): a block stages 128 whole rows
+// (one contiguous span of the input) in shared memory with 16-byte loads, then
+// each thread sums one row in double. Rows of 49 floats break 16-byte
+// alignment row by row, so a warp per row would issue short, misaligned loads.
+constexpr int kMeanRows = 128;
+constexpr int kMeanInner = 64;
+__global__ void __launch_bounds__(kMeanRows) row_mean_staged_kernel(const float* __restrict__ x,
+                                                                    float* __restrict__ y, int64_t rows,
+                                                                    int inner) {
+    __shared__ __align__(16) float sm[kMeanRows * kMeanInner];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kMeanRows;
+    const int64_t left = rows - r0;
+    const int nrows = left < kMeanRows ? static_cast<int>(left) : kMeanRows;
+    const int n = nrows * inner;
+    const float* src = x + r0 * inner;
+    const int n4 = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) ? n / 4 : 0;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(sm);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        d4[i] = __ldg(s4 + i);
+    }
+    for (int i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+        sm[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    if (threadIdx.x < nrows) {
+        const float* row = sm + threadIdx.x * inner;
+        double acc = 0.0;
+        if (inner & 1) {
+            // odd row strides put the lanes on distinct banks: sum in order
+            for (int k = 0; k < inner; ++k) {
+                acc += static_cast<double>(row[k]);
+            }
+        } else {
+            // even strides: lane-rotated start so the lanes spread over banks
+            const int rot = threadIdx.x & 31;
+            for (int k = 0; k < inner; ++k) {
+                int q = k + rot;
+                q = q >= inner ? q - inner : q;
+                acc += static_cast<double>(row[q]);
+            }
+        }
+        y[r0 + threadIdx.x] = static_cast<float>(acc / static_cast<double>(inner));
+    }
+}
+
 // Block per row for long rows.
 __global__ void row_mean_block_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t inner) {
     __shared__ double part[32];
@@ -351,7 +397,11 @@ void row_mean(nb2_device* dev, const float* x, float* y, int64_t rows, int64_t i
     if (rows <= 0 || inner <= 0) {
         return;
     }
-    if (inner <= 1024) {
+    if (inner <= kMeanInner) {
+        const int64_t blocks = (rows + kMeanRows - 1) / kMeanRows;
+        row_mean_staged_kernel<<<static_cast<unsigned>(blocks), kMeanRows, 0, dev->stream>>>(
+            x, y, rows, static_cast<int>(inner));
+    } else if (inner <= 1024) {
         const int64_t blocks = (rows * 32 + 255) / 256;
         row_mean_warp_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, rows, inner);
     } else {

@@ -17,17 +17,21 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_ref", "libnert_ref.so")
+# the same library with the reference's CUDA device (cuDNN/cuBLAS rows), the
+# GPU baseline; built only where nvcc and cuDNN are present
+CUDA_LIB_PATH = os.path.join(HERE, "_ref", "libnert_ref_cuda.so")
 # the reference checkout: NERT_REFERENCE, else a sibling of this repository
 REFERENCE_SRC = os.environ.get("NERT_REFERENCE",
                                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
-_lib = None
+_libs: dict = {}
 _NP = {0: np.float32, 1: np.int64, 2: np.bool_}
 _CODE = {np.dtype(np.float32): 0, np.dtype(np.int64): 1, np.dtype(np.bool_): 2}
 
 
 def build(quiet: bool = True) -> bool:
-    """Compile oracle/_ref from the reference sources when they are present."""
+    """Compile oracle/_ref from the reference sources when they are present
+    (the CPU library, and the CUDA-device library where nvcc and cuDNN are)."""
     if not os.path.isdir(os.path.join(REFERENCE_SRC, "src")):
         return os.path.exists(LIB_PATH)
     out = subprocess.run(["make", "-C", HERE, "-j8", f"REF={REFERENCE_SRC}"], capture_output=True, text=True)
@@ -36,16 +40,18 @@ def build(quiet: bool = True) -> bool:
     return True
 
 
-def available() -> bool:
-    return os.path.exists(LIB_PATH)
+def available(cuda: bool = False) -> bool:
+    return os.path.exists(CUDA_LIB_PATH if cuda else LIB_PATH)
 
 
-def lib():
-    global _lib
-    if _lib is None:
-        if not available():
-            raise RuntimeError(f"reference oracle library missing: {LIB_PATH} (run make -C oracle)")
-        L = ctypes.CDLL(LIB_PATH)
+def lib(cuda: bool = False):
+    """The reference library: CPU only, or (cuda=True) with its CudaDevice."""
+    key = "cuda" if cuda else "cpu"
+    if key not in _libs:
+        path = CUDA_LIB_PATH if cuda else LIB_PATH
+        if not os.path.exists(path):
+            raise RuntimeError(f"reference oracle library missing: {path} (run make -C oracle)")
+        L = ctypes.CDLL(path)
         L.nref_open.restype = ctypes.c_void_p
         L.nref_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
                                 ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
@@ -66,16 +72,26 @@ def lib():
         L.nref_output_copy.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
         L.nref_arena_bytes.restype = ctypes.c_int64
         L.nref_arena_bytes.argtypes = [ctypes.c_void_p]
-        _lib = L
-    return _lib
+        if cuda:
+            L.nref_cuda_device.restype = ctypes.c_void_p
+            L.nref_cuda_device.argtypes = []
+        _libs[key] = L
+    return _libs[key]
 
 
 class RefModel:
     """The reference's nert::Model over an ONNX file, on CpuDevice or on any
     other ``const nert::Device*`` handed in as an integer address."""
 
-    def __init__(self, onnx_path: str, input_dims: dict[str, list[int]], device: int | None = None):
-        L = lib()
+    def __init__(self, onnx_path: str, input_dims: dict[str, list[int]], device: int | None = None,
+                 cuda: bool = False):
+        """cuda=True: the library built with the reference's CudaDevice, and
+        (when `device` is None) that device."""
+        self._L = L = lib(cuda)
+        if cuda and device is None:
+            device = L.nref_cuda_device()
+            if not device:
+                raise RuntimeError("reference CudaDevice unavailable: " + L.nref_last_error(None).decode())
         names = list(input_dims)
         c_names = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
         flat = [d for n in names for d in input_dims[n]]
@@ -87,7 +103,7 @@ class RefModel:
         self.last_ms = 0.0
 
     def run(self, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
-        L = lib()
+        L = self._L
         names = list(inputs)
         arrs = [np.ascontiguousarray(inputs[n]) for n in names]
         c_names = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
@@ -110,11 +126,11 @@ class RefModel:
         return out
 
     def arena_bytes(self) -> int:
-        return lib().nref_arena_bytes(self._h)
+        return self._L.nref_arena_bytes(self._h)
 
     def close(self):
         if self._h:
-            lib().nref_close(self._h)
+            self._L.nref_close(self._h)
             self._h = None
 
     def __del__(self):
@@ -124,14 +140,16 @@ class RefModel:
             pass
 
 
-def run_graph(graph, inputs: dict[str, np.ndarray], device: int | None = None) -> dict[str, np.ndarray]:
+def run_graph(graph, inputs: dict[str, np.ndarray], device: int | None = None,
+              cuda: bool = False) -> dict[str, np.ndarray]:
     """Write ``graph`` (an nert_b200.onnx_io.Graph) to a temp ONNX file and run
-    it once through the reference loader + executor."""
+    it once through the reference loader + executor (cuda=True: on the
+    reference's own CudaDevice)."""
     from nert_b200 import onnx_io
 
     with tempfile.TemporaryDirectory() as d:
         path = onnx_io.save(graph, os.path.join(d, "model.onnx"))
-        m = RefModel(path, {k: list(v.shape) for k, v in inputs.items()}, device)
+        m = RefModel(path, {k: list(v.shape) for k, v in inputs.items()}, device, cuda)
         try:
             return m.run(inputs)
         finally:

@@ -182,3 +182,16 @@ int64_t nref_output_copy(void* handle, int i, void* dst, int64_t cap) {
 int64_t nref_arena_bytes(void* handle) { return static_cast<Session*>(handle)->model->plan().arena_size; }
 
 } // extern "C"
+
+#ifdef NREF_WITH_CUDA
+// The reference's own CUDA device (cuDNN Conv, cuBLAS Gemm/MatMul, its CUDA
+// kernel table), for the GPU baseline: src/cuda_device.cpp:98-102.
+extern "C" const void* nref_cuda_device() {
+    try {
+        return &nert::CudaDevice();
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return nullptr;
+    }
+}
+#endif

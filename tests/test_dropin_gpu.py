@@ -148,3 +148,16 @@ def test_resident_weights_are_packed_once_and_dropped_on_release(b200_device):
             assert rel_err(first, cpu) <= TOL, tag
             outs[tag] = first
     assert np.abs(outs["resnet18"] - outs["other"]).max() > 1e-3
+
+
+@pytest.mark.skipif(not ref.available(cuda=True), reason="reference CUDA library not built")
+def test_reference_cuda_baseline_matches_oracle(cuda):
+    """The GPU baseline (the reference's own CudaDevice: cuDNN Conv, cuBLAS
+    Gemm) agrees with the oracle on ResNet-18, so its timings are of a correct
+    run."""
+    from oracle import np_ref
+
+    g = configs.resnet18(1)
+    x = configs.resnet_input(1)
+    got = ref.run_graph(g, {"input": x}, cuda=True)["fc_out"]
+    assert rel_err(got, np_ref.run(g, {"input": x})["fc_out"]) <= TOL
