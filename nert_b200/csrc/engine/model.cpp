@@ -427,11 +427,30 @@ Model::Model(const uint8_t* onnx, size_t size, const std::map<std::string, std::
             exec_ = nullptr;
         }
         cudaStreamSynchronize(dev_->stream);
+        release_pipeline();
         for (void* p : allocations_) {
             cudaFree(p);
         }
         allocations_.clear();
         throw;
+    }
+}
+
+void Model::release_pipeline() {
+    if (copy_stream_) {
+        cudaStreamSynchronize(copy_stream_);
+        cudaStreamDestroy(copy_stream_);
+        copy_stream_ = nullptr;
+    }
+    for (int k = 0; k < 2; ++k) {
+        if (staged_[k]) {
+            cudaEventDestroy(staged_[k]);
+            staged_[k] = nullptr;
+        }
+        if (freed_[k]) {
+            cudaEventDestroy(freed_[k]);
+            freed_[k] = nullptr;
+        }
     }
 }
 
@@ -441,6 +460,7 @@ Model::~Model() {
         cudaGraphExecDestroy(exec_);
     }
     cudaStreamSynchronize(dev_->stream);
+    release_pipeline();
     for (void* p : allocations_) {
         cudaFree(p);
     }
@@ -1193,13 +1213,49 @@ void Model::enqueue_host(const std::vector<const void*>& in, const std::vector<v
                        std::to_string(outputs_.size()) + " outputs");
     }
     dev_->make_current();
-    for (size_t i = 0; i < in.size(); ++i) {
-        if (inputs_[i].bytes > 0) {
-            check_cuda(cudaMemcpyAsync(inputs_[i].dev, in[i], static_cast<size_t>(inputs_[i].bytes),
-                                       cudaMemcpyHostToDevice, dev_->stream),
-                       "cudaMemcpyAsync(input)");
+    if (copy_stream_ == nullptr) {
+        int64_t total = 0;
+        for (const auto& io : inputs_) {
+            total += align_up(io.bytes);
+        }
+        check_cuda(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking), "cudaStreamCreate(copy)");
+        for (int k = 0; k < 2; ++k) {
+            void* p = nullptr;
+            check_cuda(cudaMalloc(&p, static_cast<size_t>(std::max<int64_t>(total, 256))), "cudaMalloc(staging)");
+            allocations_.push_back(p);
+            stage_[k] = static_cast<uint8_t*>(p);
+            check_cuda(cudaEventCreateWithFlags(&staged_[k], cudaEventDisableTiming), "cudaEventCreate");
+            check_cuda(cudaEventCreateWithFlags(&freed_[k], cudaEventDisableTiming), "cudaEventCreate");
+            check_cuda(cudaEventRecord(freed_[k], dev_->stream), "cudaEventRecord");
         }
     }
+    // host -> staging k on the copy stream, once run pipe_runs_ - 2 has moved
+    // its inputs out of it; this run waits for the copy, moves the inputs into
+    // place and releases the staging buffer
+    const int k = static_cast<int>(pipe_runs_ & 1);
+    check_cuda(cudaStreamWaitEvent(copy_stream_, freed_[k], 0), "cudaStreamWaitEvent");
+    int64_t off = 0;
+    for (size_t i = 0; i < in.size(); ++i) {
+        if (inputs_[i].bytes > 0) {
+            check_cuda(cudaMemcpyAsync(stage_[k] + off, in[i], static_cast<size_t>(inputs_[i].bytes),
+                                       cudaMemcpyHostToDevice, copy_stream_),
+                       "cudaMemcpyAsync(input)");
+        }
+        off += align_up(inputs_[i].bytes);
+    }
+    check_cuda(cudaEventRecord(staged_[k], copy_stream_), "cudaEventRecord");
+    check_cuda(cudaStreamWaitEvent(dev_->stream, staged_[k], 0), "cudaStreamWaitEvent");
+    off = 0;
+    for (size_t i = 0; i < in.size(); ++i) {
+        if (inputs_[i].bytes > 0) {
+            check_cuda(cudaMemcpyAsync(inputs_[i].dev, stage_[k] + off, static_cast<size_t>(inputs_[i].bytes),
+                                       cudaMemcpyDeviceToDevice, dev_->stream),
+                       "cudaMemcpyAsync(stage)");
+        }
+        off += align_up(inputs_[i].bytes);
+    }
+    check_cuda(cudaEventRecord(freed_[k], dev_->stream), "cudaEventRecord");
+    ++pipe_runs_;
     launch();
     for (size_t i = 0; i < out.size(); ++i) {
         if (outputs_[i].bytes > 0) {

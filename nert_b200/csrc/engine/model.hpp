@@ -83,6 +83,16 @@ class Model {
     bool use_graph_ = true;
     cudaGraphExec_t exec_ = nullptr;
     int exec_precision_ = -1;
+    // Host-input pipeline of enqueue_host: the next run's inputs are copied
+    // from host memory into one of two staging buffers on a copy stream, so
+    // the transfer overlaps the run in flight; the run then moves its staged
+    // inputs into the input buffers on the device stream (device-to-device).
+    cudaStream_t copy_stream_ = nullptr;
+    uint8_t* stage_[2] = {nullptr, nullptr};
+    cudaEvent_t staged_[2] = {nullptr, nullptr}; // staging k filled (copy stream)
+    cudaEvent_t freed_[2] = {nullptr, nullptr};  // staging k consumed (device stream)
+    uint64_t pipe_runs_ = 0;
+    void release_pipeline();
 };
 
 } // namespace eng
