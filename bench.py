@@ -397,6 +397,52 @@ def contraction_flops(graph, analysis) -> dict:
     return out
 
 
+def contraction_bytes(graph, analysis) -> dict:
+    """Algorithmic bytes of every Conv / Gemm / MatMul row: its operands read
+    once (activation, weight, a fused residual) and its output written once."""
+    import numpy as np
+
+    t = analysis["tensors"]
+    nodes = {n.name: n for n in graph.nodes}
+    numel = lambda name: (int(np.prod(graph.initializers[name].shape)) if name in graph.initializers
+                          else int(np.prod(t[name]["dims"])))
+    out = {}
+    for e in analysis["exec"]:
+        if e["op"] not in ("Conv", "Gemm", "MatMul"):
+            continue
+        n = nodes[e["name"]]
+        b = numel(n.inputs[0]) + numel(n.inputs[1]) + int(np.prod(t[e["outs"][0]]["dims"]))
+        if e.get("residual"):
+            b += numel(e["residual"])
+        out[e["name"]] = 4.0 * b
+    return out
+
+
+def layer_roofline(sums: dict, flops: dict, nbytes: dict, tensor_peak_tflops: float, hbm_gbs: float) -> dict:
+    """Each contraction row against its own roofline: the slower of its FLOPs
+    at the tensor peak and its bytes at the HBM peak (short-K 1x1 convs are
+    HBM-bound). `frac` = the rows' roofline time / their measured time."""
+    rows, bound_ms, meas_ms, t_ms, h_ms = [], 0.0, 0.0, 0.0, 0.0
+    for lab, ms in sums.items():
+        name = row_name(lab)
+        if name not in flops or ms <= 0:
+            continue
+        tt = flops[name] / (tensor_peak_tflops * 1e12) * 1e3
+        th = nbytes.get(name, 0.0) / (hbm_gbs * 1e9) * 1e3
+        b = max(tt, th)
+        bound_ms += b
+        meas_ms += ms
+        t_ms += tt if tt >= th else 0.0
+        h_ms += th if th > tt else 0.0
+        rows.append([lab, round(ms, 4), round(flops[name] / (ms * 1e-3) / 1e12, 1),
+                     round(nbytes.get(name, 0.0) / (ms * 1e-3) / 1e9, 0), "tensor" if tt >= th else "hbm",
+                     round(b / ms, 3)])
+    rows.sort(key=lambda r: -r[1])
+    return {"frac": bound_ms / meas_ms if meas_ms else None, "rows_ms": meas_ms,
+            "tensor_bound_roofline_ms": t_ms, "hbm_bound_roofline_ms": h_ms,
+            "columns": ["row", "ms", "TFLOP/s", "GB/s", "bound", "frac of its roofline"], "rows": rows[:12]}
+
+
 def hbm_peak() -> tuple[float, str]:
     """Measured HBM copy bandwidth of this pool (MEASURED_PEAKS.json), else the fallback."""
     try:
@@ -835,7 +881,9 @@ def main():
         mean_dev, mean_e2e = float(t[0]), float(t[1])
 
     # roofline of the tensor-core contraction kernel (eager passes, event per row)
-    flops = contraction_flops(graph, nbm.analyze(graph, dims))
+    analysis = nbm.analyze(graph, dims)
+    flops = contraction_flops(graph, analysis)
+    cbytes = contraction_bytes(graph, analysis)
     sums = {}
     reps = 3
     for _ in range(reps):
@@ -894,6 +942,8 @@ def main():
                          "kernel_ms_note": "ms_per_step (timed CUDA-graph replay) x the contraction rows' share "
                                            "of an eager pass with an event between rows",
                          "kernel_ms_eager": tc_eager,
+                         "per_layer": layer_roofline(sums, flops, cbytes, tensor_peak(args.precision)[0],
+                                                     hbm_peak()[0]),
                          "traffic": TRAFFIC_BYTES.get((args.workload, batch)),
                          "traffic_note": "DRAM bytes read+written by the contraction launches of one step, "
                                          "from one ncu capture (profiles/resnet18_b64_igemm_dram.md)"
