@@ -898,6 +898,13 @@ def main():
     tc_time = mean_dev * share
     achieved = tc_flop / (tc_time * 1e-3) / 1e12 if tc_time > 0 else None
     top_rows = sorted(sums.items(), key=lambda kv: -kv[1])[:5]
+    by_op = {}
+    for lab, ms in sums.items():
+        op = lab.split(":", 1)[0]
+        if "MatMul" in op:  # attention products apart from the linear layers
+            nm = row_name(lab)
+            op += " (attention)" if (".qk" in nm or ".av" in nm or "attn" in nm) else ""
+        by_op[op] = round(by_op.get(op, 0.0) + ms, 4)
     rows_table = bandwidth_rows(local) if (rank == 0 and world == 1 and not args.no_rows) else None
 
     line = None
@@ -949,6 +956,7 @@ def main():
                                          "from one ncu capture (profiles/resnet18_b64_igemm_dram.md)"
                          if (args.workload, batch) in TRAFFIC_BYTES else None},
             "top_rows_ms": [[lab, round(ms, 4)] for lab, ms in top_rows],
+            "profile_ms_by_op": by_op,
             "bandwidth_rows": rows_table,
             "clocks": clk,
             "gpu_launches": int(stats["kernels_per_run"]) * args.steps * world,
