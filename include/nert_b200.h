@@ -137,6 +137,28 @@ int nb2_conv2d_pack(nb2_device* dev, const nb2_conv_geom* g, const float* w, voi
 int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* x, const void* packed,
                           const float* bias, const float* residual, int act, float* y);
 
+/* ConvTranspose geometry, NCHW: x [n,c,h,w], w [c, m/group, kh, kw],
+ * y [n,m,oh,ow] with oh = stride_h*(h-1) + out_pad_h + dil_h*(kh-1) + 1 -
+ * pad_top - pad_bottom (and the same for the width). */
+typedef struct nb2_convt_geom {
+    int64_t n, c, h, w;
+    int64_t m, kh, kw;
+    int64_t oh, ow;
+    int64_t stride_h, stride_w;
+    int64_t pad_top, pad_left, pad_bottom, pad_right;
+    int64_t dil_h, dil_w;
+    int64_t out_pad_h, out_pad_w;
+    int64_t group;
+} nb2_convt_geom;
+
+/* ConvTranspose row: src/kernels/conv_transpose.cpp (explicit pads,
+ * output_padding, dilations, groups, optional bias [m]), computed as a
+ * stride-1 Conv on the tensor cores over the input with stride-1 zeros
+ * inserted, with the weight transposed per group and flipped. Pads above
+ * dil*(k-1) are NB2_ERR_UNSUPPORTED. Scratch comes from the device workspace. */
+int nb2_conv_transpose2d(nb2_device* dev, const nb2_convt_geom* g, const float* x, const float* w, const float* bias,
+                         float* y);
+
 /* Conv for callers that cannot allocate device memory (no counterpart in the
  * reference). Same semantics and validation as nb2_conv2d, but the weight is
  * packed into a fixed 8 MiB static device array (per GPU, held until exit)
@@ -185,6 +207,11 @@ int nb2_binary(nb2_device* dev, int op, int dtype, const void* a, const int64_t*
 /* MaxPool 2-D (src/kernels/max_pool.cpp:138-239): x [n,c,h,w] -> y [n,c,oh,ow]. */
 int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
                   const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4], const int64_t dilations[2]);
+/* AveragePool 2-D (src/kernels/average_pool.cpp:128-225): x [n,c,h,w] ->
+ * y [n,c,oh,ow], explicit pads {top, left, bottom, right}; the divisor counts
+ * the padded window when count_include_pad, else the in-range taps. */
+int nb2_avgpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
+                  const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4], int count_include_pad);
 /* Mean over the trailing `inner` elements of `rows` rows, double accumulation
  * (GlobalAveragePool, src/kernels/global_average_pool.cpp:32-68). */
 int nb2_row_mean(nb2_device* dev, const float* x, int64_t rows, int64_t inner, float* y);
@@ -212,7 +239,7 @@ int nb2_slice(nb2_device* dev, const void* x, void* y, const int64_t* in_dims, c
 int nb2_gather(nb2_device* dev, const void* x, const int64_t* indices, void* y, int64_t outer, int64_t axis_len,
                int64_t inner, int64_t n_indices, int elem_bytes);
 /* TopK largest/sorted along the last axis of [rows, len] (src/kernels/top_k.cpp:53-142):
- * values and int64 indices ordered by (value desc, index asc); k <= 1024. */
+ * values and int64 indices ordered by (value desc, index asc); any k <= len. */
 int nb2_topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t len, int64_t k);
 /* Resize nearest/linear (src/kernels/resize.cpp:162-): mode 0 nearest, 1 linear;
  * transform 0 half_pixel, 1 pytorch_half_pixel, 2 align_corners, 3 asymmetric;

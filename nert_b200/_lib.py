@@ -35,6 +35,12 @@ class ConvGeom(ctypes.Structure):
         "pad_top", "pad_left", "pad_bottom", "pad_right", "dil_h", "dil_w", "group")]
 
 
+class ConvTGeom(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int64) for n in (
+        "n", "c", "h", "w", "m", "kh", "kw", "oh", "ow", "stride_h", "stride_w", "pad_top", "pad_left",
+        "pad_bottom", "pad_right", "dil_h", "dil_w", "out_pad_h", "out_pad_w", "group")]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "nb2_last_error": (ctypes.c_char_p, []),
@@ -60,6 +66,7 @@ _SIGS = {
     "nb2_conv2d_packed_size": (ctypes.c_int, [ctypes.POINTER(ConvGeom), c_i64p]),
     "nb2_conv2d_pack": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp]),
     "nb2_conv2d_run_packed": (ctypes.c_int, [vp, ctypes.POINTER(ConvGeom), vp, vp, vp, vp, ctypes.c_int, vp]),
+    "nb2_conv_transpose2d": (ctypes.c_int, [vp, ctypes.POINTER(ConvTGeom), vp, vp, vp, vp]),
     "nb2_gemm": (ctypes.c_int, [vp, vp, vp, vp, ctypes.c_int, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                 ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int]),
     "nb2_gemm_packed_size": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, c_i64p]),
@@ -72,6 +79,7 @@ _SIGS = {
     "nb2_binary": (ctypes.c_int, [vp, ctypes.c_int, ctypes.c_int, vp, c_i64p, ctypes.c_int, vp, c_i64p, ctypes.c_int,
                                   vp, c_i64p, ctypes.c_int]),
     "nb2_maxpool2d": (ctypes.c_int, [vp, vp, c_i64p, vp, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p]),
+    "nb2_avgpool2d": (ctypes.c_int, [vp, vp, c_i64p, vp, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_int]),
     "nb2_row_mean": (ctypes.c_int, [vp, vp, ctypes.c_int64, ctypes.c_int64, vp]),
     "nb2_softmax": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
     "nb2_layernorm": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_float]),

@@ -23,9 +23,10 @@ from .onnx_io import FLOAT, Graph
 
 
 class _Builder:
-    def __init__(self, config: str, opset: int = 13):
+    def __init__(self, config: str, opset: int = 13, bn_nodes: bool = False):
         self.config = config
         self.g = Graph(name=config, opset=opset)
+        self.bn_nodes = bn_nodes
 
     def seed(self, name: str) -> int:
         return synth.seed_of(self.config, name)
@@ -36,6 +37,15 @@ class _Builder:
         fan_in = (cin // groups) * k * k
         w = synth.normal((cout, cin // groups, k, k), math.sqrt(2.0 / fan_in), self.seed(name + ".w"))
         var = synth.uniform((cout,), 0.5, 1.5, self.seed(name + ".bn_var"))
+        if self.bn_nodes:
+            # the unfolded export: Conv without bias, then BatchNormalization
+            # (gamma 1, beta 0, mean 0, the seeded variance, epsilon 1e-5)
+            y = self.g.op("Conv", [x, self.g.const(name + ".weight", w)], name=name, kernel_shape=[k, k],
+                          strides=[stride, stride], pads=[pad, pad, pad, pad], dilations=[1, 1], group=groups)
+            stats = [self.g.const(name + ".bn_" + t, v) for t, v in
+                     (("scale", np.ones((cout,), np.float32)), ("bias", np.zeros((cout,), np.float32)),
+                      ("mean", np.zeros((cout,), np.float32)), ("var", var))]
+            return self.g.op("BatchNormalization", [y] + stats, name=name + ".bn", epsilon=1e-5)
         scale = (1.0 / np.sqrt(var.astype(np.float64) + 1e-5)).astype(np.float32)
         w = (w * scale[:, None, None, None]).astype(np.float32)
         b = np.zeros((cout,), np.float32)
@@ -48,9 +58,11 @@ class _Builder:
         return self.g.op("Relu", [x], name=name)
 
 
-def resnet18(batch: int = 1, config: str = "resnet18") -> Graph:
-    """torchvision-style ResNet-18 (BasicBlock 2/2/2/2, widths 64-512)."""
-    return _resnet(batch, config, bottleneck=False, blocks=(2, 2, 2, 2))
+def resnet18(batch: int = 1, config: str = "resnet18", bn_nodes: bool = False) -> Graph:
+    """torchvision-style ResNet-18 (BasicBlock 2/2/2/2, widths 64-512).
+    bn_nodes=True keeps every BatchNormalization as a node after its Conv (an
+    export without the fold); the same seeds give the folded graph's values."""
+    return _resnet(batch, config, bottleneck=False, blocks=(2, 2, 2, 2), bn_nodes=bn_nodes)
 
 
 def resnet50(batch: int = 1, config: str = "resnet50", softmax: bool = True, expose_logits: bool = False) -> Graph:
@@ -63,8 +75,8 @@ def resnet50(batch: int = 1, config: str = "resnet50", softmax: bool = True, exp
 
 
 def _resnet(batch: int, config: str, bottleneck: bool, blocks, softmax: bool = False,
-            expose_logits: bool = False) -> Graph:
-    b = _Builder(config)
+            expose_logits: bool = False, bn_nodes: bool = False) -> Graph:
+    b = _Builder(config, bn_nodes=bn_nodes)
     g = b.g
     x = g.add_input("input", [batch, 3, 224, 224])
     y = b.relu(b.conv_bn(x, 3, 64, 7, 2, 3, name="conv1"), "relu1")

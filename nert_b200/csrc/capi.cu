@@ -346,6 +346,50 @@ int nb2_conv2d(nb2_device* dev, const nb2_conv_geom* g, const float* x, const fl
     });
 }
 
+int nb2_conv_transpose2d(nb2_device* dev, const nb2_convt_geom* c, const float* x, const float* w,
+                         const float* bias, float* y) {
+    return guard([&] {
+        need(c != nullptr, "ConvTranspose: null geometry");
+        // the reference row's checks (src/kernels/conv_transpose.cpp:78-145)
+        need(c->n > 0 && c->c > 0 && c->h > 0 && c->w > 0 && c->m > 0 && c->kh > 0 && c->kw > 0,
+             "ConvTranspose: non-positive dimension");
+        need(c->group > 0 && c->c % c->group == 0 && c->m % c->group == 0,
+             "ConvTranspose: weight channels do not match the input and group");
+        need(c->stride_h > 0 && c->stride_w > 0 && c->dil_h > 0 && c->dil_w > 0,
+             "ConvTranspose: strides and dilations must be positive");
+        need(c->pad_top >= 0 && c->pad_left >= 0 && c->pad_bottom >= 0 && c->pad_right >= 0 && c->out_pad_h >= 0 &&
+                 c->out_pad_w >= 0,
+             "ConvTranspose: pads and output_padding must be non-negative");
+        const int64_t oh = c->stride_h * (c->h - 1) + c->out_pad_h + c->dil_h * (c->kh - 1) + 1 - c->pad_top -
+                           c->pad_bottom;
+        const int64_t ow = c->stride_w * (c->w - 1) + c->out_pad_w + c->dil_w * (c->kw - 1) + 1 - c->pad_left -
+                           c->pad_right;
+        need(oh > 0 && ow > 0 && oh == c->oh && ow == c->ow, "ConvTranspose: output shape does not match the transposed window");
+        need(x != nullptr && w != nullptr && y != nullptr, "ConvTranspose: null buffer");
+        bind(dev);
+        const ConvTGeom t{c->n, c->c, c->h, c->w, c->m, c->kh, c->kw, c->oh, c->ow, c->stride_h, c->stride_w,
+                          c->pad_top, c->pad_left, c->pad_bottom, c->pad_right, c->dil_h, c->dil_w,
+                          c->out_pad_h, c->out_pad_w, c->group};
+        const ConvGeom g = nchw_input_layout(convt_as_conv(t));
+        auto al = [](size_t v) { return (v + 255) & ~size_t(255); };
+        const size_t zb = al(convt_zero_insert_bytes(t));
+        const size_t wb = al(static_cast<size_t>(t.M * (t.C / t.group) * t.KH * t.KW * 4));
+        const size_t pb = al(conv_packed_bytes(g));
+        uint8_t* ws = static_cast<uint8_t*>(dev->scratch(zb + wb + pb + nhwc_copy_bytes(g)));
+        float* w2 = reinterpret_cast<float*>(ws + zb);
+        convt_flip_weights(dev, t, w, w2);
+        conv_pack(dev, g, w2, ws + zb + wb);
+        const float* src = x;
+        if (zb > 0) {
+            convt_zero_insert(dev, t, x, reinterpret_cast<float*>(ws));
+            src = reinterpret_cast<const float*>(ws);
+        }
+        Epilogue ep;
+        ep.bias = bias;
+        run_nchw_conv(dev, g, src, ws + zb + wb, y, ep, ws + zb + wb + pb);
+    });
+}
+
 int nb2_gemm(nb2_device* dev, const float* a, const float* b, const float* c, int c_rank, float* y, int64_t m,
              int64_t n, int64_t k, int trans_a, int trans_b, float alpha, float beta, int act) {
     return guard([&] {
@@ -533,6 +577,24 @@ int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], floa
         need(x != nullptr && y != nullptr, "MaxPool: null buffer");
         bind(dev);
         maxpool2d(dev, g, x, y);
+    });
+}
+
+int nb2_avgpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
+                  const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4], int count_include_pad) {
+    return guard([&] {
+        need(x_dims != nullptr && y_dims != nullptr && kernel != nullptr && strides != nullptr && pads != nullptr,
+             "AveragePool: null argument");
+        AvgPoolGeom g{x_dims[0], x_dims[1], x_dims[2], x_dims[3], y_dims[2], y_dims[3], kernel[0], kernel[1],
+                      strides[0], strides[1], pads[0], pads[1], pads[2], pads[3], count_include_pad ? 1 : 0};
+        need(g.N > 0 && g.C > 0 && g.H > 0 && g.W > 0, "AveragePool: non-positive dimension");
+        need(g.KH > 0 && g.KW > 0 && g.sh > 0 && g.sw > 0, "AveragePool: kernel and stride must be positive");
+        need(g.pt >= 0 && g.pl >= 0 && g.pb >= 0 && g.pr >= 0, "AveragePool: pads must be non-negative");
+        need(y_dims[0] == g.N && y_dims[1] == g.C && g.OH > 0 && g.OW > 0,
+             "AveragePool: output shape does not match the pooling window");
+        need(x != nullptr && y != nullptr, "AveragePool: null buffer");
+        bind(dev);
+        avgpool2d(dev, g, x, y);
     });
 }
 

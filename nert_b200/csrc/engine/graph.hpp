@@ -100,6 +100,11 @@ struct Graph {
 // src/model_loader.cpp:2020-2284). Constant nodes become constants.
 Graph parse_onnx(const uint8_t* data, size_t size);
 
+// Inference BatchNormalization with constant statistics: folded into the
+// producing Conv where it is that output's only use, else kept as a
+// three-input node (input, per-channel scale, per-channel shift).
+void fold_batchnorm(Graph& g);
+
 // Static shapes for one concrete input shape (reference InferShapes,
 // src/shape_inference.cpp:3022). Returns the table for every tensor.
 std::map<std::string, TensorInfo> infer_shapes(const Graph& g, const std::map<std::string, std::vector<int64_t>>& input_dims);

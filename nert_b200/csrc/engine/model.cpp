@@ -1043,6 +1043,104 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             } else {
                 st.run = [=] { maxpool2d(dev, pg, x, y); };
             }
+        } else if (e.op == "ConvTranspose") {
+            // a stride-1 Conv over the zero-inserted input (ops_convt.cu); the
+            // weight is transposed, flipped and packed once here
+            const auto& xd = dims(n.inputs[0]);
+            const auto& wd = dims(n.inputs[1]);
+            const auto& yd = dims(n.outputs[0]);
+            auto list = [&](const char* k, int64_t def, size_t len) {
+                std::vector<int64_t> v = n.getints(k);
+                if (v.empty() || (std::string(k) == "pads" && n.gets("auto_pad", "NOTSET") == "VALID")) {
+                    v.assign(len, def);
+                }
+                return v;
+            };
+            const auto s2 = list("strides", 1, 2), d2 = list("dilations", 1, 2), op2 = list("output_padding", 0, 2),
+                       p4 = list("pads", 0, 4);
+            const int64_t grp = n.geti("group", 1);
+            const ConvTGeom t{xd[0], xd[1], xd[2], xd[3], wd[1] * grp, wd[2], wd[3], yd[2], yd[3], s2[0], s2[1],
+                              p4[0], p4[1], p4[2], p4[3], d2[0], d2[1], op2[0], op2[1], grp};
+            ConvGeom geom = convt_as_conv(t);
+            if ((flags & kNchwOnly) == 0) {
+                geom = nchw_input_layout(geom);
+            }
+            if (!g_.constants.count(n.inputs[1])) {
+                throw LoadError(n.where() + ": the weight must be a constant on B200");
+            }
+            const Constant& wc = g_.constants.at(n.inputs[1]);
+            const int64_t pbytes = static_cast<int64_t>(conv_packed_bytes(geom));
+            uint8_t* packed = dmalloc(align_up(pbytes));
+            void* tmp = nullptr;
+            check_cuda(cudaMalloc(&tmp, 2 * wc.bytes.size()), "cudaMalloc(weight staging)");
+            check_cuda(cudaMemcpyAsync(tmp, wc.bytes.data(), wc.bytes.size(), cudaMemcpyHostToDevice, dev_->stream),
+                       "cudaMemcpyAsync(weight)");
+            float* w2 = reinterpret_cast<float*>(static_cast<uint8_t*>(tmp) + wc.bytes.size());
+            convt_flip_weights(dev_, t, static_cast<const float*>(tmp), w2);
+            conv_pack(dev_, geom, w2, packed);
+            check_cuda(cudaStreamSynchronize(dev_->stream), "pack sync");
+            cudaFree(tmp);
+            weight_bytes_ += pbytes;
+            const size_t zb = convt_zero_insert_bytes(t);
+            float* xz = zb ? reinterpret_cast<float*>(dmalloc(align_up(static_cast<int64_t>(zb)))) : nullptr;
+            if (geom.cvec || geom.cpad) {
+                xform_need = std::max(xform_need, geom.N * geom.Cin() * geom.H * geom.W * 4);
+            }
+            Epilogue ep;
+            ep.bias = n.inputs.size() > 2 && !n.inputs[2].empty() ? F(n.inputs[2]) : nullptr;
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            void** xp = &xform_;
+            st.launches = contraction_launches(dev_, geom.N * geom.OH * geom.OW, geom.Mg(), geom.K(), geom.group) +
+                          (zb ? 1 : 0) + ((geom.cvec || geom.cpad) ? 1 : 0);
+            st.run = [=] {
+                const float* src = x;
+                if (xz) {
+                    convt_zero_insert(dev, t, x, xz);
+                    src = xz;
+                }
+                if (geom.cvec || geom.cpad) {
+                    nchw_to_nhwc_pad(dev, src, static_cast<float*>(*xp), geom.N, geom.C, geom.H, geom.W, geom.Cin());
+                    conv_run(dev, geom, static_cast<const float*>(*xp), packed, y, ep);
+                } else {
+                    conv_run(dev, geom, src, packed, y, ep);
+                }
+            };
+        } else if (e.op == "BatchNormalization") {
+            // a BN the load-time fold could not merge into a Conv
+            const auto& xd = dims(n.inputs[0]);
+            int64_t inner = 1;
+            for (size_t d = 2; d < xd.size(); ++d) {
+                inner *= xd[d];
+            }
+            const int64_t outer = xd[0], C = xd[1];
+            const float* x = F(n.inputs[0]);
+            const float* a = F(n.inputs[1]);
+            const float* sh = F(n.inputs[2]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { channel_affine(dev, x, a, sh, y, outer, C, inner); };
+        } else if (e.op == "AveragePool") {
+            const auto& xd = dims(n.inputs[0]);
+            const auto& yd = dims(n.outputs[0]);
+            std::vector<int64_t> k = n.getints("kernel_shape"), s = n.getints("strides"), pads = n.getints("pads");
+            if (s.empty()) {
+                s = {1, 1};
+            }
+            if (pads.empty()) {
+                pads = {0, 0, 0, 0};
+            }
+            if (n.gets("auto_pad", "NOTSET") != "NOTSET") {
+                throw LoadError(n.where() + ": auto_pad is not supported on B200");
+            }
+            const AvgPoolGeom ag{xd[0], xd[1], xd[2], xd[3], yd[2], yd[3], k[0], k[1], s[0], s[1],
+                                 pads[0], pads[1], pads[2], pads[3],
+                                 n.geti("count_include_pad", 0) != 0 ? 1 : 0};
+            const float* x = F(n.inputs[0]);
+            float* y = F(n.outputs[0]);
+            nb2_device* dev = dev_;
+            st.run = [=] { avgpool2d(dev, ag, x, y); };
         } else if (e.op == "GlobalAveragePool" || e.op == "ReduceMean") {
             const auto& xd = dims(n.inputs[0]);
             int64_t rows = 1, inner = 1;

@@ -489,6 +489,7 @@ Graph parse_onnx(const uint8_t* data, size_t size) {
     if (g.nodes.empty()) {
         throw LoadError("graph has no nodes");
     }
+    fold_batchnorm(g);
     return g;
 }
 

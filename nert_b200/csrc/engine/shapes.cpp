@@ -118,6 +118,46 @@ std::vector<TensorInfo> infer_node(Ctx& c, const Node& n, int64_t opset) {
         out.insert(out.end(), o.begin(), o.end());
         return {TensorInfo{DType::F32, out}};
     }
+    if (op == "ConvTranspose") {
+        // src/kernels/conv_transpose.cpp: s*(in-1) + output_padding + d*(k-1) + 1 - pads
+        const TensorInfo& x = c.in(n, 0);
+        const TensorInfo& w = c.in(n, 1);
+        if (x.dims.size() != 4 || w.dims.size() != 4) {
+            fail(n, "input and weight must be rank 4 (NCHW)");
+        }
+        if (n.has("output_shape")) {
+            fail(n, "output_shape is not supported");
+        }
+        const std::string ap = n.gets("auto_pad", "NOTSET");
+        if (ap != "NOTSET" && ap != "VALID") {
+            fail(n, "auto_pad " + ap + " is not supported");
+        }
+        auto list = [&](const char* k, int64_t def, size_t len) {
+            std::vector<int64_t> v = n.getints(k);
+            if (v.empty() || (std::string(k) == "pads" && ap == "VALID")) {
+                v.assign(len, def);
+            }
+            if (v.size() != len) {
+                fail(n, std::string(k) + " has the wrong length");
+            }
+            return v;
+        };
+        const auto s = list("strides", 1, 2), d = list("dilations", 1, 2), op2 = list("output_padding", 0, 2),
+                   p = list("pads", 0, 4);
+        const int64_t g = n.geti("group", 1);
+        if (g <= 0 || x.dims[1] % g != 0 || w.dims[0] != x.dims[1]) {
+            fail(n, "weight channels do not match the input and group");
+        }
+        std::vector<int64_t> out = {x.dims[0], w.dims[1] * g};
+        for (int i = 0; i < 2; ++i) {
+            const int64_t o = s[i] * (x.dims[2 + i] - 1) + op2[i] + d[i] * (w.dims[2 + i] - 1) + 1 - p[i] - p[2 + i];
+            if (o <= 0) {
+                fail(n, "computes a non-positive output dimension");
+            }
+            out.push_back(o);
+        }
+        return {TensorInfo{DType::F32, out}};
+    }
     if (op == "MaxPool" || op == "AveragePool") {
         const TensorInfo& x = c.in(n, 0);
         if (x.dims.size() != 4) {
@@ -126,6 +166,14 @@ std::vector<TensorInfo> infer_node(Ctx& c, const Node& n, int64_t opset) {
         std::vector<int64_t> in_sp(x.dims.begin() + 2, x.dims.end()), o;
         window(n, in_sp, n.getints("kernel_shape"), o, n.geti("ceil_mode", 0) != 0);
         return {TensorInfo{DType::F32, {x.dims[0], x.dims[1], o[0], o[1]}}};
+    }
+    if (op == "BatchNormalization") {
+        // after fold_batchnorm: (input, per-channel scale, per-channel shift)
+        const TensorInfo& x = c.in(n, 0);
+        if (x.dims.size() < 2) {
+            fail(n, "input must have batch and channel axes");
+        }
+        return {TensorInfo{DType::F32, x.dims}};
     }
     if (op == "GlobalAveragePool") {
         const TensorInfo& x = c.in(n, 0);

@@ -69,6 +69,19 @@ struct ConvGeom {
 
 int64_t round_up(int64_t v, int64_t m);
 
+// ConvTranspose geometry (NCHW): x [N,C,H,W], w [C, M/group, KH, KW],
+// y [N,M,OH,OW]; begin pads (ph, pw), end pads (pb, pr), output_padding
+// (oph, opw).
+struct ConvTGeom {
+    int64_t N, C, H, W, M, KH, KW, OH, OW, sh, sw, ph, pw, pb, pr, dh, dw, oph, opw, group;
+};
+// The stride-1 Conv over the zero-inserted input that equals it (ops_convt.cu).
+ConvGeom convt_as_conv(const ConvTGeom& t);
+size_t convt_zero_insert_bytes(const ConvTGeom& t); // 0 when both strides are 1
+void convt_zero_insert(nb2_device* dev, const ConvTGeom& t, const float* x, float* xz);
+// w [C, M/group, KH, KW] -> w2 [M, C/group, KH, KW], transposed per group and flipped.
+void convt_flip_weights(nb2_device* dev, const ConvTGeom& t, const float* w, float* w2);
+
 // The layout a Conv over an NCHW input runs in once that input is converted
 // to NHWC in front of the contraction (group 1 only): up to 16 channels
 // padded to 4, 8 or 16 (each filter tap one to four 16-byte loads); a spatial

@@ -32,6 +32,10 @@ enum Dtype : int { kF32 = 0, kI64 = 1, kBool = 2 };
 constexpr int kMaxRank = 8;
 
 void unary(nb2_device* dev, int op, const float* x, float* y, int64_t n);
+// y[o][c][i] = x[o][c][i] * a[c] + b[c] over an [outer, C, inner] view: an
+// inference BatchNormalization whose scale and shift were folded on the host.
+void channel_affine(nb2_device* dev, const float* x, const float* a, const float* b, float* y, int64_t outer,
+                    int64_t C, int64_t inner);
 // y = a (op) b with NumPy broadcasting; a/b/y dims given explicitly.
 void binary(nb2_device* dev, int op, int dtype, const void* a, const std::vector<int64_t>& ad, const void* b,
             const std::vector<int64_t>& bd, void* y, const std::vector<int64_t>& yd);
@@ -41,6 +45,13 @@ struct PoolGeom {
     int64_t N, C, H, W, OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
 };
 void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
+// AveragePool 2-D (src/kernels/average_pool.cpp): begin pads (pt, pl), end
+// pads (pb, pr); include_pad selects count_include_pad.
+struct AvgPoolGeom {
+    int64_t N, C, H, W, OH, OW, KH, KW, sh, sw, pt, pl, pb, pr;
+    int include_pad;
+};
+void avgpool2d(nb2_device* dev, const AvgPoolGeom& g, const float* x, float* y);
 // The same window over channels-last x[N][H][W][C] -> y[N][OH][OW][C].
 void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
 // y[n][c] = mean over the hw pixels of channels-last x[n][hw][c]

@@ -335,4 +335,26 @@ void copy(nb2_device* dev, const void* src, void* dst, int64_t bytes) {
                "cudaMemcpyAsync(D2D)");
 }
 
+namespace {
+__global__ void channel_affine_kernel(const float* __restrict__ x, const float* __restrict__ a,
+                                      const float* __restrict__ b, float* __restrict__ y, int64_t C, int64_t inner,
+                                      int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = (i / inner) % C;
+        y[i] = fmaf(__ldg(x + i), __ldg(a + c), __ldg(b + c));
+    }
+}
+} // namespace
+
+void channel_affine(nb2_device* dev, const float* x, const float* a, const float* b, float* y, int64_t outer,
+                    int64_t C, int64_t inner) {
+    const int64_t total = outer * C * inner;
+    if (total == 0) {
+        return;
+    }
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
+    channel_affine_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, a, b, y, C, inner, total);
+    check_cuda(cudaGetLastError(), "channel_affine launch");
+}
+
 } // namespace nb2

@@ -368,6 +368,45 @@ void mean_nhwc(nb2_device* dev, const float* x, float* y, int64_t n, int64_t hw,
     check_cuda(cudaGetLastError(), "mean_nhwc launch");
 }
 
+namespace {
+
+// One thread per output, NCHW. Same window clipping, float summation order
+// (rows, then columns) and divisor as the reference row
+// (src/kernels/average_pool.cpp:198-225), so results are bit-identical.
+__global__ void avgpool2d_kernel(const float* __restrict__ x, float* __restrict__ y, AvgPoolGeom g, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t ow = i % g.OW;
+        int64_t t = i / g.OW;
+        const int64_t oh = t % g.OH;
+        t /= g.OH; // n * C + c
+        const float* xc = x + t * g.H * g.W;
+        const int64_t hs = oh * g.sh - g.pt, he = min(hs + g.KH, g.H + g.pb);
+        const int64_t ws = ow * g.sw - g.pl, we = min(ws + g.KW, g.W + g.pr);
+        const int64_t h0 = hs > 0 ? hs : 0, h1 = min(he, g.H);
+        const int64_t w0 = ws > 0 ? ws : 0, w1 = min(we, g.W);
+        float sum = 0.0f;
+        for (int64_t ih = h0; ih < h1; ++ih) {
+            for (int64_t iw = w0; iw < w1; ++iw) {
+                sum += __ldg(xc + ih * g.W + iw);
+            }
+        }
+        const int64_t div = g.include_pad ? (he - hs) * (we - ws) : (h1 - h0) * (w1 - w0);
+        y[i] = div > 0 ? sum / static_cast<float>(div) : 0.0f;
+    }
+}
+
+} // namespace
+
+void avgpool2d(nb2_device* dev, const AvgPoolGeom& g, const float* x, float* y) {
+    const int64_t total = g.N * g.C * g.OH * g.OW;
+    if (total == 0) {
+        return;
+    }
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
+    avgpool2d_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
+    check_cuda(cudaGetLastError(), "avgpool launch");
+}
+
 void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {
     const int64_t total = g.N * g.C * g.OH * g.OW;
     if (total <= 0) {

@@ -443,6 +443,40 @@ __global__ void __launch_bounds__(kThreads) topk_sort_kernel(const float* __rest
 }
 
 
+// grid (ceil(k / 256), rows), 256 threads: K above kMaxK. Each thread places
+// one of the row's k candidates at its rank in (key desc, index asc) order,
+// counting the candidates that precede it (staged through shared memory).
+__global__ void __launch_bounds__(256) topk_rank_kernel(const float* __restrict__ x, int64_t L, int k,
+                                                         const uint32_t* __restrict__ cand_key,
+                                                         const int64_t* __restrict__ cand_idx,
+                                                         float* __restrict__ values, int64_t* __restrict__ indices) {
+    __shared__ uint32_t sk[1024];
+    __shared__ int64_t si[1024];
+    const int64_t row = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t* ck = cand_key + row * k;
+    const int64_t* ci = cand_idx + row * k;
+    const uint32_t mk = i < k ? ck[i] : 0u;
+    const int64_t mi = i < k ? ci[i] : 0;
+    int rank = 0;
+    for (int base = 0; base < k; base += 1024) {
+        const int n = min(1024, k - base);
+        __syncthreads();
+        for (int q = threadIdx.x; q < n; q += blockDim.x) {
+            sk[q] = ck[base + q];
+            si[q] = ci[base + q];
+        }
+        __syncthreads();
+        for (int q = 0; q < n; ++q) {
+            rank += (sk[q] > mk || (sk[q] == mk && si[q] < mi)) ? 1 : 0;
+        }
+    }
+    if (i < k) {
+        values[row * k + rank] = x[row * L + mi];
+        indices[row * k + rank] = mi;
+    }
+}
+
 // ---- sampled-threshold path for long rows --------------------------------------
 //
 // One read of the row instead of five: a threshold t is taken from a sample
@@ -766,7 +800,7 @@ TopkScratch topk_layout(void* base, int64_t rows, int64_t L, int64_t k) {
 } // namespace
 
 size_t topk_scratch_bytes(int64_t rows, int64_t L, int64_t k) {
-    if (L < kSplitMin) {
+    if (L < kSplitMin && k <= kMaxK) {
         return 0;
     }
     return topk_layout(nullptr, rows, L, k).total;
@@ -776,9 +810,6 @@ void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int6
           void* scratch) {
     if (rows == 0 || k == 0) {
         return;
-    }
-    if (k > kMaxK) {
-        fail(kStatusUnsupported, "TopK: K above 1024 is not supported on B200");
     }
     if (k > L) {
         fail(kStatusInvalid, "TopK: K is larger than the axis");
@@ -790,7 +821,10 @@ void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int6
     while (sort_n < k) {
         sort_n <<= 1;
     }
-    if (L < kSplitMin) {
+    if (k >= (int64_t(1) << 30)) {
+        fail(kStatusUnsupported, "TopK: K too large");
+    }
+    if (L < kSplitMin && k <= kMaxK) {
         topk_row_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, values, indices, L,
                                                                                    static_cast<int>(k), sort_n);
         check_cuda(cudaGetLastError(), "topk launch");
@@ -824,8 +858,14 @@ void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int6
     topk_eqcount_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, t.hist, t.eq_counts, chunks, done);
     topk_collect_kernel<<<grid, 512, 0, dev->stream>>>(x, L, ki, t.hist, t.eq_counts, chunks, t.gt_count, t.cand_key,
                                                        t.cand_idx, done);
-    topk_sort_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, ki, sort_n, t.cand_key,
-                                                                                t.cand_idx, values, indices, done);
+    if (k <= kMaxK) {
+        topk_sort_kernel<<<static_cast<unsigned>(rows), kThreads, 0, dev->stream>>>(x, L, ki, sort_n, t.cand_key,
+                                                                                    t.cand_idx, values, indices, done);
+    } else {
+        // the sampled path never takes K above kSampledMaxK, so every row is here
+        const dim3 rgrid(static_cast<unsigned>((k + 255) / 256), static_cast<unsigned>(rows));
+        topk_rank_kernel<<<rgrid, 256, 0, dev->stream>>>(x, L, ki, t.cand_key, t.cand_idx, values, indices);
+    }
     check_cuda(cudaGetLastError(), "topk launch");
 }
 

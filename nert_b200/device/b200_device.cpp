@@ -363,6 +363,70 @@ void Conv(const Node& node, const std::vector<TensorView>& in, const std::vector
           ctx);
 }
 
+// ConvTranspose (src/kernels/conv_transpose.cpp:76-145): explicit pads
+// (auto_pad NOTSET or VALID), output_padding, dilations, groups, bias [M].
+void ConvTranspose(const Node& node, const std::vector<TensorView>& in, const std::vector<TensorView>& out) {
+    const std::string ctx = context(node);
+    expect_io(node, in, out, 2, 3, 1);
+    const TensorView &x = in[0], &w = in[1], &y = out[0];
+    expect_f32(node, x);
+    expect_f32(node, w);
+    if (x.dims.size() != 4 || w.dims.size() != 4) {
+        fail(ctx, "input and weight must be rank 4 (NCHW)");
+    }
+    const int64_t group = int_attr(node, "group", 1);
+    if (group <= 0 || x.dims[1] % group != 0 || w.dims[0] != x.dims[1]) {
+        fail(ctx, "weight channels do not match the input and group");
+    }
+    std::vector<int64_t> s = ints_attr(node, "strides"), d = ints_attr(node, "dilations"),
+                         op = ints_attr(node, "output_padding"), p = ints_attr(node, "pads");
+    if (s.empty()) {
+        s = {1, 1};
+    }
+    if (d.empty()) {
+        d = {1, 1};
+    }
+    if (op.empty()) {
+        op = {0, 0};
+    }
+    if (p.empty() || str_attr(node, "auto_pad", "NOTSET") == "VALID") {
+        p = {0, 0, 0, 0};
+    }
+    if (s.size() != 2 || d.size() != 2 || op.size() != 2 || p.size() != 4) {
+        fail(ctx, "strides, dilations, output_padding, and pads must be 2-D");
+    }
+    const bool has_bias = in.size() == 3 && in[2].data != nullptr;
+    const int64_t m = w.dims[1] * group;
+    if (has_bias && (in[2].dims.size() != 1 || in[2].dims[0] != m)) {
+        fail(ctx, "bias must be rank-1 of length M");
+    }
+    nb2_convt_geom g{};
+    g.n = x.dims[0];
+    g.c = x.dims[1];
+    g.h = x.dims[2];
+    g.w = x.dims[3];
+    g.m = m;
+    g.kh = w.dims[2];
+    g.kw = w.dims[3];
+    g.oh = y.dims.size() == 4 ? y.dims[2] : -1;
+    g.ow = y.dims.size() == 4 ? y.dims[3] : -1;
+    g.stride_h = s[0];
+    g.stride_w = s[1];
+    g.pad_top = p[0];
+    g.pad_left = p[1];
+    g.pad_bottom = p[2];
+    g.pad_right = p[3];
+    g.dil_h = d[0];
+    g.dil_w = d[1];
+    g.out_pad_h = op[0];
+    g.out_pad_w = op[1];
+    g.group = group;
+    check(nb2_conv_transpose2d(current(ctx), &g, static_cast<const float*>(x.data), static_cast<const float*>(w.data),
+                               has_bias ? static_cast<const float*>(in[2].data) : nullptr,
+                               static_cast<float*>(y.data)),
+          ctx);
+}
+
 void Gemm(const Node& node, const std::vector<TensorView>& in, const std::vector<TensorView>& out) {
     const std::string ctx = context(node);
     expect_io(node, in, out, 2, 3, 1);
@@ -520,6 +584,44 @@ void MaxPool(const Node& node, const std::vector<TensorView>& in, const std::vec
     const int64_t pads[4] = {pb[0], pb[1], pe[0], pe[1]};
     check(nb2_maxpool2d(current(ctx), static_cast<const float*>(x.data), x.dims.data(), static_cast<float*>(y.data),
                         y.dims.data(), k.data(), s.data(), pads, d.data()),
+          ctx);
+}
+
+// AveragePool (src/kernels/average_pool.cpp:128-225): dilations fixed at 1,
+// count_include_pad selects the divisor.
+void AveragePool(const Node& node, const std::vector<TensorView>& in, const std::vector<TensorView>& out) {
+    const std::string ctx = context(node);
+    expect_io(node, in, out, 1, 1, 1);
+    const TensorView &x = in[0], &y = out[0];
+    expect_f32(node, x);
+    expect_f32(node, y);
+    if (x.dims.size() != 4) {
+        fail(ctx, "input must be rank 4 (NCHW)");
+    }
+    const std::vector<int64_t> k = ints_attr(node, "kernel_shape");
+    if (k.size() != 2) {
+        fail(ctx, "kernel_shape must have two spatial entries");
+    }
+    std::vector<int64_t> s = ints_attr(node, "strides");
+    if (s.empty()) {
+        s = {1, 1};
+    }
+    if (s.size() != 2) {
+        fail(ctx, "strides must have two spatial entries");
+    }
+    const std::vector<int64_t> d = {1, 1};
+    const bool ceil_mode = int_attr(node, "ceil_mode", 0) != 0;
+    std::vector<int64_t> pb, pe;
+    resolve_pads(node, {x.dims[2], x.dims[3]}, k, d, s, pb, pe);
+    const std::vector<int64_t> expected = {x.dims[0], x.dims[1],
+                                           window_out(node, x.dims[2], k[0], 1, pb[0], pe[0], s[0], ceil_mode),
+                                           window_out(node, x.dims[3], k[1], 1, pb[1], pe[1], s[1], ceil_mode)};
+    if (y.dims != expected) {
+        fail(ctx, "output shape does not match the pooling window");
+    }
+    const int64_t pads[4] = {pb[0], pb[1], pe[0], pe[1]};
+    check(nb2_avgpool2d(current(ctx), static_cast<const float*>(x.data), x.dims.data(), static_cast<float*>(y.data),
+                        y.dims.data(), k.data(), s.data(), pads, int_attr(node, "count_include_pad", 0) != 0 ? 1 : 0),
           ctx);
 }
 
@@ -1020,6 +1122,7 @@ class B200Table final : public KernelTable {
     explicit B200Table(DeviceState* s) : s_(s) {
         rows_ = {{"Conv", Conv},
                  {"Gemm", Gemm},
+                 {"ConvTranspose", ConvTranspose},
                  {"MatMul", MatMul},
                  {"Relu", Unary<NB2_UNARY_RELU>},
                  {"Sigmoid", Unary<NB2_UNARY_SIGMOID>},
@@ -1035,6 +1138,7 @@ class B200Table final : public KernelTable {
                  {"Div", Binary<NB2_BINARY_DIV>},
                  {"Pow", Binary<NB2_BINARY_POW>},
                  {"MaxPool", MaxPool},
+                 {"AveragePool", AveragePool},
                  {"GlobalAveragePool", GlobalAveragePool},
                  {"ReduceMean", ReduceMean},
                  {"Softmax", Softmax},

@@ -94,6 +94,44 @@ def conv(node, x, w, b=None):
     return y.astype(F32)
 
 
+def conv_transpose(node, x, w, b=None):
+    """reference kernels::ConvTranspose, src/kernels/conv_transpose.cpp:76-191:
+    every input pixel scattered through the [C, M/group, KH, KW] weight to
+    oh = ih*s - pad_begin + kh*d (kept when inside the output), bias first;
+    summed here in float64 and rounded once (the reference sums in float32)."""
+    group = _attr(node, "group", 1)
+    s = _attr(node, "strides", [1, 1])
+    d = _attr(node, "dilations", [1, 1])
+    op = _attr(node, "output_padding", [0, 0])
+    p = _attr(node, "pads", [0, 0, 0, 0])
+    if _attr(node, "auto_pad", "NOTSET") == "VALID":
+        p = [0, 0, 0, 0]
+    n, c, H, W = x.shape
+    kh, kw = w.shape[2], w.shape[3]
+    mg = w.shape[1]
+    m = mg * group
+    cg = c // group
+    oh = s[0] * (H - 1) + op[0] + d[0] * (kh - 1) + 1 - p[0] - p[2]
+    ow = s[1] * (W - 1) + op[1] + d[1] * (kw - 1) + 1 - p[1] - p[3]
+    # full (uncropped) canvas, then the window [p_begin, p_begin + out)
+    fh = s[0] * (H - 1) + d[0] * (kh - 1) + 1 + op[0] + p[0] + p[2]
+    fw = s[1] * (W - 1) + d[1] * (kw - 1) + 1 + op[1] + p[1] + p[3]
+    full = np.zeros((n, m, fh, fw), np.float64)
+    x64, w64 = x.astype(np.float64), w.astype(np.float64)
+    for gi in range(group):
+        xg = x64[:, gi * cg:(gi + 1) * cg]
+        wg = w64[gi * cg:(gi + 1) * cg]  # [cg, mg, kh, kw]
+        for i in range(kh):
+            for j in range(kw):
+                contrib = np.einsum("nchw,cm->nmhw", xg, wg[:, :, i, j])
+                full[:, gi * mg:(gi + 1) * mg, i * d[0]:i * d[0] + s[0] * (H - 1) + 1:s[0],
+                     j * d[1]:j * d[1] + s[1] * (W - 1) + 1:s[1]] += contrib
+    y = full[:, :, p[0]:p[0] + oh, p[1]:p[1] + ow]
+    if b is not None:
+        y = y + b.astype(np.float64)[None, :, None, None]
+    return y.astype(F32)
+
+
 def gemm(node, a, b, c=None):
     """reference kernels::Gemm, src/kernels/gemm.cpp:59-137."""
     a = a.T if _attr(node, "transA", 0) else a
@@ -169,6 +207,41 @@ def maxpool(node, x):
         for j in range(k[1]):
             t = xp[:, :, i * d[0]:i * d[0] + s[0] * (oh - 1) + 1:s[0], j * d[1]:j * d[1] + s[1] * (ow - 1) + 1:s[1]]
             y = np.where(t > y, t, y)
+    return y.astype(F32)
+
+
+def average_pool(node, x):
+    """reference kernels::AveragePool, src/kernels/average_pool.cpp:128-225:
+    dilation 1, the window clipped to [start, min(start + k, in + pad_end)),
+    in-range taps summed in float32 in row-major order, divided by the padded
+    window size (count_include_pad) or the in-range tap count."""
+    k = _attr(node, "kernel_shape", None)
+    s = _attr(node, "strides", [1, 1])
+    ceil_mode = bool(_attr(node, "ceil_mode", 0))
+    include = bool(_attr(node, "count_include_pad", 0))
+    pb, pe = _window_pads(_attr(node, "auto_pad", "NOTSET"), list(x.shape[2:]), k, [1, 1], s, _attr(node, "pads", []))
+    H, W = x.shape[2], x.shape[3]
+    oh = _out_dim(H, k[0], 1, pb[0], pe[0], s[0], ceil_mode)
+    ow = _out_dim(W, k[1], 1, pb[1], pe[1], s[1], ceil_mode)
+    hs = np.arange(oh) * s[0] - pb[0]
+    he = np.minimum(hs + k[0], H + pe[0])
+    h0, h1 = np.maximum(hs, 0), np.minimum(he, H)
+    ws = np.arange(ow) * s[1] - pb[1]
+    we = np.minimum(ws + k[1], W + pe[1])
+    w0, w1 = np.maximum(ws, 0), np.minimum(we, W)
+    acc = np.zeros(x.shape[:2] + (oh, ow), F32)
+    for i in range(k[0]):
+        ih = hs + i
+        vh = (ih >= h0) & (ih < h1)
+        rows = x[:, :, np.clip(ih, 0, H - 1), :]
+        for j in range(k[1]):
+            iw = ws + j
+            vw = (iw >= w0) & (iw < w1)
+            vals = rows[:, :, :, np.clip(iw, 0, W - 1)]
+            acc = np.where(vh[:, None] & vw[None, :], (acc + vals).astype(F32), acc)
+    div = ((he - hs)[:, None] * (we - ws)[None, :]) if include else ((h1 - h0)[:, None] * (w1 - w0)[None, :])
+    with np.errstate(divide="ignore", invalid="ignore"):
+        y = np.where(div > 0, acc / div.astype(F32), np.float32(0.0))
     return y.astype(F32)
 
 
@@ -488,6 +561,8 @@ OPS = {
     "Div": div,
     "Sigmoid": sigmoid,
     "MaxPool": maxpool,
+    "ConvTranspose": conv_transpose,
+    "AveragePool": average_pool,
     "GlobalAveragePool": global_average_pool,
     "Flatten": flatten,
     "Reshape": reshape,

@@ -161,3 +161,26 @@ def test_reference_cuda_baseline_matches_oracle(cuda):
     x = configs.resnet_input(1)
     got = ref.run_graph(g, {"input": x}, cuda=True)["fc_out"]
     assert rel_err(got, np_ref.run(g, {"input": x})["fc_out"]) <= TOL
+
+
+def test_average_pool_row_through_reference_executor(b200_device):
+    """The AveragePool row on the new handle, SAME_UPPER padding resolved as
+    the reference does, bit-exact with the reference CpuDevice."""
+    g = Graph(opset=13)
+    g.add_input("x", [2, 8, 14, 13])
+    y = g.op("AveragePool", ["x"], name="pool", kernel_shape=[5, 5], strides=[3, 3], auto_pad="SAME_UPPER",
+             count_include_pad=1)
+    g.add_output(y, None, FLOAT)
+    cpu, gpu = both(g, {"x": synth.normal((2, 8, 14, 13), 1.0, 77)}, b200_device)
+    np.testing.assert_array_equal(list(gpu.values())[0], list(cpu.values())[0])
+
+
+def test_conv_transpose_row_through_reference_executor(b200_device):
+    """The ConvTranspose row on the new handle against the reference CpuDevice."""
+    g = Graph(opset=13)
+    g.add_input("x", [2, 16, 9, 11])
+    w = g.const("w", synth.normal((16, 8, 3, 3), 0.25, 81))
+    y = g.op("ConvTranspose", ["x", w], name="ct", strides=[2, 2], pads=[1, 0, 1, 0], output_padding=[1, 1])
+    g.add_output(y, None, FLOAT)
+    cpu, gpu = both(g, {"x": synth.normal((2, 16, 9, 11), 1.0, 82)}, b200_device)
+    assert rel_err(list(gpu.values())[0], list(cpu.values())[0]) <= TOL

@@ -195,3 +195,25 @@ def test_transpose_after_matmul_kept_when_not_a_head_split():
     a = nbm.analyze(g, {"x": [6, 10, 24]})
     # columns 20 = 4 x 5: inner block 5 is not a multiple of 16, so no map
     assert any(e["op"] == "Transpose" for e in a["exec"])
+
+
+def test_batchnorm_folded_into_conv_at_load():
+    """An export that keeps BatchNormalization after every Conv plans to the
+    same rows as the folded graph (the reference loader rejects the op,
+    src/model_loader.cpp:1677-1690; the engine folds it at load)."""
+    dims = {"input": [2, 3, 224, 224]}
+    a = nbm.analyze(configs.resnet18(2, bn_nodes=True), dims)
+    b = nbm.analyze(configs.resnet18(2), dims)
+    assert [e["op"] for e in a["exec"]] == [e["op"] for e in b["exec"]]
+    assert "BatchNormalization" not in {e["op"] for e in a["exec"]}
+
+
+def test_batchnorm_without_conv_stays_a_row():
+    g = Graph(opset=13)
+    g.add_input("x", [2, 5, 3, 4])
+    r = g.op("Relu", ["x"], name="r")
+    stats = [g.const(f"s{i}", np.full((5,), v, np.float32)) for i, v in enumerate((2.0, 0.5, 0.1, 3.0))]
+    y = g.op("BatchNormalization", [r] + stats, name="bn", epsilon=1e-3)
+    g.add_output(y, None, FLOAT)
+    a = nbm.analyze(g, {"x": [2, 5, 3, 4]})
+    assert [e["op"] for e in a["exec"]][-1] == "BatchNormalization"

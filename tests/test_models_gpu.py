@@ -203,3 +203,33 @@ def test_pipelined_host_runs_keep_each_input(cuda):
             assert rel_err(ho.array, ref) <= TOL
     finally:
         m.close()
+
+
+def test_resnet18_with_batchnorm_nodes(cuda):
+    """The unfolded export (Conv then BatchNormalization, folded at load)
+    matches the oracle on the folded graph."""
+    x = configs.resnet_input(2)
+    ref = np_ref.run(configs.resnet18(2), {"input": x})["fc_out"]
+    out, _ = _run(configs.resnet18(2, bn_nodes=True), {"input": x})
+    assert rel_err(out["fc_out"], ref) <= TOL
+
+
+def test_standalone_batchnorm_row(cuda):
+    """A BatchNormalization that follows no Conv runs as the per-channel
+    affine y = x * gamma / sqrt(var + eps) + (beta - mean * gamma / sqrt(var + eps))."""
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    g = Graph(opset=13)
+    g.add_input("x", [2, 6, 5, 7])
+    r = g.op("Relu", ["x"], name="r")
+    gamma, beta = synth.normal((6,), 1.0, 1), synth.normal((6,), 1.0, 2)
+    mean, var = synth.normal((6,), 1.0, 3), synth.uniform((6,), 0.5, 2.0, 4)
+    stats = [g.const(n, v) for n, v in (("g", gamma), ("b", beta), ("m", mean), ("v", var))]
+    y = g.op("BatchNormalization", [r] + stats, name="bn", epsilon=1e-3)
+    g.add_output(y, None, FLOAT)
+    x = synth.normal((2, 6, 5, 7), 1.0, 5)
+    out, _ = _run(g, {"x": x})
+    a = gamma.astype(np.float64) / np.sqrt(var.astype(np.float64) + np.float32(1e-3))
+    want = np.maximum(x, 0).astype(np.float64) * a[None, :, None, None] + (beta - mean * a)[None, :, None, None]
+    assert rel_err(out[y], want) <= TOL

@@ -153,3 +153,48 @@ def test_np_ref_matches_bench_config_fixtures(config):
                 np.testing.assert_array_equal(have, want, err_msg=f"{config} {out_name} {i}")
             else:
                 assert rel_err(have, want) <= 1e-5, (config, out_name, i)
+
+
+AVGPOOL_CASES = [
+    ({"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]}, (2, 3, 17, 19)),
+    ({"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1], "count_include_pad": 1}, (2, 3, 17, 19)),
+    ({"kernel_shape": [2, 3], "strides": [2, 1], "pads": [0, 1, 1, 0], "ceil_mode": 1}, (1, 4, 9, 10)),
+    ({"kernel_shape": [5, 5], "strides": [3, 3], "auto_pad": "SAME_UPPER"}, (1, 2, 14, 13)),
+    ({"kernel_shape": [2, 2], "strides": [2, 2]}, (3, 8, 8, 8)),
+]
+
+
+@needs_ref
+@pytest.mark.parametrize("case", AVGPOOL_CASES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c[0].items()))
+def test_np_ref_average_pool_bit_exact_with_reference(case):
+    """AveragePool sums in float32 in the reference's order: bit-exact."""
+    attrs, shape = case
+    x = synth.normal(shape, 1.0, synth.seed_of("oracle_avgpool", str(case)))
+    g = single_op_graph("AveragePool", attrs, [shape])
+    want = list(ref.run_graph(g, {"in0": x}).values())[0]
+    np.testing.assert_array_equal(np_ref.run_op("AveragePool", attrs, [x]), want)
+
+
+CONVT_CASES = [
+    ({"strides": [2, 2], "pads": [1, 1, 1, 1], "output_padding": [1, 1]}, (2, 8, 7, 9), (8, 6, 3, 3)),
+    ({"strides": [2, 2]}, (1, 16, 10, 10), (16, 8, 2, 2)),
+    ({"strides": [1, 2], "pads": [0, 1, 2, 0], "dilations": [2, 1]}, (1, 6, 5, 6), (6, 4, 3, 3)),
+    ({"strides": [3, 3], "group": 2, "pads": [1, 1, 1, 1]}, (1, 8, 4, 5), (8, 3, 4, 4)),
+]
+
+
+@needs_ref
+@pytest.mark.parametrize("case", CONVT_CASES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c[0].items()))
+def test_np_ref_conv_transpose_matches_reference(case):
+    attrs, xs, ws = case
+    x = synth.normal(xs, 1.0, synth.seed_of("oracle_convt", str(case) + "x"))
+    w = synth.normal(ws, 0.3, synth.seed_of("oracle_convt", str(case) + "w"))
+    b = synth.normal((ws[1] * attrs.get("group", 1),), 1.0, synth.seed_of("oracle_convt", str(case) + "b"))
+    g = Graph(opset=13)
+    g.add_input("x", list(xs))
+    y = g.op("ConvTranspose", ["x", g.const("w", w), g.const("b", b)], name="ct", **attrs)
+    g.add_output(y, None, FLOAT)
+    want = list(ref.run_graph(g, {"x": x}).values())[0]
+    got = np_ref.run(g, {"x": x})[y]
+    assert got.shape == want.shape
+    assert np.abs(got.astype(np.float64) - want).max() <= 1e-5 * np.abs(want).max()

@@ -224,3 +224,63 @@ def test_topk_long_rows_mixed_ties(cuda):
     got = run_engine(g, {"in0": x})
     for name in ref:
         np.testing.assert_array_equal(got[name], ref[name])
+
+
+AVGPOOL_GPU_CASES = [
+    ({"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]}, (2, 16, 57, 57)),
+    ({"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1], "count_include_pad": 1}, (2, 16, 57, 57)),
+    ({"kernel_shape": [2, 3], "strides": [2, 1], "pads": [0, 1, 1, 0], "ceil_mode": 1}, (1, 4, 9, 10)),
+    ({"kernel_shape": [7, 7], "strides": [1, 1]}, (4, 512, 7, 7)),
+]
+
+
+@pytest.mark.parametrize("case", AVGPOOL_GPU_CASES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c[0].items()))
+def test_average_pool_bit_exact(cuda, case):
+    """AveragePool (engine row) sums in the reference's order: bit-exact with
+    the oracle, which is bit-exact with the reference library."""
+    attrs, shape = case
+    g, feeds = one("AveragePool", [shape], attrs)
+    ref = np_ref.run(g, feeds)
+    got = run_engine(g, feeds)
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
+
+
+@pytest.mark.parametrize("length,k", [(5000, 2000), (300000, 1500), (20000, 20000)], ids=["short", "long", "whole_row"])
+def test_topk_large_k(cuda, length, k):
+    """K above 1024 (the reference accepts any constant K,
+    src/kernels/top_k.cpp:53-142): radix passes then a rank-by-count
+    placement, bit-exact; half the values repeat, so ties resolve by index."""
+    x = synth.normal((3, length), 1.0, 31)
+    x[:, ::2] = np.round(x[:, ::2] * 4) / 4  # many exact ties
+    g, _ = one("TopK", [(3, length), (1,)], {"axis": -1}, {1: np.array([k], np.int64)}, n_out=2)
+    ref = np_ref.run(g, {"in0": x})
+    got = run_engine(g, {"in0": x})
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
+
+
+CONVT_GPU_CASES = [
+    ({"strides": [2, 2], "pads": [1, 1, 1, 1], "output_padding": [1, 1]}, (2, 64, 20, 20), (64, 32, 3, 3)),
+    ({"strides": [2, 2]}, (2, 128, 20, 20), (128, 64, 2, 2)),
+    ({"strides": [1, 2], "pads": [0, 1, 2, 0], "dilations": [2, 1]}, (1, 6, 15, 16), (6, 4, 3, 3)),
+    ({"strides": [3, 3], "group": 2, "pads": [1, 1, 1, 1]}, (1, 8, 14, 15), (8, 3, 4, 4)),
+]
+
+
+@pytest.mark.parametrize("case", CONVT_GPU_CASES, ids=lambda c: "_".join(f"{k}{v}" for k, v in c[0].items()))
+def test_conv_transpose_engine(cuda, case):
+    """ConvTranspose as a stride-1 tensor-core Conv over the zero-inserted
+    input, against the restatement of src/kernels/conv_transpose.cpp."""
+    attrs, xs, ws = case
+    x = synth.normal(xs, 1.0, 61)
+    w = synth.normal(ws, 1.0 / np.sqrt(ws[0] * ws[2] * ws[3]), 62)
+    b = synth.normal((ws[1] * attrs.get("group", 1),), 1.0, 63)
+    g = Graph(opset=13)
+    g.add_input("x", list(xs))
+    y = g.op("ConvTranspose", ["x", g.const("w", w), g.const("b", b)], name="ct", **attrs)
+    g.add_output(y, None, FLOAT)
+    ref = np_ref.run(g, {"x": x})[y]
+    got = run_engine(g, {"x": x})[y]
+    assert got.shape == ref.shape
+    assert rel_err(got, ref) <= TOL
