@@ -109,6 +109,13 @@ int64_t nb2_device_get_wait_bound(const nb2_device* dev);
 int nb2_device_last_contraction(const nb2_device* dev, int* tile_n, int* two_in_flight, int* k_slices, int* a_mode,
                                 int64_t* tiles);
 
+/* 1 when kernels can read `ptr` directly (device, managed or pinned host
+ * memory), 0 for ordinary pageable host memory or null. The nert::Device rows
+ * use it to stage host views (the reference's FoldConstants hands every
+ * device's rows host initializer bytes, src/constant_folding.cpp:32-95). No
+ * counterpart in the reference. */
+int nb2_pointer_on_device(const void* ptr);
+
 /* Device memory (replaces CudaAllocator, src/cuda_device.cpp:30-51):
  * 256-byte aligned, null on bytes <= 0. */
 int nb2_device_malloc(nb2_device* dev, int64_t bytes, void** out);

@@ -55,6 +55,7 @@ _SIGS = {
     "nb2_device_last_contraction": (ctypes.c_int, [vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                                    ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                                    c_i64p]),
+    "nb2_pointer_on_device": (ctypes.c_int, [vp]),
     "nb2_device_malloc": (ctypes.c_int, [vp, ctypes.c_int64, ctypes.POINTER(vp)]),
     "nb2_device_free": (ctypes.c_int, [vp, vp]),
     "nb2_memcpy_h2d": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64]),

@@ -207,6 +207,18 @@ int nb2_device_synchronize(nb2_device* dev) {
     });
 }
 
+int nb2_pointer_on_device(const void* ptr) {
+    if (ptr == nullptr) {
+        return 0;
+    }
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged || a.type == cudaMemoryTypeHost ? 1 : 0;
+}
+
 int nb2_device_malloc(nb2_device* dev, int64_t bytes, void** out) {
     return guard([&] {
         need(out != nullptr, "null output pointer");

@@ -970,6 +970,66 @@ void Cast(const Node& node, const std::vector<TensorView>& in, const std::vector
           ctx);
 }
 
+// Every row runs through this wrapper: views whose memory kernels cannot read
+// (pageable host memory) are staged through device buffers, inputs copied in
+// before the row and outputs copied back after it. The executor only passes
+// arena and resident views (no staging); the reference's FoldConstants passes
+// the initializers' own host bytes to whatever device it is given
+// (src/constant_folding.cpp:32-95), and then this makes the row work anyway.
+template <KernelFn F>
+void HostSafe(const Node& node, const std::vector<TensorView>& in, const std::vector<TensorView>& out) {
+    bool host = false;
+    for (const auto* vs : {&in, &out}) {
+        for (const TensorView& v : *vs) {
+            host = host || (v.data != nullptr && nb2_pointer_on_device(v.data) == 0);
+        }
+    }
+    if (!host) {
+        F(node, in, out);
+        return;
+    }
+    const std::string ctx = context(node);
+    nb2_device* dev = current(ctx);
+    std::vector<void*> owned;
+    auto stage = [&](const std::vector<TensorView>& vs, bool upload) {
+        std::vector<TensorView> d = vs;
+        for (TensorView& v : d) {
+            if (v.data == nullptr || nb2_pointer_on_device(v.data) != 0) {
+                continue;
+            }
+            const int64_t bytes = count_of(v.dims) * elem_bytes(v.dtype);
+            void* p = nullptr;
+            if (bytes > 0) {
+                check(nb2_device_malloc(dev, bytes, &p), ctx);
+                owned.push_back(p);
+                if (upload) {
+                    check(nb2_memcpy_h2d(dev, p, v.data, bytes), ctx);
+                }
+            }
+            v.data = p;
+        }
+        return d;
+    };
+    try {
+        const std::vector<TensorView> din = stage(in, true), dout = stage(out, false);
+        F(node, din, dout);
+        for (size_t i = 0; i < out.size(); ++i) {
+            if (out[i].data != nullptr && dout[i].data != out[i].data) {
+                check(nb2_memcpy_d2h(dev, out[i].data, dout[i].data, count_of(out[i].dims) * elem_bytes(out[i].dtype)),
+                      ctx);
+            }
+        }
+    } catch (...) {
+        for (void* p : owned) {
+            nb2_device_free(dev, p);
+        }
+        throw;
+    }
+    for (void* p : owned) {
+        nb2_device_free(dev, p);
+    }
+}
+
 // ---- seam objects ------------------------------------------------------------
 
 struct DeviceState {
@@ -1120,42 +1180,42 @@ class B200Transfer final : public Transfer {
 class B200Table final : public KernelTable {
   public:
     explicit B200Table(DeviceState* s) : s_(s) {
-        rows_ = {{"Conv", Conv},
-                 {"Gemm", Gemm},
-                 {"ConvTranspose", ConvTranspose},
-                 {"MatMul", MatMul},
-                 {"Relu", Unary<NB2_UNARY_RELU>},
-                 {"Sigmoid", Unary<NB2_UNARY_SIGMOID>},
-                 {"Erf", Unary<NB2_UNARY_ERF>},
-                 {"Sqrt", Unary<NB2_UNARY_SQRT>},
-                 {"Neg", Unary<NB2_UNARY_NEG>},
-                 {"Abs", Unary<NB2_UNARY_ABS>},
-                 {"Exp", Unary<NB2_UNARY_EXP>},
-                 {"Tanh", Unary<NB2_UNARY_TANH>},
-                 {"Add", Binary<NB2_BINARY_ADD>},
-                 {"Sub", Binary<NB2_BINARY_SUB>},
-                 {"Mul", Binary<NB2_BINARY_MUL>},
-                 {"Div", Binary<NB2_BINARY_DIV>},
-                 {"Pow", Binary<NB2_BINARY_POW>},
-                 {"MaxPool", MaxPool},
-                 {"AveragePool", AveragePool},
-                 {"GlobalAveragePool", GlobalAveragePool},
-                 {"ReduceMean", ReduceMean},
-                 {"Softmax", Softmax},
-                 {"LayerNormalization", LayerNormalization},
-                 {"Flatten", CopyView},
-                 {"Reshape", CopyView},
-                 {"Squeeze", CopyView},
-                 {"Unsqueeze", CopyView},
-                 {"Identity", CopyView},
-                 {"Transpose", Transpose},
-                 {"Concat", Concat},
-                 {"Split", Split},
-                 {"Slice", Slice},
-                 {"Gather", Gather},
-                 {"TopK", TopK},
-                 {"Resize", Resize},
-                 {"Cast", Cast}};
+        rows_ = {{"Conv", HostSafe<Conv>},
+                 {"Gemm", HostSafe<Gemm>},
+                 {"ConvTranspose", HostSafe<ConvTranspose>},
+                 {"MatMul", HostSafe<MatMul>},
+                 {"Relu", HostSafe<Unary<NB2_UNARY_RELU>>},
+                 {"Sigmoid", HostSafe<Unary<NB2_UNARY_SIGMOID>>},
+                 {"Erf", HostSafe<Unary<NB2_UNARY_ERF>>},
+                 {"Sqrt", HostSafe<Unary<NB2_UNARY_SQRT>>},
+                 {"Neg", HostSafe<Unary<NB2_UNARY_NEG>>},
+                 {"Abs", HostSafe<Unary<NB2_UNARY_ABS>>},
+                 {"Exp", HostSafe<Unary<NB2_UNARY_EXP>>},
+                 {"Tanh", HostSafe<Unary<NB2_UNARY_TANH>>},
+                 {"Add", HostSafe<Binary<NB2_BINARY_ADD>>},
+                 {"Sub", HostSafe<Binary<NB2_BINARY_SUB>>},
+                 {"Mul", HostSafe<Binary<NB2_BINARY_MUL>>},
+                 {"Div", HostSafe<Binary<NB2_BINARY_DIV>>},
+                 {"Pow", HostSafe<Binary<NB2_BINARY_POW>>},
+                 {"MaxPool", HostSafe<MaxPool>},
+                 {"AveragePool", HostSafe<AveragePool>},
+                 {"GlobalAveragePool", HostSafe<GlobalAveragePool>},
+                 {"ReduceMean", HostSafe<ReduceMean>},
+                 {"Softmax", HostSafe<Softmax>},
+                 {"LayerNormalization", HostSafe<LayerNormalization>},
+                 {"Flatten", HostSafe<CopyView>},
+                 {"Reshape", HostSafe<CopyView>},
+                 {"Squeeze", HostSafe<CopyView>},
+                 {"Unsqueeze", HostSafe<CopyView>},
+                 {"Identity", HostSafe<CopyView>},
+                 {"Transpose", HostSafe<Transpose>},
+                 {"Concat", HostSafe<Concat>},
+                 {"Split", HostSafe<Split>},
+                 {"Slice", HostSafe<Slice>},
+                 {"Gather", HostSafe<Gather>},
+                 {"TopK", HostSafe<TopK>},
+                 {"Resize", HostSafe<Resize>},
+                 {"Cast", HostSafe<Cast>}};
     }
     // Returns the row (null when this device has none, as the reference
     // tables do) and binds this GPU to the calling thread for it.

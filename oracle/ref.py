@@ -58,6 +58,10 @@ def lib(cuda: bool = False):
         L.nref_last_error.restype = ctypes.c_char_p
         L.nref_last_error.argtypes = [ctypes.c_void_p]
         L.nref_close.argtypes = [ctypes.c_void_p]
+        L.nref_open_folded.restype = ctypes.c_void_p
+        L.nref_open_folded.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                       ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int), ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
         L.nref_run.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
                                ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_void_p),
                                ctypes.POINTER(ctypes.c_int64)]
@@ -84,7 +88,7 @@ class RefModel:
     other ``const nert::Device*`` handed in as an integer address."""
 
     def __init__(self, onnx_path: str, input_dims: dict[str, list[int]], device: int | None = None,
-                 cuda: bool = False):
+                 cuda: bool = False, fold_device: int | None = None, fold: bool = False):
         """cuda=True: the library built with the reference's CudaDevice, and
         (when `device` is None) that device."""
         self._L = L = lib(cuda)
@@ -97,7 +101,15 @@ class RefModel:
         flat = [d for n in names for d in input_dims[n]]
         c_dims = (ctypes.c_int64 * max(1, len(flat)))(*flat)
         c_ranks = (ctypes.c_int * len(names))(*[len(input_dims[n]) for n in names])
-        self._h = L.nref_open(onnx_path.encode(), len(names), c_names, c_dims, c_ranks, device)
+        self.folded = 0
+        if fold:
+            # nert::FoldConstants with `fold_device`'s rows first (CpuDevice when None)
+            n_fold = ctypes.c_int(0)
+            self._h = L.nref_open_folded(onnx_path.encode(), len(names), c_names, c_dims, c_ranks, fold_device,
+                                         device, ctypes.byref(n_fold))
+            self.folded = n_fold.value
+        else:
+            self._h = L.nref_open(onnx_path.encode(), len(names), c_names, c_dims, c_ranks, device)
         if not self._h:
             raise RuntimeError("reference load failed: " + L.nref_last_error(None).decode())
         self.last_ms = 0.0

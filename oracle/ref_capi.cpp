@@ -16,6 +16,7 @@
 // point returns 0 on success and a negative code otherwise, with the message
 // kept on the session (or in a thread-local buffer when there is none).
 
+#include "nert/constant_folding.hpp"
 #include "nert/device.hpp"
 #include "nert/executor.hpp"
 #include "nert/graph.hpp"
@@ -89,6 +90,39 @@ void* nref_open(const char* onnx_path, int n_inputs, const char* const* names, c
     auto session = std::make_unique<Session>();
     try {
         session->graph = nert::LoadGraphFromFile(onnx_path);
+        nert::ShapeMap shapes;
+        int64_t at = 0;
+        for (int i = 0; i < n_inputs; ++i) {
+            std::vector<int64_t> dims(dims_flat + at, dims_flat + at + ranks[i]);
+            at += ranks[i];
+            shapes.emplace(names[i], dims);
+        }
+        const nert::Device& dev =
+            device != nullptr ? *static_cast<const nert::Device*>(device) : nert::CpuDevice();
+        session->model = std::make_unique<nert::Model>(session->graph, shapes, dev);
+        for (const auto& out : session->graph.outputs) {
+            session->output_names.push_back(out.first);
+        }
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return nullptr;
+    }
+    return session.release();
+}
+
+// nref_open with the reference's load-time constant folding first:
+// nert::FoldConstants(graph, *fold_device) (include/nert/constant_folding.hpp:22),
+// which runs every all-constant node with that device's rows on the
+// initializers' host bytes; *folded receives the number of nodes it folded.
+// The Model then runs on `device` (CpuDevice when null).
+void* nref_open_folded(const char* onnx_path, int n_inputs, const char* const* names, const int64_t* dims_flat,
+                       const int* ranks, const void* fold_device, const void* device, int* folded) {
+    auto session = std::make_unique<Session>();
+    try {
+        session->graph = nert::LoadGraphFromFile(onnx_path);
+        const nert::Device& fdev =
+            fold_device != nullptr ? *static_cast<const nert::Device*>(fold_device) : nert::CpuDevice();
+        *folded = nert::FoldConstants(session->graph, fdev);
         nert::ShapeMap shapes;
         int64_t at = 0;
         for (int i = 0; i < n_inputs; ++i) {

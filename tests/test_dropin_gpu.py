@@ -184,3 +184,47 @@ def test_conv_transpose_row_through_reference_executor(b200_device):
     g.add_output(y, None, FLOAT)
     cpu, gpu = both(g, {"x": synth.normal((2, 16, 9, 11), 1.0, 82)}, b200_device)
     assert rel_err(list(gpu.values())[0], list(cpu.values())[0]) <= TOL
+
+
+def test_reference_constant_folding_with_b200_rows(b200_device):
+    """nert::FoldConstants (src/constant_folding.cpp:32-95) runs each
+    all-constant node with the given device's rows on the initializers' HOST
+    bytes. With the B200 handle the rows stage those views through HBM, so
+    folding with it gives the graph the CPU fold gives, within the north-star
+    bound (the folded MatMul runs on the tensor cores)."""
+    g = Graph(opset=13)
+    g.add_input("x", [2, 8, 6, 6])
+    a = g.const("a", synth.normal((8,), 1.0, 91))
+    b = g.const("b", synth.normal((8,), 1.0, 92))
+    s = g.op("Add", [a, b], name="fold_add")
+    s = g.op("Mul", [s, b], name="fold_mul")
+    s = g.op("Relu", [s], name="fold_relu")
+    p = g.const("p", synth.normal((8, 64), 0.3, 93))
+    q = g.const("q", synth.normal((64, 8), 0.3, 94))
+    m = g.op("MatMul", [p, q], name="fold_matmul")
+    w = g.const("w", synth.normal((8, 8, 3, 3), 0.2, 95))
+    y = g.op("Conv", ["x", w, s], name="cv", pads=[1, 1, 1, 1])
+    y = g.op("Add", [y, g.const("shape4", np.ones((1, 8, 1, 1), np.float32))], name="y_add")
+    y = g.op("Reshape", [y, g.const("rs", np.array([2, 8, 36], np.int64))], name="rs")
+    y = g.op("MatMul", [m, y], name="mix")
+    g.add_output(y, None, FLOAT)
+    x = synth.normal((2, 8, 6, 6), 1.0, 96)
+    import tempfile
+
+    from nert_b200 import onnx_io
+
+    with tempfile.TemporaryDirectory() as d:
+        path = onnx_io.save(g, os.path.join(d, "model.onnx"))
+        plain = ref.RefModel(path, {"x": [2, 8, 6, 6]})
+        cpu_fold = ref.RefModel(path, {"x": [2, 8, 6, 6]}, fold=True)
+        b200_fold = ref.RefModel(path, {"x": [2, 8, 6, 6]}, fold=True, fold_device=b200_device)
+        try:
+            assert cpu_fold.folded == b200_fold.folded == 4
+            want = list(plain.run({"x": x}).values())[0]
+            via_cpu = list(cpu_fold.run({"x": x}).values())[0]
+            via_b200 = list(b200_fold.run({"x": x}).values())[0]
+        finally:
+            for mdl in (plain, cpu_fold, b200_fold):
+                mdl.close()
+    np.testing.assert_array_equal(via_cpu, want)
+    assert rel_err(via_b200, want) <= TOL
