@@ -49,7 +49,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-18 fp32 images/s bs64 at 1/2/4/8 B200; Conv/GEMM % of TF32 tensor peak"
 UNIT = "images/s"
-DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32, "conv": 64}
+DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32, "conv": 64, "rows": 0}
 
 
 def parse():
@@ -243,7 +243,7 @@ def run_reference(args):
     if not ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnert_ref.so was not built"}))
         return 0
-    if args.workload in ("sweep", "conv"):
+    if args.workload in ("sweep", "conv", "rows"):
         print(json.dumps({"impl": "reference", "unavailable": "the single-op workloads have no reference CPU arm"}))
         return 0
     cores = ref_cores()
@@ -345,7 +345,7 @@ def measure_tf32_peak() -> float:
 
 # dram__bytes_read.sum + dram__bytes_write.sum over the contraction launches of
 # one forward, from the ncu capture summarised in profiles/ (per workload, batch)
-TRAFFIC_BYTES = {("resnet18", 64): int((788.2 + 192.7) * 1e6)}
+TRAFFIC_BYTES = {("resnet18", 64): int((788.3 + 196.2) * 1e6)}
 
 
 def tensor_peak(precision: str) -> tuple[float, str]:
@@ -452,7 +452,7 @@ def hbm_peak() -> tuple[float, str]:
         return 6650.0, "of fallback"
 
 
-def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
+def bandwidth_rows(local: int, reps: int = 10, warm: int = 3) -> list[dict]:
     """Every HBM-bound row at the largest config geometry that uses it,
     launched through the C ABI on the layer's stream and timed with CUDA
     events around each launch (L2 flushed before each by a 256 MB write and a
@@ -558,7 +558,7 @@ def bandwidth_rows(local: int, reps: int = 10) -> list[dict]:
     torch.cuda.synchronize()
     for name, shape, nbytes, fn in rows:
         with torch.cuda.stream(stream):
-            for _ in range(3):
+            for _ in range(warm):
                 _lib.check(fn())
             evs = []
             for _ in range(reps):
@@ -769,7 +769,7 @@ def main():
     rank, world, local = dist_env()
 
     cpu = None
-    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv")
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv", "rows")
             and args.api == "engine"):
         from oracle import ref
 
@@ -794,6 +794,15 @@ def main():
         return run_sweep(args, local)
     if args.workload == "conv":
         return run_conv(args, local)
+    if args.workload == "rows":
+        # the HBM-bound rows alone (also the target of their committed ncu
+        # captures): --steps timed launches per row after --warmup untimed
+        rows = bandwidth_rows(local, reps=args.steps, warm=args.warmup)
+        print(json.dumps({"metric": "HBM-bound rows: algorithmic GB/s", "unit": "GB/s", "n_gpus": 1,
+                          "steps": args.steps, "warmup": args.warmup, "data": "synthetic",
+                          "config": {"workload": "rows", "l2": "flushed before each launch"},
+                          "bandwidth_rows": rows}), flush=True)
+        return 0
     if args.api == "seam":
         return run_seam(args, local)
 

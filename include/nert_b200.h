@@ -214,6 +214,25 @@ int nb2_binary(nb2_device* dev, int op, int dtype, const void* a, const int64_t*
 /* MaxPool 2-D (src/kernels/max_pool.cpp:138-239): x [n,c,h,w] -> y [n,c,oh,ow]. */
 int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
                   const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4], const int64_t dilations[2]);
+/* Fused attention, the chain MatMul(Q, K^T) -> Div/Mul by a scalar ->
+ * Softmax(axis -1) -> MatMul(., V) (src/kernels/mat_mul.cpp:79-169,
+ * div.cpp, softmax.cpp:47-120) in one launch, one CTA per (batch, head), on
+ * the tcgen05 tensor cores with the 3xTF32 split. Element (token t, dim j)
+ * of head (b, h) is at b*s[0] + h*s[1] + t*s[2] + j*s[3] of q, k and v (so a
+ * K^T operand [.., d, T] has s[2] = 1, s[3] = T); output row (b, h, t) at
+ * b*o[0] + h*o[1] + t*o[2], its head_dim values contiguous (o = {T*H*D, D,
+ * H*D} writes the merged [B, T, H*D] layout). scale_mode 0: no scale, 1:
+ * multiply by `scale`, 2: divide by `scale`. head_dim 64, 1 <= tokens <= 208. */
+int nb2_attention(nb2_device* dev, const float* q, const float* k, const float* v, float* out, int64_t batch,
+                  int64_t heads, int64_t tokens, int64_t head_dim, const int64_t q_strides[4],
+                  const int64_t k_strides[4], const int64_t v_strides[4], const int64_t out_strides[3],
+                  int scale_mode, float scale);
+/* SPPF, the YOLO spatial-pyramid block as one pass: y [n,(chain+1)*c,h,w] =
+ * Concat over channels of [x, m1, ..., m_chain], m_l the k x k stride-1
+ * pad-k/2 MaxPool of m_{l-1} (m0 = x) with the reference's MaxPool semantics
+ * (src/kernels/max_pool.cpp:207-235) and Concat layout (src/kernels/concat.cpp).
+ * Replaces `chain` MaxPool rows and one Concat row; k odd, h*w <= 6144. */
+int nb2_sppf(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, int64_t k, int64_t chain);
 /* AveragePool 2-D (src/kernels/average_pool.cpp:128-225): x [n,c,h,w] ->
  * y [n,c,oh,ow], explicit pads {top, left, bottom, right}; the divisor counts
  * the padded window when count_include_pad, else the in-range taps. */
@@ -276,6 +295,9 @@ typedef struct nb2_model nb2_model;
  * layout-free elementwise rows is kept channels-last (NHWC) inside the arena;
  * graph inputs and outputs are NCHW either way. */
 #define NB2_MODEL_NCHW_ONLY 4
+/* Run attention chains (MatMul Q K^T, scale, Softmax, MatMul with V) as
+ * separate rows instead of the fused attention step. */
+#define NB2_MODEL_NO_ATTENTION 8
 
 int nb2_model_create(const void* onnx, int64_t size, int n_inputs, const char* const* input_names,
                      const int64_t* dims_flat, const int* ranks, int ordinal, int flags, nb2_model** out);

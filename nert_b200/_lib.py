@@ -81,6 +81,9 @@ _SIGS = {
                                   vp, c_i64p, ctypes.c_int]),
     "nb2_maxpool2d": (ctypes.c_int, [vp, vp, c_i64p, vp, c_i64p, c_i64p, c_i64p, c_i64p, c_i64p]),
     "nb2_avgpool2d": (ctypes.c_int, [vp, vp, c_i64p, vp, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_int]),
+    "nb2_sppf": (ctypes.c_int, [vp, vp, c_i64p, vp, ctypes.c_int64, ctypes.c_int64]),
+    "nb2_attention": (ctypes.c_int, [vp, vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                     ctypes.c_int64, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_int, ctypes.c_float]),
     "nb2_row_mean": (ctypes.c_int, [vp, vp, ctypes.c_int64, ctypes.c_int64, vp]),
     "nb2_softmax": (ctypes.c_int, [vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
     "nb2_layernorm": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_float]),

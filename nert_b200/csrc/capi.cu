@@ -592,6 +592,38 @@ int nb2_maxpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], floa
     });
 }
 
+int nb2_attention(nb2_device* dev, const float* q, const float* k, const float* v, float* out, int64_t batch,
+                  int64_t heads, int64_t tokens, int64_t head_dim, const int64_t q_strides[4],
+                  const int64_t k_strides[4], const int64_t v_strides[4], const int64_t out_strides[3],
+                  int scale_mode, float scale) {
+    return guard([&] {
+        need(q && k && v && out && q_strides && k_strides && v_strides && out_strides, "Attention: null argument");
+        need(batch >= 0 && heads >= 0, "Attention: negative dimension");
+        need(head_dim == 64, "Attention: the fused kernel takes a head dimension of 64");
+        need(tokens >= 1 && tokens <= kAttnMaxT, "Attention: between 1 and 208 tokens");
+        need(scale_mode >= 0 && scale_mode <= 2, "Attention: scale_mode is 0, 1 or 2");
+        need(scale_mode != 2 || scale != 0.0f, "Attention: division by zero scale");
+        const AttnGeom g{batch,        heads,        tokens,       q_strides[0], q_strides[1], q_strides[2],
+                         q_strides[3], k_strides[0], k_strides[1], k_strides[2], k_strides[3], v_strides[0],
+                         v_strides[1], v_strides[2], v_strides[3], out_strides[0], out_strides[1],
+                         out_strides[2], scale_mode,   scale};
+        bind(dev);
+        attention(dev, g, q, k, v, out);
+    });
+}
+
+int nb2_sppf(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, int64_t k, int64_t chain) {
+    return guard([&] {
+        need(x_dims != nullptr && x != nullptr && y != nullptr, "SPPF: null argument");
+        const SppfGeom g{x_dims[0], x_dims[1], x_dims[2], x_dims[3], k, chain};
+        need(g.N >= 0 && g.C >= 0 && g.H >= 0 && g.W >= 0, "SPPF: negative dimension");
+        need(k > 0 && k % 2 == 1 && chain >= 1, "SPPF: the window must be odd and the cascade at least one pool");
+        need(g.H * g.W <= kSppfMaxPlane, "SPPF: plane larger than 6144 elements");
+        bind(dev);
+        sppf_nchw(dev, g, x, y);
+    });
+}
+
 int nb2_avgpool2d(nb2_device* dev, const float* x, const int64_t x_dims[4], float* y, const int64_t y_dims[4],
                   const int64_t kernel[2], const int64_t strides[2], const int64_t pads[4], int count_include_pad) {
     return guard([&] {

@@ -39,6 +39,12 @@ struct ExecNode {
     int pos = 0;
     bool alias = false; // output is a view of input 0
     int group = 1;      // nodes in the group
+    int pool_k = 0, chain = 0; // SPPF: window and cascade length
+    // Attention: scale applied to Q K^T (0 none, 1 Mul, 2 Div) and whether the
+    // head-merge Transpose + Reshape were absorbed ([B, T, H*D] output)
+    int attn_mode = 0;
+    float attn_scale = 1.f;
+    bool attn_merged = false;
     // a MatMul whose (Reshape +) Transpose consumer was absorbed: the
     // contraction writes its result straight into the transposed layout
     std::vector<int64_t> view, perm;
@@ -139,7 +145,7 @@ bool is_alias_op(const std::string& op) {
 }
 
 std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInfo>& shapes, bool enable,
-                           int64_t& fused_groups) {
+                           int64_t& fused_groups, bool attention_on) {
     std::map<std::string, std::vector<int>> consumers;
     for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
         for (const auto& in : g.nodes[i].inputs) {
@@ -166,8 +172,224 @@ std::vector<ExecNode> fuse(const Graph& g, const std::map<std::string, TensorInf
     };
     std::vector<ExecNode> list;
     fused_groups = 0;
+    // SPPF: a Concat over channels of [t, m1, ..., mL] where m_l is a k x k,
+    // stride-1, pad k/2 MaxPool of m_{l-1} (m0 = t) read only by the next pool
+    // and the Concat becomes one pass over t (sppf_nchw); the pools are
+    // absorbed into the Concat's node
+    std::map<int, std::pair<std::string, std::pair<int64_t, int64_t>>> sppf; // concat -> (t, (k, L))
+    if (enable) {
+        std::map<std::string, int> producer;
+        for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+            for (const auto& o : g.nodes[i].outputs) {
+                producer[o] = i;
+            }
+        }
+        auto same_pool = [&](const Node& p, int64_t& k) {
+            const std::vector<int64_t> ks = p.getints("kernel_shape"), st = p.getints("strides"),
+                                       dl = p.getints("dilations"), pd = p.getints("pads");
+            if (p.op != "MaxPool" || p.outputs.size() != 1 || ks.size() != 2 || ks[0] != ks[1] || ks[0] % 2 == 0 ||
+                p.gets("auto_pad", "NOTSET") != "NOTSET") {
+                return false;
+            }
+            k = ks[0];
+            const int64_t r = k / 2;
+            const bool s1 = st.empty() || (st.size() == 2 && st[0] == 1 && st[1] == 1);
+            const bool d1 = dl.empty() || (dl.size() == 2 && dl[0] == 1 && dl[1] == 1);
+            const bool pr = pd.size() == 4 && pd[0] == r && pd[1] == r && pd[2] == r && pd[3] == r;
+            return s1 && d1 && (pr || (r == 0 && pd.empty()));
+        };
+        for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+            const Node& cat = g.nodes[i];
+            if (cat.op != "Concat" || cat.inputs.size() < 2 || cat.outputs.size() != 1) {
+                continue;
+            }
+            const std::string& t = cat.inputs[0];
+            const auto td = shapes.find(t);
+            const int64_t axis = cat.geti("axis", 0);
+            if (td == shapes.end() || td->second.dims.size() != 4 || td->second.dtype != DType::F32 ||
+                (axis != 1 && axis != -3) || td->second.dims[2] * td->second.dims[3] > kSppfMaxPlane) {
+                continue;
+            }
+            int64_t k = 0;
+            bool ok = true;
+            std::vector<int> pools;
+            for (size_t l = 1; l < cat.inputs.size() && ok; ++l) {
+                const std::string& m = cat.inputs[l];
+                auto pi = producer.find(m);
+                int64_t kl = 0;
+                ok = pi != producer.end() && same_pool(g.nodes[pi->second], kl) && (l == 1 || kl == k) &&
+                     g.nodes[pi->second].inputs[0] == cat.inputs[l - 1] && !outputs.count(m);
+                if (!ok) {
+                    break;
+                }
+                k = kl;
+                // read by the Concat once and, before the last, by the next pool
+                const auto& cs = consumers[m];
+                const bool last = l + 1 == cat.inputs.size();
+                ok = last ? (cs.size() == 1 && cs[0] == i)
+                          : (cs.size() == 2 && ((cs[0] == i && producer[cat.inputs[l + 1]] == cs[1]) ||
+                                                (cs[1] == i && producer[cat.inputs[l + 1]] == cs[0])));
+                pools.push_back(pi->second);
+            }
+            if (!ok) {
+                continue;
+            }
+            for (int p : pools) {
+                absorbed[p] = true;
+            }
+            sppf[i] = {t, {k, static_cast<int64_t>(pools.size())}};
+        }
+    }
+    // Attention: MatMul(q, k) [-> Div / Mul by a float scalar] -> Softmax over
+    // the last axis -> MatMul(., v) [-> Transpose(0, 2, 1, 3) -> Reshape to
+    // [B, T, H*D]] with q, v [B, H, T, 64], k [B, H, 64, T], T <= 208 and every
+    // intermediate read only by the next node: one fused step (ops_attn.cu)
+    struct AttnMatch {
+        std::string q, k, v, out;
+        int mode;
+        float scale;
+        bool merged;
+    };
+    std::map<int, AttnMatch> attn; // index of the chain's last node -> match
+    if (enable && attention_on) {
+        std::map<std::string, int> producer;
+        for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+            for (const auto& o : g.nodes[i].outputs) {
+                producer[o] = i;
+            }
+        }
+        auto only_reader = [&](const std::string& t) -> int {
+            if (outputs.count(t)) {
+                return -1;
+            }
+            auto it = consumers.find(t);
+            return it == consumers.end() || it->second.size() != 1 ? -1 : it->second[0];
+        };
+        auto dims_of = [&](const std::string& t) -> const std::vector<int64_t>* {
+            auto it = shapes.find(t);
+            return it == shapes.end() || it->second.dtype != DType::F32 ? nullptr : &it->second.dims;
+        };
+        for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
+            const Node& sm = g.nodes[i];
+            if (sm.op != "Softmax" || sm.inputs.empty() || sm.outputs.size() != 1 || absorbed[i]) {
+                continue;
+            }
+            const std::vector<int64_t>* sd = dims_of(sm.inputs[0]);
+            if (!sd || sd->size() != 4) {
+                continue;
+            }
+            const int64_t axis = sm.geti("axis", g.opset >= 13 ? -1 : 1);
+            if (axis != -1 && axis != 3) {
+                continue;
+            }
+            // producer chain upstream of the Softmax
+            auto pi = producer.find(sm.inputs[0]);
+            if (pi == producer.end() || only_reader(sm.inputs[0]) != i) {
+                continue;
+            }
+            int scale_node = -1, mode = 0;
+            float scale = 1.f;
+            int qk = pi->second;
+            if (g.nodes[qk].op == "Div" || g.nodes[qk].op == "Mul") {
+                const Node& dv = g.nodes[qk];
+                auto c = g.constants.find(dv.inputs.size() == 2 ? dv.inputs[1] : std::string());
+                if (c == g.constants.end() || c->second.dtype != DType::F32 || c->second.count() != 1) {
+                    continue;
+                }
+                std::memcpy(&scale, c->second.bytes.data(), 4);
+                mode = dv.op == "Mul" ? 1 : 2;
+                if (mode == 2 && scale == 0.f) {
+                    continue;
+                }
+                scale_node = qk;
+                auto pq = producer.find(dv.inputs[0]);
+                if (pq == producer.end() || only_reader(dv.inputs[0]) != qk) {
+                    continue;
+                }
+                qk = pq->second;
+            }
+            const Node& mq = g.nodes[qk];
+            if (mq.op != "MatMul" || absorbed[qk] || g.constants.count(mq.inputs[0]) ||
+                g.constants.count(mq.inputs[1])) {
+                continue;
+            }
+            const int av = only_reader(sm.outputs[0]);
+            if (av < 0 || g.nodes[av].op != "MatMul" || g.nodes[av].inputs[0] != sm.outputs[0] ||
+                g.constants.count(g.nodes[av].inputs[1])) {
+                continue;
+            }
+            const std::vector<int64_t>*qd = dims_of(mq.inputs[0]), *kd = dims_of(mq.inputs[1]),
+                                 *vd = dims_of(g.nodes[av].inputs[1]), *od = dims_of(g.nodes[av].outputs[0]);
+            if (!qd || !kd || !vd || !od || qd->size() != 4) {
+                continue;
+            }
+            const int64_t B = (*qd)[0], H = (*qd)[1], T = (*qd)[2], D = (*qd)[3];
+            if (D != 64 || T < 1 || T > kAttnMaxT || *kd != std::vector<int64_t>{B, H, D, T} ||
+                *vd != std::vector<int64_t>{B, H, T, D} || *od != std::vector<int64_t>{B, H, T, D}) {
+                continue;
+            }
+            AttnMatch m{mq.inputs[0], mq.inputs[1], g.nodes[av].inputs[1], g.nodes[av].outputs[0], mode, scale, false};
+            int last = av;
+            // the head merge: Transpose(0, 2, 1, 3) -> Reshape [B, T, H*D]
+            const int tr = only_reader(m.out);
+            if (tr >= 0 && g.nodes[tr].op == "Transpose" &&
+                g.nodes[tr].getints("perm") == std::vector<int64_t>{0, 2, 1, 3}) {
+                const int rs = only_reader(g.nodes[tr].outputs[0]);
+                const std::vector<int64_t>* rd = rs >= 0 ? dims_of(g.nodes[rs].outputs[0]) : nullptr;
+                if (rs >= 0 && g.nodes[rs].op == "Reshape" && g.nodes[rs].inputs[0] == g.nodes[tr].outputs[0] && rd &&
+                    *rd == std::vector<int64_t>{B, T, H * D}) {
+                    absorbed[tr] = absorbed[rs] = true;
+                    m.out = g.nodes[rs].outputs[0];
+                    m.merged = true;
+                    last = rs;
+                }
+            }
+            absorbed[qk] = absorbed[i] = absorbed[av] = true;
+            if (scale_node >= 0) {
+                absorbed[scale_node] = true;
+            }
+            attn[last] = m;
+        }
+    }
+    // the chain's output is produced where its last node was
+    for (auto& kv : attn) {
+        absorbed[kv.first] = false;
+    }
     for (int i = 0; i < static_cast<int>(g.nodes.size()); ++i) {
         if (absorbed[i]) {
+            continue;
+        }
+        if (attn.count(i)) {
+            const AttnMatch& m = attn[i];
+            ExecNode e;
+            e.node = &g.nodes[i];
+            e.op = "Attention";
+            e.pos = i;
+            e.ins = {m.q, m.k, m.v};
+            e.outs = {m.out};
+            e.out = m.out;
+            e.attn_mode = m.mode;
+            e.attn_scale = m.scale;
+            e.attn_merged = m.merged;
+            e.group = 3 + (m.mode != 0 ? 1 : 0) + (m.merged ? 2 : 0);
+            ++fused_groups;
+            list.push_back(std::move(e));
+            continue;
+        }
+        if (sppf.count(i)) {
+            const Node& cat = g.nodes[i];
+            ExecNode e;
+            e.node = &cat;
+            e.op = "SPPF";
+            e.pos = i;
+            e.ins = {sppf[i].first};
+            e.outs = cat.outputs;
+            e.out = cat.outputs[0];
+            e.pool_k = static_cast<int>(sppf[i].second.first);
+            e.chain = static_cast<int>(sppf[i].second.second);
+            e.group = e.chain + 1;
+            ++fused_groups;
+            list.push_back(std::move(e));
             continue;
         }
         const Node& n = g.nodes[i];
@@ -498,7 +720,7 @@ PlanResult plan_graph(const Graph& g_, const std::map<std::string, std::vector<i
     pr.shapes = infer_shapes(g_, input_dims);
     const auto& shapes_ = pr.shapes;
     std::vector<ExecNode>& ex = pr.ex;
-    ex = fuse(g_, shapes_, (flags & kNoFusion) == 0, pr.fused_groups);
+    ex = fuse(g_, shapes_, (flags & kNoFusion) == 0, pr.fused_groups, (flags & kNoAttention) == 0);
 
     // ---- liveness over the fused list (aliases share their root's buffer)
     std::map<std::string, std::string> root;
@@ -1016,6 +1238,38 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             const auto ad = dims(n.inputs[0]), bd = dims(n.inputs[1]), yd = dims(n.outputs[0]);
             nb2_device* dev = dev_;
             st.run = [=] { binary(dev, code, dt, a, ad, b, bd, y, yd); };
+        } else if (e.op == "Attention") {
+            const auto& qd = dims(e.ins[0]);
+            const int64_t B = qd[0], H = qd[1], T = qd[2], D = qd[3];
+            AttnGeom ag{};
+            ag.B = B;
+            ag.H = H;
+            ag.T = T;
+            ag.qb = H * T * D, ag.qh = T * D, ag.qt = D, ag.qj = 1;
+            ag.kb = H * D * T, ag.kh = D * T, ag.kt = 1, ag.kj = T; // K^T [B, H, D, T]
+            ag.vb = H * T * D, ag.vh = T * D, ag.vt = D, ag.vj = 1;
+            if (e.attn_merged) {
+                ag.ob = T * H * D, ag.oh = D, ag.ot = H * D; // [B, T, H*D]
+            } else {
+                ag.ob = H * T * D, ag.oh = T * D, ag.ot = D;
+            }
+            ag.scale_mode = e.attn_mode;
+            ag.scale = e.attn_scale;
+            const float* q = F(e.ins[0]);
+            const float* k = F(e.ins[1]);
+            const float* v = F(e.ins[2]);
+            float* y = F(e.out);
+            nb2_device* dev = dev_;
+            st.label = std::string("Attention:") + n.name;
+            st.run = [=] { attention(dev, ag, q, k, v, y); };
+        } else if (e.op == "SPPF") {
+            const auto& xd = dims(e.ins[0]);
+            const SppfGeom sg{xd[0], xd[1], xd[2], xd[3], e.pool_k, e.chain};
+            const float* x = F(e.ins[0]);
+            float* y = F(e.out);
+            nb2_device* dev = dev_;
+            st.label = "SPPF:" + n.name;
+            st.run = [=] { sppf_nchw(dev, sg, x, y); };
         } else if (e.op == "MaxPool") {
             const auto& xd = dims(n.inputs[0]);
             const auto& yd = dims(n.outputs[0]);

@@ -23,8 +23,9 @@
 namespace nb2 {
 namespace eng {
 
-// kNchwOnly keeps every activation NCHW (no channels-last trunk).
-enum ModelFlags : int { kNoFusion = 1, kNoGraph = 2, kNchwOnly = 4 };
+// kNchwOnly keeps every activation NCHW (no channels-last trunk);
+// kNoAttention runs attention chains as their MatMul / Softmax rows.
+enum ModelFlags : int { kNoFusion = 1, kNoGraph = 2, kNchwOnly = 4, kNoAttention = 8 };
 
 struct IOInfo {
     std::string name;

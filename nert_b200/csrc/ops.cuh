@@ -52,6 +52,32 @@ struct AvgPoolGeom {
     int include_pad;
 };
 void avgpool2d(nb2_device* dev, const AvgPoolGeom& g, const float* x, float* y);
+// Fused attention out = Softmax(scale(Q K^T)) V per (batch, head) with head
+// dim 64 and T <= kAttnMaxT tokens; element (token t, dim j) of head (b, h)
+// sits at b*xb + h*xh + t*xt + j*xj for x = q, k, v; the output row at
+// b*ob + h*oh + t*ot with its 64 values contiguous. scale_mode: 0 none,
+// 1 multiply by `scale`, 2 divide by `scale` (the graph's Mul / Div).
+constexpr int64_t kAttnMaxT = 208;
+struct AttnGeom {
+    int64_t B, H, T;
+    int64_t qb, qh, qt, qj;
+    int64_t kb, kh, kt, kj;
+    int64_t vb, vh, vt, vj;
+    int64_t ob, oh, ot;
+    int scale_mode;
+    float scale;
+};
+void attention(nb2_device* dev, const AttnGeom& g, const float* q, const float* k, const float* v, float* out);
+size_t attention_smem_bytes(int T);
+// SPPF: y[n] = Concat over axis 1 of [x, m1, ..., m_chain] with m_l the
+// k x k, stride-1, pad k/2 MaxPool of m_{l-1} (m0 = x); x is [N][C][H][W] and
+// y [N][(chain+1)*C][H][W]. One read of each plane, kept in shared memory
+// (H*W <= kSppfMaxPlane) while the cascade runs.
+constexpr int64_t kSppfMaxPlane = 6144;
+struct SppfGeom {
+    int64_t N, C, H, W, k, chain;
+};
+void sppf_nchw(nb2_device* dev, const SppfGeom& g, const float* x, float* y);
 // The same window over channels-last x[N][H][W][C] -> y[N][OH][OW][C].
 void maxpool2d_nhwc(nb2_device* dev, const PoolGeom& g, const float* x, float* y);
 // y[n][c] = mean over the hw pixels of channels-last x[n][hw][c]

@@ -100,8 +100,11 @@ struct TilePerm {
     int64_t out_u;     // output stride of u
 };
 
+// A 32 (u) x 64 (v) tile per block and pass: each thread has eight loads in
+// flight (rows v) before the shared-memory exchange, then eight stores
+// (two 32-wide v halves of four u rows).
 __global__ void permute_tile_kernel(const float* __restrict__ x, float* __restrict__ y, TilePerm p, int64_t batches) {
-    __shared__ float tile[32][33];
+    __shared__ float tile[64][33];
     for (int64_t b = blockIdx.z; b < batches; b += gridDim.z) {
         int64_t rem = b, ib = 0, ob = 0;
         for (int d = p.nb - 1; d >= 0; --d) {
@@ -110,18 +113,26 @@ __global__ void permute_tile_kernel(const float* __restrict__ x, float* __restri
             ib += c * p.bin[d];
             ob += c * p.bout[d];
         }
-        const int64_t u0 = blockIdx.x * 32, v0 = blockIdx.y * 32;
-        for (int i = threadIdx.y; i < 32; i += 8) {
-            const int64_t v = v0 + i, u = u0 + threadIdx.x;
-            if (u < p.U && v < p.V) {
-                tile[i][threadIdx.x] = x[ib + v * p.in_v + u];
-            }
+        const int64_t u0 = blockIdx.x * 32, v0 = blockIdx.y * 64;
+        const int64_t u = u0 + threadIdx.x;
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t v = v0 + threadIdx.y + 8 * j;
+            r[j] = (u < p.U && v < p.V) ? __ldg(x + ib + v * p.in_v + u) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            tile[threadIdx.y + 8 * j][threadIdx.x] = r[j];
         }
         __syncthreads();
-        for (int i = threadIdx.y; i < 32; i += 8) {
-            const int64_t u = u0 + i, v = v0 + threadIdx.x;
-            if (u < p.U && v < p.V) {
-                y[ob + u * p.out_u + v] = tile[threadIdx.x][i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int64_t uu = u0 + threadIdx.y + 8 * (j & 3);
+            const int vl = threadIdx.x + 32 * (j >> 2);
+            const int64_t v = v0 + vl;
+            if (uu < p.U && v < p.V) {
+                y[ob + uu * p.out_u + v] = tile[vl][threadIdx.y + 8 * (j & 3)];
             }
         }
         __syncthreads();
@@ -199,6 +210,26 @@ __global__ void resize_nearest2_kernel(const T* __restrict__ x, T* __restrict__ 
         const uint32_t t = i / OW;
         const uint32_t oh = t % OH, o = t / OH;
         y[i] = x[((size_t)o * H + static_cast<uint32_t>(__ldg(lh + oh))) * W + static_cast<uint32_t>(__ldg(lw + ow))];
+    }
+}
+
+// The same for float rows with OW % 4 == 0: four outputs of one row per
+// thread and one 16-byte store (the gathers of a quad share one input row).
+__global__ void resize_nearest2_vec4_kernel(const float* __restrict__ x, float4* __restrict__ y,
+                                            const int64_t* __restrict__ lh, const int64_t* __restrict__ lw,
+                                            uint32_t H, uint32_t W, uint32_t OH, uint32_t OW4, uint32_t n4) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const uint32_t q = i % OW4;
+        const uint32_t t = i / OW4;
+        const uint32_t oh = t % OH, o = t / OH;
+        const float* row = x + ((size_t)o * H + static_cast<uint32_t>(__ldg(lh + oh))) * W;
+        const int64_t* c = lw + 4 * q;
+        float4 v;
+        v.x = __ldg(row + __ldg(c));
+        v.y = __ldg(row + __ldg(c + 1));
+        v.z = __ldg(row + __ldg(c + 2));
+        v.w = __ldg(row + __ldg(c + 3));
+        y[i] = v;
     }
 }
 
@@ -522,7 +553,7 @@ void transpose(nb2_device* dev, const void* x, void* y, const std::vector<int64_
                 batches *= cd[cperm[d]];
                 ++tp.nb;
             }
-            const int64_t gx = (tp.U + 31) / 32, gy = (tp.V + 31) / 32;
+            const int64_t gx = (tp.U + 31) / 32, gy = (tp.V + 63) / 64;
             if (gy <= 65535) {
                 const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
                                 static_cast<unsigned>(std::min<int64_t>(batches, 65535)));
@@ -670,7 +701,11 @@ void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, cons
         const auto OH = static_cast<uint32_t>(t.out_dims[a]), OW = static_cast<uint32_t>(t.out_dims[b]);
         const int64_t* lh = r.lower + t.axis_off[a];
         const int64_t* lw = r.lower + t.axis_off[b];
-        if (is_f32) {
+        if (is_f32 && OW % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+            const uint32_t n4 = static_cast<uint32_t>(n / 4);
+            resize_nearest2_vec4_kernel<<<blocks_for(dev, n4), 256, 0, dev->stream>>>(
+                static_cast<const float*>(x), static_cast<float4*>(y), lh, lw, H, W, OH, OW / 4, n4);
+        } else if (is_f32) {
             resize_nearest2_kernel<float><<<g, 256, 0, dev->stream>>>(
                 static_cast<const float*>(x), static_cast<float*>(y), lh, lw, H, W, OH, OW, static_cast<uint32_t>(n));
         } else {

@@ -152,6 +152,45 @@ __global__ void softmax_strided_kernel(const float* __restrict__ x, float* __res
     }
 }
 
+// The same for short axes (L <= LMAX, e.g. YOLO's 16 DFL bins): the column
+// is loaded once into registers with all L loads in flight, then max, sum
+// and output exactly as above (same order, same expressions).
+template <int LMAX>
+__global__ void softmax_strided_reg_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t outer, int L,
+                                           int64_t inner) {
+    const int64_t total = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = t / inner, i = t - o * inner;
+        const float* r = x + o * L * inner + i;
+        float v[LMAX];
+#pragma unroll
+        for (int k = 0; k < LMAX; ++k) {
+            v[k] = k < L ? __ldg(r + k * inner) : -INFINITY;
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < LMAX; ++k) {
+            m = k < L ? fmaxf(m, v[k]) : m;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int k = 0; k < LMAX; ++k) {
+            if (k < L) {
+                v[k] = expf(v[k] - m);
+                s += v[k];
+            }
+        }
+        const float inv = 1.0f / s;
+        float* w = y + o * L * inner + i;
+#pragma unroll
+        for (int k = 0; k < LMAX; ++k) {
+            if (k < L) {
+                w[k * inner] = v[k] * inv;
+            }
+        }
+    }
+}
+
 // Warp per row LayerNorm, D <= 1024; two-pass mean/variance in double.
 template <int PER_LANE>
 __global__ void layernorm_warp_kernel(const float* __restrict__ x, const float* __restrict__ scale,
@@ -207,8 +246,10 @@ __global__ void layernorm_warp_kernel(const float* __restrict__ x, const float* 
 // stores, two-pass mean / centred variance in fp32 from registers (the
 // reference's double sums differ from these by rounding far below the fp32
 // output's own precision).
+// Up to D = 768 the kernel is held to 48 registers so five 256-thread blocks
+// fit an SM and a ViT-B row count (6304 rows at b32) runs in one wave.
 template <int V4>
-__global__ void layernorm_warp4_kernel(const float4* __restrict__ x, const float4* __restrict__ scale,
+__global__ void __launch_bounds__(256, V4 <= 6 ? 5 : 1) layernorm_warp4_kernel(const float4* __restrict__ x, const float4* __restrict__ scale,
                                        const float4* __restrict__ bias, float4* __restrict__ y,
                                        float* __restrict__ mean_out, float* __restrict__ inv_out, uint32_t rows,
                                        float eps) {
@@ -343,7 +384,15 @@ void softmax(nb2_device* dev, const float* x, float* y, int64_t outer, int64_t L
     } else {
         const int64_t total = outer * inner;
         const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, dev->num_sms * 32));
-        softmax_strided_kernel<<<blocks, 256, 0, dev->stream>>>(x, y, outer, L, inner);
+        if (L <= 8) {
+            softmax_strided_reg_kernel<8><<<blocks, 256, 0, dev->stream>>>(x, y, outer, static_cast<int>(L), inner);
+        } else if (L <= 16) {
+            softmax_strided_reg_kernel<16><<<blocks, 256, 0, dev->stream>>>(x, y, outer, static_cast<int>(L), inner);
+        } else if (L <= 32) {
+            softmax_strided_reg_kernel<32><<<blocks, 256, 0, dev->stream>>>(x, y, outer, static_cast<int>(L), inner);
+        } else {
+            softmax_strided_kernel<<<blocks, 256, 0, dev->stream>>>(x, y, outer, L, inner);
+        }
     }
     check_cuda(cudaGetLastError(), "softmax launch");
 }

@@ -120,8 +120,23 @@ __global__ void __launch_bounds__(kMeanRows) row_mean_staged_kernel(const float*
     const int n4 = ((reinterpret_cast<uintptr_t>(src) & 15) == 0) ? n / 4 : 0;
     const float4* s4 = reinterpret_cast<const float4*>(src);
     float4* d4 = reinterpret_cast<float4*>(sm);
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-        d4[i] = __ldg(s4 + i);
+    // every 16-byte load of the thread (at most 16) in flight before the
+    // shared stores
+    constexpr int kPer = kMeanRows * kMeanInner / 4 / kMeanRows;
+    float4 v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i4 = threadIdx.x + j * kMeanRows;
+        if (i4 < n4) {
+            v[j] = __ldg(s4 + i4);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const int i4 = threadIdx.x + j * kMeanRows;
+        if (i4 < n4) {
+            d4[i4] = v[j];
+        }
     }
     for (int i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
         sm[i] = __ldg(src + i);
@@ -405,6 +420,78 @@ void avgpool2d(nb2_device* dev, const AvgPoolGeom& g, const float* x, float* y) 
     const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(dev->num_sms) * 32);
     avgpool2d_kernel<<<static_cast<unsigned>(blocks), 256, 0, dev->stream>>>(x, y, g, total);
     check_cuda(cudaGetLastError(), "avgpool launch");
+}
+
+namespace {
+
+// One CTA per (n, c) plane at a time: the plane is read once into shared
+// memory, then each pool of the cascade is a row pass (max over the in-range
+// columns w-r..w+r) and a column pass (rows h-r..h+r) between two shared
+// buffers; the column pass writes its slice of the Concat. Max over in-range
+// taps of a separable window is the max of row maxima, so every slice equals
+// the reference's one-window-at-a-time MaxPool (src/kernels/max_pool.cpp:207-235:
+// `v > best` from -inf, NaN never taken).
+__global__ void __launch_bounds__(128) sppf_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t planes,
+                                                   int64_t C, int H, int W, int r, int chain) {
+    extern __shared__ float sppf_smem[];
+    const int hw = H * W;
+    float* a = sppf_smem;
+    float* b = sppf_smem + hw;
+    const int64_t slice = C * hw;
+    for (int64_t p = blockIdx.x; p < planes; p += gridDim.x) {
+        const int64_t n = p / C, c = p % C;
+        const float* xp = x + p * hw;
+        float* yp = y + (n * (chain + 1) * C + c) * hw;
+        __syncthreads(); // the previous plane's readers of a are done
+        for (int i = threadIdx.x; i < hw; i += blockDim.x) {
+            const float v = __ldg(xp + i);
+            a[i] = v;
+            yp[i] = v;
+        }
+        for (int l = 1; l <= chain; ++l) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < hw; i += blockDim.x) {
+                const int h = i / W, w = i - h * W;
+                const int w0 = w - r < 0 ? 0 : w - r, w1 = w + r >= W ? W - 1 : w + r;
+                const float* row = a + h * W;
+                float best = -INFINITY;
+                for (int q = w0; q <= w1; ++q) {
+                    best = row[q] > best ? row[q] : best;
+                }
+                b[i] = best;
+            }
+            __syncthreads();
+            float* ys = yp + l * slice;
+            for (int i = threadIdx.x; i < hw; i += blockDim.x) {
+                const int h = i / W, w = i - h * W;
+                const int h0 = h - r < 0 ? 0 : h - r, h1 = h + r >= H ? H - 1 : h + r;
+                float best = -INFINITY;
+                for (int q = h0; q <= h1; ++q) {
+                    const float v = b[q * W + w];
+                    best = v > best ? v : best;
+                }
+                a[i] = best;
+                ys[i] = best;
+            }
+        }
+    }
+}
+
+} // namespace
+
+void sppf_nchw(nb2_device* dev, const SppfGeom& g, const float* x, float* y) {
+    if (g.H * g.W > kSppfMaxPlane || g.k % 2 == 0 || g.k < 1 || g.chain < 1) {
+        fail(kStatusInvalid, "SPPF: needs an odd window and a plane of at most 6144 elements");
+    }
+    const int64_t planes = g.N * g.C;
+    if (planes == 0 || g.H * g.W == 0) {
+        return;
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(planes, static_cast<int64_t>(dev->num_sms) * 16));
+    const size_t smem = static_cast<size_t>(2 * g.H * g.W) * sizeof(float);
+    sppf_kernel<<<grid, 128, smem, dev->stream>>>(x, y, planes, g.C, static_cast<int>(g.H), static_cast<int>(g.W),
+                                                  static_cast<int>(g.k / 2), static_cast<int>(g.chain));
+    check_cuda(cudaGetLastError(), "sppf launch");
 }
 
 void maxpool2d(nb2_device* dev, const PoolGeom& g, const float* x, float* y) {

@@ -18,7 +18,7 @@ import numpy as np
 from . import _lib, onnx_io
 from ._lib import check, lib
 
-NO_FUSION, NO_GRAPH, NCHW_ONLY = 1, 2, 4
+NO_FUSION, NO_GRAPH, NCHW_ONLY, NO_ATTENTION = 1, 2, 4, 8
 _NP = {0: np.float32, 1: np.int64, 2: np.bool_}
 
 _EXTRA = {
@@ -118,12 +118,13 @@ class Model:
     """One graph on one GPU for one input shape (nert::Model on B200)."""
 
     def __init__(self, graph, input_dims: dict, device: int = 0, fuse: bool = True, cuda_graph: bool = True,
-                 channels_last: bool = True):
-        """channels_last=False keeps every activation NCHW (no NHWC conv trunk)."""
+                 channels_last: bool = True, fused_attention: bool = True):
+        """channels_last=False keeps every activation NCHW (no NHWC conv trunk);
+        fused_attention=False runs attention chains as separate rows."""
         data = _onnx_bytes(graph)
         n, c_names, c_dims, c_ranks = _dims_args(input_dims)
         flags = ((0 if fuse else NO_FUSION) | (0 if cuda_graph else NO_GRAPH) |
-                 (0 if channels_last else NCHW_ONLY))
+                 (0 if channels_last else NCHW_ONLY) | (0 if fused_attention else NO_ATTENTION))
         h = ctypes.c_void_p()
         check(lib().nb2_model_create(data, len(data), n, c_names, c_dims, c_ranks, device, flags, ctypes.byref(h)))
         self._h = h.value

@@ -159,8 +159,16 @@ def test_vit_gelu_and_scale_fusion_plan():
     a = nbm.analyze(g, {"input": [2, 3, 224, 224]})
     rows = {e["name"]: e for e in a["exec"]}
     assert rows["blk0.fc1"]["group"] == 7 and rows["blk0.fc1"]["act"] == 4  # bias + erf-form GELU
-    assert rows["blk0.qk"]["group"] == 2  # / sqrt(64) as the epilogue scale
-    assert not any(e["op"] in ("Erf", "Div") for e in a["exec"])
+    # QK^T, / sqrt(64), Softmax, AV and the head merge: one fused attention step
+    assert rows["blk0.ctx"]["op"] == "Attention" and rows["blk0.ctx"]["group"] == 6
+    assert not any(e["op"] in ("Erf", "Div", "Softmax", "MatMul") and e["name"].startswith("blk0.")
+                   and e["name"] not in ("blk0.q", "blk0.k", "blk0.v", "blk0.proj", "blk0.fc1", "blk0.fc2")
+                   for e in a["exec"])
+    # without the fused step the scale is the QK^T contraction's epilogue alpha
+    b = nbm.analyze(g, {"input": [2, 3, 224, 224]}, flags=nbm.NO_ATTENTION)
+    rows = {e["name"]: e for e in b["exec"]}
+    assert rows["blk0.qk"]["group"] == 2
+    assert not any(e["op"] in ("Erf", "Div", "Attention") for e in b["exec"])
 
 
 def test_vit_head_transposes_written_in_place_plan():
@@ -170,7 +178,7 @@ def test_vit_head_transposes_written_in_place_plan():
     from nert_b200 import configs
 
     g = configs.vit_b16(2, layers=2)
-    a = nbm.analyze(g, {"input": [2, 3, 224, 224]})
+    a = nbm.analyze(g, {"input": [2, 3, 224, 224]}, flags=nbm.NO_ATTENTION)
     rows = {e["name"]: e for e in a["exec"]}
     for b in ("blk0", "blk1"):
         assert rows[f"{b}.q"]["group"] == 4 and rows[f"{b}.q"]["perm"] == [0, 2, 1, 3]
@@ -217,3 +225,57 @@ def test_batchnorm_without_conv_stays_a_row():
     g.add_output(y, None, FLOAT)
     a = nbm.analyze(g, {"x": [2, 5, 3, 4]})
     assert [e["op"] for e in a["exec"]][-1] == "BatchNormalization"
+
+
+def test_sppf_cascade_planned_as_one_pass():
+    """YOLO's SPPF (three 5x5/s1 MaxPools and the Concat of the four tensors)
+    plans as one SPPF step reading only the first tensor; the pools' outputs
+    get no buffer."""
+    g = configs.yolov8n(2)
+    a = nbm.analyze(g, {"images": [2, 3, 640, 640]})
+    sppf = [e for e in a["exec"] if e["op"] == "SPPF"]
+    assert len(sppf) == 1 and sppf[0]["name"] == "sppf.cat" and sppf[0]["group"] == 4
+    assert not any(e["name"].startswith("sppf.m") for e in a["exec"])
+
+
+def test_sppf_not_fused_when_a_pool_output_has_another_reader():
+    g = Graph(opset=13)
+    x = g.add_input("x", [1, 4, 8, 8])
+    m1 = g.op("MaxPool", [x], name="m1", kernel_shape=[5, 5], strides=[1, 1], pads=[2, 2, 2, 2])
+    m2 = g.op("MaxPool", [m1], name="m2", kernel_shape=[5, 5], strides=[1, 1], pads=[2, 2, 2, 2])
+    c = g.op("Concat", [x, m1, m2], name="cat", axis=1)
+    g.add_output(c, None, FLOAT)
+    g.add_output(g.op("Relu", [m1], name="side"), None, FLOAT)
+    a = nbm.analyze(g, {"x": [1, 4, 8, 8]})
+    assert not any(e["op"] == "SPPF" for e in a["exec"])
+    # a stride-2 pool in the chain is not a "same" window either
+    g2 = Graph(opset=13)
+    x = g2.add_input("x", [1, 4, 8, 8])
+    m1 = g2.op("MaxPool", [x], name="m1", kernel_shape=[3, 3], strides=[1, 1], pads=[1, 1, 1, 1])
+    c = g2.op("Concat", [x, m1], name="cat", axis=1)
+    g2.add_output(c, None, FLOAT)
+    assert any(e["op"] == "SPPF" for e in nbm.analyze(g2, {"x": [1, 4, 8, 8]})["exec"])
+
+
+def test_attention_fusion_limits():
+    """The fused attention step needs head dim 64 and at most 208 tokens;
+    other chains stay MatMul / Softmax rows."""
+    from nert_b200 import synth
+
+    def chain(T, D, merge=True):
+        g = Graph(opset=13)
+        q = g.add_input("q", [2, 3, T, D])
+        k = g.add_input("k", [2, 3, D, T])
+        v = g.add_input("v", [2, 3, T, D])
+        s = g.op("Div", [g.op("MatMul", [q, k], name="qk"), g.const("c", np.array(8.0, np.float32))], name="sc")
+        o = g.op("MatMul", [g.op("Softmax", [s], name="sm", axis=-1), v], name="av")
+        if merge:
+            o = g.op("Reshape", [g.op("Transpose", [o], name="t", perm=[0, 2, 1, 3]),
+                                 g.const("m", np.array([2, T, 3 * D], np.int64))], name="merge")
+        g.add_output(o, None, FLOAT)
+        return nbm.analyze(g, {"q": [2, 3, T, D], "k": [2, 3, D, T], "v": [2, 3, T, D]})["exec"]
+
+    assert [e["op"] for e in chain(197, 64)] == ["Attention"]
+    assert [e["op"] for e in chain(5, 64, merge=False)] == ["Attention"]
+    assert "Attention" not in [e["op"] for e in chain(209, 64)]
+    assert "Attention" not in [e["op"] for e in chain(50, 32)]

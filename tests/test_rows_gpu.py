@@ -284,3 +284,46 @@ def test_conv_transpose_engine(cuda, case):
     got = run_engine(g, {"x": x})[y]
     assert got.shape == ref.shape
     assert rel_err(got, ref) <= TOL
+
+
+@pytest.mark.parametrize("shape,k,chain", [((16, 128, 20, 20), 5, 3), ((2, 7, 13, 9), 3, 2), ((1, 3, 1, 1), 5, 1),
+                                          ((3, 5, 40, 41), 5, 3)], ids=["yolo_b16", "ragged", "one_pixel", "p4"])
+def test_sppf_fused_bit_exact(cuda, shape, k, chain):
+    """The SPPF step (one pass per plane, ops_pool.cu) against the reference
+    MaxPool cascade and Concat, bit-exact; the plan must have fused it."""
+    from nert_b200 import model as nbm
+
+    g = Graph(opset=13)
+    x = g.add_input("x", list(shape))
+    ins, cur = [x], x
+    for l in range(chain):
+        cur = g.op("MaxPool", [cur], name=f"m{l + 1}", kernel_shape=[k, k], strides=[1, 1], pads=[k // 2] * 4)
+        ins.append(cur)
+    g.add_output(g.op("Concat", ins, name="cat", axis=1), None, FLOAT)
+    assert [e["op"] for e in nbm.analyze(g, {"x": list(shape)})["exec"]] == ["SPPF"]
+    xv = synth.normal(shape, 1.0, 123)
+    xv.ravel()[::17] = -np.inf  # in-range -inf taps stay -inf only where the whole window is
+    ref = np_ref.run(g, {"x": xv})
+    got = run_engine(g, {"x": xv})
+    np.testing.assert_array_equal(list(got.values())[0], list(ref.values())[0])
+
+
+def test_sppf_c_abi_matches_rows(cuda):
+    """nb2_sppf through the C ABI against the unfused MaxPool rows."""
+    import torch
+
+    from nert_b200 import _lib
+    from nert_b200._lib import i64s
+
+    L, dev = _lib.lib(), _lib.device(0)
+    x = torch.randn(4, 32, 20, 20, device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    y = torch.empty(4, 128, 20, 20, device="cuda")
+    _lib.check(L.nb2_sppf(dev, x.data_ptr(), i64s(x.shape), y.data_ptr(), 5, 3))
+    _lib.check(L.nb2_device_synchronize(dev))
+    cur, want = x, [x]
+    for _ in range(3):
+        cur = torch.nn.functional.max_pool2d(cur, 5, 1, 2)
+        want.append(cur)
+    assert torch.equal(y, torch.cat(want, 1))
+    # invalid arguments are refused before any launch
+    assert L.nb2_sppf(dev, x.data_ptr(), i64s(x.shape), y.data_ptr(), 4, 3) != 0
