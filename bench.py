@@ -914,6 +914,22 @@ def main():
             nm = row_name(lab)
             op += " (attention)" if (".qk" in nm or ".av" in nm or "attn" in nm) else ""
         by_op[op] = round(by_op.get(op, 0.0) + ms, 4)
+    # the fused attention step (its two contractions, 4*B*H*T^2*D FLOP, plus
+    # the softmax), reported apart from the contraction kernel's roofline
+    attn = None
+    attn_flop = 0.0
+    for e in analysis["exec"]:
+        if e["op"] == "Attention":
+            b_, h_, t_, d_ = analysis["tensors"][e["ins"][0]]["dims"]
+            attn_flop += 4.0 * b_ * h_ * t_ * t_ * d_
+    if attn_flop:
+        a_eager = sum(ms for lab, ms in sums.items() if lab.startswith("Attention:"))
+        a_time = mean_dev * (a_eager / total_prof if total_prof else 0.0)
+        a_tf = attn_flop / (a_time * 1e-3) / 1e12 if a_time > 0 else None
+        attn = {"kernel": "attention_kernel (fused QK^T, scale, softmax, PV on tcgen05, 3xTF32)",
+                "flops_per_step": attn_flop, "kernel_ms_per_step": a_time, "achieved": a_tf,
+                "unit": "TFLOP/s", "frac": (a_tf / tensor_peak(args.precision)[0]) if a_tf else None,
+                "note": "FLOPs of the two contractions only; the softmax between them runs on the CUDA cores"}
     rows_table = bandwidth_rows(local) if (rank == 0 and world == 1 and not args.no_rows) else None
 
     line = None
@@ -964,6 +980,7 @@ def main():
                          "traffic_note": "DRAM bytes read+written by the contraction launches of one step, "
                                          "from one ncu capture (profiles/resnet18_b64_igemm_dram.md)"
                          if (args.workload, batch) in TRAFFIC_BYTES else None},
+            "attention": attn,
             "top_rows_ms": [[lab, round(ms, 4)] for lab, ms in top_rows],
             "profile_ms_by_op": by_op,
             "bandwidth_rows": rows_table,

@@ -64,8 +64,9 @@ struct AttnArgs {
     long long wait_bound;
 };
 
-__device__ __forceinline__ float attn_scale(int mode, float c, float s) {
-    return mode == 1 ? s * c : (mode == 2 ? __fdiv_rn(s, c) : s);
+template <int MODE>
+__device__ __forceinline__ float attn_scale(float c, float s) {
+    return MODE == 1 ? s * c : (MODE == 2 ? __fdiv_rn(s, c) : s);
 }
 
 // Byte offset of (row, k) in a 128-byte swizzled K-major slab (32 fp32 per
@@ -82,6 +83,7 @@ struct SwzRow {
 };
 
 
+template <int MODE>
 __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) {
     extern __shared__ uint8_t attn_smem_raw[];
     const AttnGeom& g = a.g;
@@ -127,17 +129,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     if (g.kt == 1) { // K^T in memory ([d][T]): thread = key, loop over d
         const int t = tid;
         const SwzRow sr(t);
-        for (int j0 = 0; j0 < kAttnD; j0 += 8) {
-            float x[8];
+#pragma unroll 1
+        for (int j0 = 0; j0 < kAttnD; j0 += 32) { // 32 loads in flight per thread
+            float x[32];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 32; ++u) {
                 x[u] = t < T ? __ldg(kz + t + (j0 + u) * g.kj) : 0.0f;
             }
             if (t < np) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int j = j0 + u;
-                    split_store(k_hi, k_lo, static_cast<uint32_t>((j >> 5) * kslab) + sr.at(j & 31), x[u]);
+                for (int u = 0; u < 32; ++u) {
+                    split_store(k_hi, k_lo, static_cast<uint32_t>((j0 >> 5) * kslab) + sr.at(u), x[u]);
                 }
             }
         }
@@ -163,15 +165,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     if (g.vj == 1) { // [T][d]: thread = (d, key mod 4), loop over keys
         const int j = tid & 63;
         const SwzRow sr(j);
-        for (int t0 = tid >> 6; t0 < tv; t0 += 32) {
-            float x[8];
+#pragma unroll 1
+        for (int t0 = tid >> 6; t0 < tv; t0 += 128) { // 32 loads in flight per thread
+            float x[32];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 32; ++u) {
                 const int t = t0 + 4 * u;
                 x[u] = t < T ? __ldg(vz + t * g.vt + j) : 0.0f;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 32; ++u) {
                 const int t = t0 + 4 * u;
                 if (t < tv) {
                     split_store(v_hi, v_lo, static_cast<uint32_t>((t >> 5) * 8192) + sr.at(t & 31), x[u]);
@@ -208,9 +211,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
     const int c0 = half == 0 ? 0 : (nch + 1) / 2, c1 = half == 0 ? (nch + 1) / 2 : nch;
     // with a positive scale (or none) the row max of the scaled scores is the
     // scaled max of the raw ones (rounding is monotonic)
-    const int mode = g.scale_mode;
     const float sc = g.scale;
-    const bool scale_after_max = mode == 0 || sc > 0.0f;
+    const bool scale_after_max = MODE == 0 || sc > 0.0f;
     uint32_t uses = 0; // completed phases of `bar`
     bool ok = true;
 
@@ -285,30 +287,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(AttnArgs a) 
         // ---- softmax of row `row` over keys [0, T): this warp's columns,
         // the two halves combined through shared memory
         const uint32_t srow = tmem + lane_base;
+        // chunks wholly below T skip the per-key test
         float m = -INFINITY;
         for (int c = c0; c < c1; ++c) {
             float v[16];
             tmem_ld16(srow + c * 16, v);
+            if (c * 16 + 16 <= T) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float s = scale_after_max ? v[i] : attn_scale(mode, sc, v[i]);
-                m = c * 16 + i < T ? fmaxf(m, s) : m;
+                for (int i = 0; i < 16; ++i) {
+                    m = fmaxf(m, scale_after_max ? v[i] : attn_scale<MODE>(sc, v[i]));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float s = scale_after_max ? v[i] : attn_scale<MODE>(sc, v[i]);
+                    m = c * 16 + i < T ? fmaxf(m, s) : m;
+                }
             }
         }
         red_max[half * 128 + row] = m;
         __syncthreads();
         m = fmaxf(red_max[row], red_max[128 + row]);
         if (scale_after_max) {
-            m = attn_scale(mode, sc, m);
+            m = attn_scale<MODE>(sc, m);
         }
         float sum = 0.0f;
         for (int c = c0; c < c1; ++c) {
             float v[16];
             tmem_ld16(srow + c * 16, v);
+            if (c * 16 + 16 <= T) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                v[i] = c * 16 + i < T ? expf(attn_scale(mode, sc, v[i]) - m) : 0.0f;
-                sum += v[i];
+                for (int i = 0; i < 16; ++i) {
+                    v[i] = expf(attn_scale<MODE>(sc, v[i]) - m);
+                    sum += v[i];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    v[i] = c * 16 + i < T ? expf(attn_scale<MODE>(sc, v[i]) - m) : 0.0f;
+                    sum += v[i];
+                }
             }
             tmem_st16(srow + c * 16, v);
         }
@@ -412,9 +430,10 @@ void attention(nb2_device* dev, const AttnGeom& g, const float* q, const float* 
     const size_t smem = attention_smem_bytes(static_cast<int>(g.T));
     static size_t attr_bytes[64] = {};
     if (attr_bytes[dev->ordinal] < smem) {
-        check_cuda(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)),
-                   "cudaFuncSetAttribute(attention)");
+        for (auto fn : {attention_kernel<0>, attention_kernel<1>, attention_kernel<2>}) {
+            check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                       "cudaFuncSetAttribute(attention)");
+        }
         attr_bytes[dev->ordinal] = smem;
     }
     AttnArgs a{g, q, k, v, out, dev->err_word, dev->wait_bound};
@@ -431,7 +450,14 @@ void attention(nb2_device* dev, const AttnGeom& g, const float* q, const float* 
             }
         }
     }
-    attention_kernel<<<static_cast<unsigned>(g.B * g.H), kAttnThreads, smem, dev->stream>>>(a);
+    const unsigned grid = static_cast<unsigned>(g.B * g.H);
+    if (a.g.scale_mode == 1) {
+        attention_kernel<1><<<grid, kAttnThreads, smem, dev->stream>>>(a);
+    } else if (a.g.scale_mode == 2) {
+        attention_kernel<2><<<grid, kAttnThreads, smem, dev->stream>>>(a);
+    } else {
+        attention_kernel<0><<<grid, kAttnThreads, smem, dev->stream>>>(a);
+    }
     check_cuda(cudaGetLastError(), "attention launch");
 }
 
