@@ -102,8 +102,9 @@ int nb2_device_set_wait_bound(nb2_device* dev, int64_t cycles);
 int64_t nb2_device_get_wait_bound(const nb2_device* dev);
 /* Schedule the host chose for the most recent Conv/Gemm/MatMul launch on this
  * device: output tile width (64 or 128), whether two tiles were kept in flight
- * (MMA issuers on alternate tiles), the number of K slices (1 = unsplit), the
- * A-operand mode and the number of output tiles. Any pointer may be null.
+ * (MMA issuers on alternate tiles), the number of K slices (1 = unsplit; 0 =
+ * the balanced split, every CTA an equal span of all (tile, K block) pairs),
+ * the A-operand mode and the number of output tiles. Any pointer may be null.
  * Diagnostics for tests and tuning; the reference has no counterpart (cuDNN
  * and cuBLAS pick their algorithms internally, src/cuda/conv.cu:230-530). */
 int nb2_device_last_contraction(const nb2_device* dev, int* tile_n, int* two_in_flight, int* k_slices, int* a_mode,

@@ -54,6 +54,13 @@ struct Args {
     // raw fp32 partial sums to part[((ks*zcount + z)*M + row)*N + col] and a
     // second kernel reduces them and applies the real epilogue
     int ksplit, kper;
+    // balanced split (stream > 0): the (tile, K block) pairs in tile-major
+    // order, sk_total of them, are cut into equal spans of sk_span, one per
+    // CTA; a unit is the part of one tile inside a CTA's span. Units that
+    // cover a whole tile take the normal epilogue; the others write raw
+    // partials to part[(cta * 2 + slot) * 128 * BN] (slot 0: the span's first
+    // unit, 1: its last) and streamk_reduce_kernel finishes those tiles.
+    int stream, sk_span, sk_total;
     float* part;
     int zcount; // batch / group slices
     int mode;
@@ -356,10 +363,12 @@ __host__ __device__ constexpr bool tma_a_mode() {
     return MODE == kADenseTma || MODE == kAConvNhwc;
 }
 
-template <int BN, bool THREE, int MODE>
+template <int BN, bool THREE, int MODE, bool STREAM>
 // 17 or 21 warps: an SM sub-partition has 16K registers and holds 5 or 6 of
 // them, so a thread may use at most 96 or 80 registers (the launch bound
-// makes the compiler keep to that).
+// makes the compiler keep to that). STREAM: the balanced split's unit walk
+// and partial tiles (a separate instance, so the other schedules keep their
+// registers).
 __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 1)
     igemm_kernel(const __grid_constant__ Args p, const __grid_constant__ CUtensorMap tm_hi,
                  const __grid_constant__ CUtensorMap tm_lo, const __grid_constant__ CUtensorMap tm_a) {
@@ -456,8 +465,12 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
     // tile t -> (z, n_tile, m_tile), m fastest
     // unit t -> (K slice, z, n tile, m tile), m fastest; kb0 / kcnt = the
     // slice's first K block and block count
+    // this CTA's units: [u_first, u_end), stepping by u_next
+    constexpr bool stream = STREAM;
+    const int u_first = stream ? static_cast<int>(blockIdx.x) * p.sk_span : static_cast<int>(blockIdx.x);
+    const int u_end = stream ? min(u_first + p.sk_span, p.sk_total) : num_tiles;
     auto decode = [&](int t, int& z, int& m0, int& n0) {
-        const int u = t % (tiles_per_z * p.zcount);
+        const int u = stream ? t / nkb : t % (tiles_per_z * p.zcount);
         z = u / tiles_per_z;
         const int r = u - z * tiles_per_z;
         const int nt = r / num_m;
@@ -465,8 +478,16 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         n0 = nt * BN;
     };
     auto kslice = [&](int t, int& kb0, int& kcnt) {
+        if (stream) {
+            kb0 = t % nkb;
+            kcnt = min(nkb - kb0, u_end - t);
+            return;
+        }
         kb0 = (t / (tiles_per_z * p.zcount)) * p.kper;
         kcnt = min(nkb - kb0, p.kper);
+    };
+    auto u_next = [&](int t) -> int {
+        return stream ? min((t / nkb + 1) * nkb, u_end) : t + static_cast<int>(gridDim.x);
     };
 
     if (warp >= C::kEpiWarps && warp < C::kEpiWarps + C::kProdWarps) {
@@ -483,7 +504,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             // waits on its phases in order.
             static_assert(S % 2 == 0, "converter groups need an even ring depth");
             uint32_t items = 0;
-            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            for (int t = u_first; t < u_end; t = u_next(t)) {
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
                 items += static_cast<uint32_t>(kcnt);
@@ -529,7 +550,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         // The (tile, K block) items of this CTA form one stream: the gather
         // cursor runs two items ahead of the stores, across tile boundaries,
         // so short-K layers also keep loads in flight.
-        int ct = blockIdx.x; // cursor unit
+        int ct = u_first; // cursor unit
         int ckb = 0;         // cursor K block
         int ckb_end = 0;     // end of the cursor unit's K slice
         RowState rs;
@@ -569,17 +590,17 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 rs.base = az + (rs.ok ? rs.m : 0);
             }
         };
-        if (ct < num_tiles) {
+        if (ct < u_end) {
             start_tile(ct);
         }
         auto next = [&](float (&buf)[16]) -> bool {
-            if (ct >= num_tiles) {
+            if (ct >= u_end) {
                 return false;
             }
             gather16<MODE>(p, rs, ckb, half, ktab, buf);
             if (++ckb == ckb_end) {
-                ct += gridDim.x;
-                if (ct < num_tiles) {
+                ct = u_next(ct);
+                if (ct < u_end) {
                     start_tile(ct);
                 }
             }
@@ -631,7 +652,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
         auto tiles = [&](auto act_tag) {
             constexpr int ACT = decltype(act_tag)::value;
             int i = 0;
-            for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+            for (int t = u_first; t < u_end; t = u_next(t), ++i) {
                 int z, m0, n0;
                 decode(t, z, m0, n0);
                 const int b = i % nbuf;
@@ -666,7 +687,36 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
                 const bool two = !alt && kcnt > 1; // odd-block accumulator in use
-                if (p.ksplit > 1) {
+                const bool piece = stream && !(kb0 == 0 && kcnt == nkb);
+                if (piece) {
+                    // balanced split, part of a tile: raw partials into this
+                    // CTA's slot (0: its span's first unit, 1: its last), a
+                    // 128 x BN tile, all rows
+                    const int slot = t == u_first ? 0 : 1;
+                    float* prow = p.part + (((int64_t)blockIdx.x * 2 + slot) * 128 + quarter * 32 + lane) * BN;
+#pragma unroll 1
+                    for (int cc = col_lo; cc < col_lo + kCols; cc += 16) {
+                        float v[16], v1[16];
+                        tmem_ld16(acc0 + cc, v);
+                        if (two) {
+                            tmem_ld16(acc0 + BN + cc, v1);
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                v[j] += v1[j];
+                            }
+                        }
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            *reinterpret_cast<float4*>(prow + cc + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&acc_empty[b]);
+                    }
+                    continue;
+                } else if (p.ksplit > 1) {
                     // raw partial sums of this K slice, row-major [M][N]
                     float* prow = p.part + ((int64_t)(kb0 / p.kper) * p.zcount + z) * p.M * p.N + (int64_t)row * p.N;
 #pragma unroll 1
@@ -851,7 +901,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             prefetch_tmap(map);
             uint32_t g = 0;
             bool alive = true;
-            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x) {
+            for (int t = u_first; t < u_end && alive; t = u_next(t)) {
                 int z, m0, n0;
                 decode(t, z, m0, n0);
                 const int row = n0 + z * p.b_zrows;
@@ -909,7 +959,7 @@ __global__ void __launch_bounds__(Cfg<BN, THREE, tma_a_mode<MODE>()>::kThreads, 
             uint32_t g = 0;
             int i = 0;
             bool alive = true;
-            for (int t = blockIdx.x; t < num_tiles && alive; t += gridDim.x, ++i) {
+            for (int t = u_first; t < u_end && alive; t = u_next(t), ++i) {
                 int kb0, kcnt;
                 kslice(t, kb0, kcnt);
                 if (alt && (i & 1) != par) {
@@ -1087,6 +1137,62 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ Args p) {
     }
 }
 
+// Balanced split: each tile whose K blocks crossed a CTA span boundary sums
+// its pieces in CTA order (deterministic) and applies the epilogue. Blocks
+// (tile, y): a thread takes four consecutive columns of one row, loads the
+// pieces' 16-byte vectors, then writes the four outputs; tiles done whole by
+// one CTA return at once.
+template <int BN>
+__global__ void __launch_bounds__(256) streamk_reduce_kernel(const __grid_constant__ Args p) {
+    const int tile = blockIdx.x;
+    const int nkb = p.nkb, span = p.sk_span;
+    const int g0 = tile * nkb, g1 = g0 + nkb;
+    const int c_first = g0 / span, c_last = (g1 - 1) / span;
+    if (c_first == c_last) {
+        return;
+    }
+    const int num_m = (p.M + 127) / 128;
+    const int num_n = (p.N + BN - 1) / BN;
+    const int tiles_per_z = num_m * num_n;
+    const int z = tile / tiles_per_z;
+    const int r = tile - z * tiles_per_z;
+    const int nt = r / num_m;
+    const int m0 = (r - nt * num_m) * 128, n0 = nt * BN;
+    for (int q = blockIdx.y * blockDim.x + threadIdx.x; q < 128 * BN / 4; q += gridDim.y * blockDim.x) {
+        const int e = q * 4;
+        const int lr = e / BN, lc = e - lr * BN;
+        const int row = m0 + lr;
+        if (row >= p.M || n0 + lc >= p.N) {
+            continue;
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = c_first; c <= c_last; ++c) {
+            const int slot = (c * span >= g0) ? 0 : 1;
+            const float4 v = __ldg(reinterpret_cast<const float4*>(p.part + ((int64_t)c * 2 + slot) * 128 * BN + e));
+            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        }
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int col = n0 + lc + j;
+            if (col >= p.N) {
+                break;
+            }
+            int64_t off;
+            if (p.conv_out) {
+                const int n_img = row / (int)p.OHW;
+                const int pix = row - n_img * (int)p.OHW;
+                off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix + (int64_t)col * p.OHW;
+            } else {
+                off = (int64_t)z * p.out_zstride + (int64_t)row * p.ldc + col;
+            }
+            const float bb = p.bias ? p.bias[(int64_t)z * p.bias_zstride + col] : 0.0f;
+            const float rv = p.res ? p.res[off] : 0.0f;
+            p.out[off] = act_rt(fmaf(p.res_scale, rv, fmaf(p.alpha, a4[j], p.bias_scale * bb)), p);
+        }
+    }
+}
+
 // 2-D fp32 map over [rows][inner] (row stride `ld` elements) with 32 x
 // box_rows boxes in the 128-byte swizzle; out-of-range boxes read zeros.
 void make_tmap(CUtensorMap* map, const float* base, int64_t inner, int64_t rows, int box_rows, int64_t ld = -1) {
@@ -1105,20 +1211,32 @@ void make_tmap(CUtensorMap* map, const float* base, int64_t inner, int64_t rows,
     }
 }
 
-template <int BN, bool THREE, int MODE>
-void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo,
-                 const CUtensorMap& am) {
+template <int BN, bool THREE, int MODE, bool STREAM>
+void launch_variant(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo,
+                    const CUtensorMap& am) {
     using C = Cfg<BN, THREE, tma_a_mode<MODE>()>;
     const int smem = C::kSmemBytes + (a.ktab_smem ? a.nkb * 32 * 8 : 0);
     static int attr_bytes[64] = {};
     if (attr_bytes[dev->ordinal] < smem) {
-        check_cuda(cudaFuncSetAttribute(igemm_kernel<BN, THREE, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        smem),
+        check_cuda(cudaFuncSetAttribute(igemm_kernel<BN, THREE, MODE, STREAM>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                    "cudaFuncSetAttribute(igemm)");
         attr_bytes[dev->ordinal] = smem;
     }
-    igemm_kernel<BN, THREE, MODE><<<grid, C::kThreads, smem, dev->stream>>>(a, hi, lo, am);
+    igemm_kernel<BN, THREE, MODE, STREAM><<<grid, C::kThreads, smem, dev->stream>>>(a, hi, lo, am);
     check_cuda(cudaGetLastError(), "igemm launch");
+}
+
+template <int BN, bool THREE, int MODE>
+void launch_mode(nb2_device* dev, const Args& a, dim3 grid, const CUtensorMap& hi, const CUtensorMap& lo,
+                 const CUtensorMap& am) {
+    if constexpr (BN == 128) {
+        if (a.stream) {
+            launch_variant<BN, THREE, MODE, true>(dev, a, grid, hi, lo, am);
+            return;
+        }
+    }
+    launch_variant<BN, THREE, MODE, false>(dev, a, grid, hi, lo, am);
 }
 
 template <int BN, bool THREE>
@@ -1177,12 +1295,36 @@ int tile_width(const nb2_device* dev, int64_t M, int64_t n_per_z, int nkb, int64
     return t128 >= 4 * static_cast<int64_t>(dev->num_sms) ? 128 : 64;
 }
 
+// Balanced split for 128-wide tiles whose count leaves the last wave short
+// (e.g. 52, 100 or 196 tiles on 148 SMs): every CTA takes an equal span of
+// the (tile, K block) pairs. Cost model in K-block times: a unit costs its K
+// blocks plus ~9 for the single-buffered accumulator's drain, a reduce ~11;
+// compared with the unsplit tiles or, where those apply, equal K slices.
+// Taken when it saves at least 10%; returns the span (0: not taken).
+// Measured on ResNet-18 bs64 layers 3 and 4 (196 and 100 tiles): 103 -> 78
+// µs per contraction kernel plus 6-15 µs of reduce.
+int64_t balanced_span(const nb2_device* dev, int64_t tiles, int nkb, int bn) {
+    if (bn != 128 || nkb < 8 || dev->no_grow || tiles * nkb >= (1LL << 30)) {
+        return 0;
+    }
+    const int64_t G = dev->num_sms, E = 9, R = 11;
+    int64_t other = (tiles + G - 1) / G * (nkb + E); // unsplit
+    int kper = nkb;
+    const int ks = split_k_slices(dev, tiles, nkb, &kper);
+    if (ks > 1) { // equal K slices
+        other = (tiles * ks + G - 1) / G * (kper + E) + R;
+    }
+    const int64_t span = (tiles * nkb + G - 1) / G;
+    const int64_t balanced = span + ((span + nkb - 1) / nkb + 1) * E + R;
+    return balanced * 10 < other * 9 ? span : 0;
+}
+
 int contraction_launches(const nb2_device* dev, int64_t M, int64_t n_per_z, int64_t K, int64_t z) {
     const int nkb = static_cast<int>((K + 31) / 32);
     const int bn = tile_width(dev, M, n_per_z, nkb, z);
     const int64_t tiles = ((M + 127) / 128) * ((n_per_z + bn - 1) / bn) * z;
     int kper = 0;
-    return split_k_slices(dev, tiles, nkb, &kper) > 1 ? 2 : 1;
+    return (balanced_span(dev, tiles, nkb, bn) > 0 || split_k_slices(dev, tiles, nkb, &kper) > 1) ? 2 : 1;
 }
 
 namespace {
@@ -1233,7 +1375,9 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     a.kper = a.nkb;
     a.part = nullptr;
     int kper = a.nkb;
-    const int ks = a.omap ? 1 : split_k_slices(dev, tiles, a.nkb, &kper); // the reduce writes row-major
+    // the reduce kernels write row-major or NCHW, not through an output map
+    const int64_t bspan = a.omap ? 0 : balanced_span(dev, tiles, a.nkb, bn);
+    const int ks = (a.omap || bspan > 0) ? 1 : split_k_slices(dev, tiles, a.nkb, &kper);
     if (ks > 1) {
         const size_t bytes = static_cast<size_t>(ks) * static_cast<size_t>(z) * a.M * n_per_z * sizeof(float);
         float* part = static_cast<float*>(dev->split_scratch(bytes));
@@ -1243,16 +1387,32 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
             a.part = part;
         }
     }
+    a.stream = 0;
+    if (bspan > 0) {
+        const size_t bytes = static_cast<size_t>(dev->num_sms) * 2 * 128 * bn * sizeof(float);
+        float* part = static_cast<float*>(dev->split_scratch(bytes));
+        if (part != nullptr) {
+            a.stream = 1;
+            a.sk_span = static_cast<int>(bspan);
+            a.sk_total = static_cast<int>(tiles * a.nkb);
+            a.part = part;
+        }
+    }
     // persistent: one CTA per SM (shared memory admits exactly one)
-    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(tiles * a.ksplit, dev->num_sms)), 1, 1);
+    const dim3 grid(static_cast<unsigned>(a.stream ? std::min<int64_t>((a.sk_total + a.sk_span - 1) / a.sk_span,
+                                                                          dev->num_sms)
+                                                   : std::min<int64_t>(tiles * a.ksplit, dev->num_sms)),
+                    1, 1);
     // two 128-wide tiles in flight once every CTA has several short-K
     // tiles (with one or two tiles per CTA, or long K, the single issuer's
     // gaps between K blocks cost more than the epilogue overlap saves:
     // measured 10-15% slower on 4096^3)
-    a.alt = (bn == 128 && a.ksplit == 1 && a.nkb <= 32 && tiles >= 4 * static_cast<int64_t>(grid.x)) ? 1 : 0;
+    a.alt = (bn == 128 && a.ksplit == 1 && !a.stream && a.nkb <= 32 && tiles >= 4 * static_cast<int64_t>(grid.x))
+                ? 1
+                : 0;
     dev->last_sched.tile_n = bn;
     dev->last_sched.alt = a.alt;
-    dev->last_sched.ksplit = a.ksplit;
+    dev->last_sched.ksplit = a.stream ? 0 : a.ksplit;
     dev->last_sched.a_mode = a.mode;
     dev->last_sched.grid = static_cast<int>(grid.x);
     dev->last_sched.tiles = tiles;
@@ -1261,6 +1421,10 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
         three ? launch_bn<64, true>(dev, a, grid, hi, lo, am) : launch_bn<64, false>(dev, a, grid, hi, lo, am);
     } else {
         three ? launch_bn<128, true>(dev, a, grid, hi, lo, am) : launch_bn<128, false>(dev, a, grid, hi, lo, am);
+    }
+    if (a.stream) {
+        streamk_reduce_kernel<128><<<dim3(static_cast<unsigned>(tiles), 16), 256, 0, dev->stream>>>(a);
+        check_cuda(cudaGetLastError(), "balanced-split reduce launch");
     }
     if (a.ksplit > 1) {
         const int64_t total = z * a.M * static_cast<int64_t>(n_per_z);

@@ -2,8 +2,11 @@
 
 The host picks, per launch, the output tile width (64 or 128 columns), whether
 two 128-wide tiles are kept in flight (the two MMA issuers take alternate
-tiles and hand off through a barrier), and whether K is split into slices
-reduced by a second kernel. Each case below is sized so that one schedule is
+tiles and hand off through a barrier), whether K is split into slices
+reduced by a second kernel, and whether the (tile, K block) pairs are cut
+into one equal span per CTA (the balanced split, k_slices == 0, for tile
+counts that leave the last wave short; the tiles cut at a span boundary are
+finished by a second kernel). Each case below is sized so that one schedule is
 taken, asserts through nb2_device_last_contraction that it was, and compares
 the result with the numpy restatement of the reference rows
 (src/kernels/gemm.cpp:122-136, conv.cpp:263-289: float64 accumulation, one
@@ -66,6 +69,9 @@ GEMMS = [
     ("split_k_sweep_64x1000x512", 64, 1000, 512, dict(tile_n=128, two_in_flight=0, k_slices=4)),
     ("narrow_64_many_tiles", 30000, 64, 576, dict(tile_n=64, two_in_flight=0, k_slices=1)),
     ("short_k_64_wide", 2000, 256, 128, dict(tile_n=64, two_in_flight=0, k_slices=1)),
+    # 100 and 196 tiles on 148 SMs: the balanced split
+    ("balanced_100_tiles_2560x640x4096", 2560, 640, 4096, dict(tile_n=128, two_in_flight=0, k_slices=0)),
+    ("balanced_196_tiles_1792x1792x2304", 1792, 1792, 2304, dict(tile_n=128, two_in_flight=0, k_slices=0)),
 ]
 
 
@@ -125,6 +131,9 @@ CONVS = [
     ("resnet50_b32_1x1_expand", 32, 64, 56, 56, 256, 1, 1, 0, dict(tile_n=128, two_in_flight=1, k_slices=1)),
     # ResNet-18 bs64 layer 1: 64 channels, double-buffered 64-wide tiles
     ("resnet18_b64_layer1", 64, 64, 56, 56, 64, 3, 1, 1, dict(tile_n=64, two_in_flight=0, k_slices=1)),
+    # ResNet-18 bs64 layers 3 and 4: 196 and 100 tiles, 72 and 144 K blocks
+    ("resnet18_b64_layer3", 64, 256, 14, 14, 256, 3, 1, 1, dict(tile_n=128, two_in_flight=0, k_slices=0)),
+    ("resnet18_b64_layer4", 64, 512, 7, 7, 512, 3, 1, 1, dict(tile_n=128, two_in_flight=0, k_slices=0)),
 ]
 
 
