@@ -344,8 +344,19 @@ int nb2_conv2d_run_packed(nb2_device* dev, const nb2_conv_geom* g, const float* 
 int nb2_conv2d(nb2_device* dev, const nb2_conv_geom* g, const float* x, const float* w, const float* bias,
                const float* residual, int act, float* y) {
     return guard([&] {
-        const ConvGeom geom = nchw_input_layout(to_geom(g));
+        const ConvGeom plain = to_geom(g);
         need(x != nullptr && w != nullptr && y != nullptr, "Conv: null buffer");
+        if (direct_conv_ok(plain)) {
+            // narrow output (<= 32 channels): the CUDA-core direct kernel
+            bind(dev);
+            Epilogue ep;
+            ep.bias = bias;
+            ep.res = residual;
+            ep.act = act;
+            conv_direct(dev, plain, x, w, y, ep);
+            return;
+        }
+        const ConvGeom geom = nchw_input_layout(plain);
         bind(dev);
         const size_t pbytes = (conv_packed_bytes(geom) + 255) & ~size_t(255);
         uint8_t* ws = static_cast<uint8_t*>(dev->scratch(pbytes + nhwc_copy_bytes(geom)));

@@ -848,6 +848,10 @@ std::set<std::string> assign_nhwc(const Graph& g, const std::map<std::string, Te
                 if (!cg.nhwc_input_ok()) {
                     bad.insert(n.inputs[0]);
                 }
+                if (direct_conv_ok(cg)) { // the CUDA-core path reads and writes NCHW
+                    bad.insert(n.inputs[0]);
+                    bad.insert(e.out);
+                }
             } else {
                 bad.insert(n.inputs[0]);
             }
@@ -1042,8 +1046,9 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             // channels padded to 4, 8 or 16 (each tap one to four 16-byte
             // loads); a spatial filter over more channels padded to a multiple
             // of 32 and read through TMA im2col.
+            const bool direct = direct_conv_ok(geom);
             const bool convertible = (flags & kNchwOnly) == 0 && !geom.in_nhwc &&
-                                     packed_conv.count(n.inputs[1]) > 0 && geom.group == 1;
+                                     packed_conv.count(n.inputs[1]) > 0 && geom.group == 1 && !direct;
             if (convertible) {
                 geom = nchw_input_layout(geom);
             }
@@ -1056,6 +1061,29 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             ep.act_c = e.act_c;
             const float* x = F(n.inputs[0]);
             float* y = F(e.out);
+            if (direct) {
+                // narrow output: the CUDA-core direct kernel on the raw weights
+                const float* w = nullptr;
+                if (packed_conv.count(n.inputs[1])) {
+                    const Constant& wc = g_.constants.at(n.inputs[1]);
+                    uint8_t* wd = dmalloc(align_up(static_cast<int64_t>(wc.bytes.size())));
+                    check_cuda(cudaMemcpyAsync(wd, wc.bytes.data(), wc.bytes.size(), cudaMemcpyHostToDevice,
+                                               dev_->stream),
+                               "cudaMemcpyAsync(weight)");
+                    check_cuda(cudaStreamSynchronize(dev_->stream), "weight upload sync");
+                    weight_bytes_ += static_cast<int64_t>(wc.bytes.size());
+                    w = reinterpret_cast<const float*>(wd);
+                } else {
+                    w = F(n.inputs[1]);
+                }
+                nb2_device* dev = dev_;
+                st.label += "[direct]";
+                st.launches = 1;
+                st.run = [=] { conv_direct(dev, geom, x, w, y, ep); };
+                launches_ += st.launches;
+                steps_.push_back(std::move(st));
+                continue;
+            }
             const int64_t pbytes = static_cast<int64_t>(conv_packed_bytes(geom));
             // the contraction kernel, plus a reduce launch when it splits K
             const int conv_k = contraction_launches(dev_, geom.N * geom.OH * geom.OW, geom.Mg(), geom.K(), geom.group);

@@ -99,6 +99,11 @@ int contraction_launches(const nb2_device* dev, int64_t M, int64_t n_per_z, int6
 
 // Bytes of the packed weight buffer of a Conv: hi and lo planes of
 // [M][Kpad] fp32, then (generic layout only) a Kpad-entry int2 tap table.
+// Direct convolution on the CUDA cores (conv_direct.cu) for narrow outputs:
+// group 1, M <= 32, NCHW in and out, the shared weight tile within 48 KB;
+// raw fp32 weights [M][C][KH][KW], fp32 FMAs, the same epilogue.
+bool direct_conv_ok(const ConvGeom& g);
+void conv_direct(nb2_device* dev, const ConvGeom& g, const float* x, const float* w, float* y, const Epilogue& ep);
 size_t conv_packed_bytes(const ConvGeom& g);
 void conv_pack(nb2_device* dev, const ConvGeom& g, const float* w, void* packed);
 void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* packed, float* y, const Epilogue& ep);

@@ -164,13 +164,14 @@ def test_captured_graph_survives_split_k_workspace_growth(cuda):
     m = Model(g, {"input": [1, 3, 224, 224]})
     try:
         first = m.run({"input": x})["fc_out"]
-        # 72 output tiles, 128 K blocks: three K slices of 1152 x 1024 sums
+        # 72 output tiles, 128 K blocks: split into equal K spans per CTA,
+        # whose partial tiles (148 x 2 x 64 KB) outgrow the model's buffer
         a = torch.randn(1152, 4096, device="cuda")
         b = torch.randn(4096, 1024, device="cuda") / 64
         y = ops.gemm(a, b)
         from nert_b200 import _lib
 
-        assert _lib.last_contraction(0)["k_slices"] == 3
+        assert _lib.last_contraction(0)["k_slices"] == 0
         want = (a.double() @ b.double()).float()
         assert rel_err(y.cpu().numpy(), want.cpu().numpy()) <= TOL
         again = m.run({"input": x})["fc_out"]

@@ -15,14 +15,16 @@ from nert_b200 import configs, model
 from oracle import np_ref
 
 # (id, batch, cin, h, w, c, m, kernel, strides, pads, dilations, residual, pool, gap)
+# (c >= 64: a Conv with at most 32 output channels runs the direct CUDA-core
+# kernel, which reads and writes NCHW)
 CHAINS = [
-    ("3x3s1_res", 2, 3, 20, 20, 32, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
+    ("3x3s1_res", 2, 3, 20, 20, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
     ("3x3s2_m40", 2, 8, 16, 15, 64, 40, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1), False, False, False),
     ("1x1s2_res", 2, 16, 14, 14, 64, 128, (1, 1), (2, 2), (0, 0, 0, 0), (1, 1), True, False, False),
-    ("7x7s2p3", 1, 3, 23, 29, 32, 32, (7, 7), (2, 2), (3, 3, 3, 3), (1, 1), False, False, False),
-    ("asym_pads", 2, 4, 17, 13, 32, 48, (3, 3), (2, 2), (0, 0, 1, 1), (1, 1), False, False, False),
+    ("7x7s2p3", 1, 3, 23, 29, 64, 64, (7, 7), (2, 2), (3, 3, 3, 3), (1, 1), False, False, False),
+    ("asym_pads", 2, 4, 17, 13, 64, 48, (3, 3), (2, 2), (0, 0, 1, 1), (1, 1), False, False, False),
     ("dil2", 1, 5, 19, 21, 96, 64, (3, 3), (1, 1), (2, 2, 2, 2), (2, 2), False, False, False),
-    ("5x3_s3x1_m42", 2, 3, 25, 11, 32, 42, (5, 3), (3, 1), (2, 1, 2, 1), (1, 1), False, False, False),
+    ("5x3_s3x1_m42", 2, 3, 25, 11, 64, 42, (5, 3), (3, 1), (2, 1, 2, 1), (1, 1), False, False, False),
     ("pool_gap", 2, 3, 33, 31, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, True, True),
     ("b4_56x56", 4, 16, 56, 56, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
 ]
@@ -64,8 +66,8 @@ def test_grouped_and_narrow_convs_keep_their_input_nchw():
     x = g.add_input("x", [1, 8, 10, 10])
     w0 = np.ones((32, 8, 1, 1), np.float32)
     w1 = np.ones((32, 8, 3, 3), np.float32)
-    w2 = np.ones((24, 32, 1, 1), np.float32)
-    w3 = np.ones((8, 24, 1, 1), np.float32)
+    w2 = np.ones((48, 32, 1, 1), np.float32)  # more than 32 outputs: a tensor-core Conv
+    w3 = np.ones((8, 48, 1, 1), np.float32)
     t0 = g.op("Conv", [x, g.const("w0", w0)], name="c0", kernel_shape=[1, 1])
     t1 = g.op("Conv", [t0, g.const("w1", w1)], name="grouped", kernel_shape=[3, 3], pads=[1] * 4, group=4)
     t2 = g.op("Conv", [t1, g.const("w2", w2)], name="c2", kernel_shape=[1, 1])
@@ -75,7 +77,7 @@ def test_grouped_and_narrow_convs_keep_their_input_nchw():
     lay = _layout(g)
     assert not lay[t0]   # read by a grouped Conv
     assert lay[t1]       # produced by a Conv, read by a C % 32 == 0 Conv
-    assert not lay[t2]   # 24 channels: TMA im2col needs C % 32 == 0
+    assert not lay[t2]   # 48 channels: TMA im2col needs C % 32 == 0
     assert not lay[t3]
 
 
@@ -155,9 +157,12 @@ def _c4_graph(case):
 def test_narrow_channel_conv_c4_path(cuda, case):
     """NCHW inputs with up to 16 channels run on an NHWC copy padded to 4, 8
     or 16 channels (one to four 16-byte loads per tap); off with
-    channels_last=False."""
+    channels_last=False. Layers with at most 32 outputs and few
+    multiply-adds per pixel take the direct CUDA-core kernel instead."""
     g, feed = _c4_graph(case)
-    tag = _cvec_label(case[2])
+    _, _, c, _, _, m_out, k = case[:7]
+    direct = m_out <= 32 and c * k[0] * k[1] * m_out <= 2560
+    tag = "[direct]" if direct else _cvec_label(case[2])
     ref = np_ref.run(g, feed)
     out_name = g.outputs[0][0]
     for cl in (True, False):
@@ -167,7 +172,7 @@ def test_narrow_channel_conv_c4_path(cuda, case):
             labels = [lab for lab, _ in m.profile()]
         finally:
             m.close()
-        assert any(tag in lab for lab in labels) == cl, labels
+        assert any(tag in lab for lab in labels) == (cl or direct), labels
         assert rel_err(out, ref[out_name]) <= TOL, cl
 
 
