@@ -49,7 +49,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-18 fp32 images/s bs64 at 1/2/4/8 B200; Conv/GEMM % of TF32 tensor peak"
 UNIT = "images/s"
-DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32, "conv": 64, "rows": 0}
+DEFAULT_BATCH = {"resnet18": 64, "resnet50": 32, "vit_b16": 32, "yolov8n": 16, "sweep": 32, "conv": 64, "rows": 0,
+                 "attention": 32}
 
 
 def parse():
@@ -243,7 +244,7 @@ def run_reference(args):
     if not ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libnert_ref.so was not built"}))
         return 0
-    if args.workload in ("sweep", "conv", "rows"):
+    if args.workload in ("sweep", "conv", "rows", "attention"):
         print(json.dumps({"impl": "reference", "unavailable": "the single-op workloads have no reference CPU arm"}))
         return 0
     cores = ref_cores()
@@ -638,6 +639,65 @@ def run_conv(args, local):
     return 0
 
 
+def run_attention(args, local):
+    """The ViT-B/16 attention chain (QK^T, / 8, Softmax, AV, head merge) of
+    `--batch` images x 12 heads x 197 tokens as an engine graph, which the
+    engine fuses into one attention step; timed like the conv workload (also
+    the target of the committed ncu capture of that kernel)."""
+    import numpy as np
+    import torch
+
+    from nert_b200 import model as nbm
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    B, H, T, D = args.batch, 12, 197, 64
+    g = Graph(opset=13)
+    q = g.add_input("q", [B, H, T, D])
+    k = g.add_input("k", [B, H, D, T])
+    v = g.add_input("v", [B, H, T, D])
+    sc = g.op("Div", [g.op("MatMul", [q, k], name="qk"), g.const("c", np.array(8.0, np.float32))], name="sc")
+    o = g.op("MatMul", [g.op("Softmax", [sc], name="sm", axis=-1), v], name="av")
+    o = g.op("Reshape", [g.op("Transpose", [o], name="t", perm=[0, 2, 1, 3]),
+                         g.const("m", np.array([B, T, H * D], np.int64))], name="merge")
+    g.add_output(o, None, FLOAT)
+    feed = {"q": synth.normal((B, H, T, D), 1.0, synth.seed_of("bench_attn", "q")),
+            "k": synth.normal((B, H, D, T), 1.0, synth.seed_of("bench_attn", "k")),
+            "v": synth.normal((B, H, T, D), 1.0, synth.seed_of("bench_attn", "v"))}
+    mdl = nbm.Model(g, {n: list(a.shape) for n, a in feed.items()}, device=local)
+    mdl.run(feed)
+    stream = torch.cuda.ExternalStream(mdl.stream(), device=torch.device("cuda", local))
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    evs = []
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            mdl.launch()
+        for _ in range(args.steps):
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            mdl.launch()
+            e0.record(stream)
+            evs.append((s0, e0))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    rows = {lab: t for lab, t in mdl.profile()}
+    kpr = mdl.stats()["kernels_per_run"]
+    mdl.close()
+    flops = 4.0 * B * H * T * T * D
+    peak, note = tensor_peak(args.precision)
+    print(json.dumps({"metric": "fused attention TFLOP/s (ViT-B/16 heads, T=197, d=64)",
+                      "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32 (3xTF32)", "data": "synthetic",
+                      "config": {"workload": "attention", "batch": B, "heads": H, "tokens": T, "head_dim": D,
+                                 "l2": "flushed between timed steps"},
+                      "rows_ms": rows, "roofline": {"bound": "tensor", "peak": peak, "peak_note": note,
+                                                    "frac": flops / (ms * 1e-3) / 1e12 / peak},
+                      "gpu_launches": kpr * args.steps}), flush=True)
+    return 0
+
+
 def run_seam(args, local):
     """The workload through the drop-in boundary: the reference's unmodified
     LoadGraphFromFile -> nert::Model -> Run (compiled from its sources into
@@ -769,7 +829,8 @@ def main():
     rank, world, local = dist_env()
 
     cpu = None
-    if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload not in ("sweep", "conv", "rows")
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline
+            and args.workload not in ("sweep", "conv", "rows", "attention")
             and args.api == "engine"):
         from oracle import ref
 
@@ -794,6 +855,8 @@ def main():
         return run_sweep(args, local)
     if args.workload == "conv":
         return run_conv(args, local)
+    if args.workload == "attention":
+        return run_attention(args, local)
     if args.workload == "rows":
         # the HBM-bound rows alone (also the target of their committed ncu
         # captures): --steps timed launches per row after --warmup untimed

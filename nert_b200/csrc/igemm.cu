@@ -1165,11 +1165,27 @@ __global__ void __launch_bounds__(256) streamk_reduce_kernel(const __grid_consta
         if (row >= p.M || n0 + lc >= p.N) {
             continue;
         }
+        // up to four pieces loaded before the sum (a tile spans at most
+        // ceil(nkb / span) + 1 CTAs), then any further ones; CTA order kept
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = c_first; c <= c_last; ++c) {
-            const int slot = (c * span >= g0) ? 0 : 1;
-            const float4 v = __ldg(reinterpret_cast<const float4*>(p.part + ((int64_t)c * 2 + slot) * 128 * BN + e));
-            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        float4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = c_first + j;
+            if (c <= c_last) {
+                const int slot = (c * span >= g0) ? 0 : 1;
+                v[j] = __ldg(reinterpret_cast<const float4*>(p.part + ((int64_t)c * 2 + slot) * 128 * BN + e));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (c_first + j <= c_last) {
+                acc.x += v[j].x, acc.y += v[j].y, acc.z += v[j].z, acc.w += v[j].w;
+            }
+        }
+        for (int c = c_first + 4; c <= c_last; ++c) {
+            const float4 w = __ldg(reinterpret_cast<const float4*>(p.part + ((int64_t)c * 2) * 128 * BN + e));
+            acc.x += w.x, acc.y += w.y, acc.z += w.z, acc.w += w.w;
         }
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
