@@ -1032,7 +1032,7 @@ MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::stri
         int64_t* ip = static_cast<int64_t*>(ptr(n.outputs[1]));
         const size_t sb = topk_scratch_bytes(rows, L, k);
         uint8_t* scratch = sb ? dmalloc(static_cast<int64_t>(sb)) : nullptr;
-        st.launches = sb ? 7 : 1; // clear + 3 digit passes + count + collect + sort
+        st.launches = topk_launches(rows, L, k);
         st.run = [=](nb2_device* dev) { topk(dev, xp, vp, ip, rows, L, k, scratch); };
     } else if (n.op == "Resize") {
         const TensorInfo& x = sh(n.inputs[0]);

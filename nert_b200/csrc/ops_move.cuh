@@ -64,6 +64,8 @@ void cast(nb2_device* dev, const void* x, int from, void* y, int to, int64_t n);
 // CTAs and need `scratch` of topk_scratch_bytes(rows, L, k) bytes (0 for
 // short rows).
 size_t topk_scratch_bytes(int64_t rows, int64_t L, int64_t k);
+// kernels one topk() call launches
+int topk_launches(int64_t rows, int64_t L, int64_t k);
 void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t L, int64_t k,
           void* scratch);
 

@@ -806,6 +806,14 @@ size_t topk_scratch_bytes(int64_t rows, int64_t L, int64_t k) {
     return topk_layout(nullptr, rows, L, k).total;
 }
 
+int topk_launches(int64_t rows, int64_t L, int64_t k) {
+    (void)rows;
+    if (L < kSplitMin && k <= kMaxK) {
+        return 1;
+    }
+    return (sample_rank(L, k) > 0 ? 3 : 0) + 6;
+}
+
 void topk(nb2_device* dev, const float* x, float* values, int64_t* indices, int64_t rows, int64_t L, int64_t k,
           void* scratch) {
     if (rows == 0 || k == 0) {

@@ -327,3 +327,28 @@ def test_sppf_c_abi_matches_rows(cuda):
     assert torch.equal(y, torch.cat(want, 1))
     # invalid arguments are refused before any launch
     assert L.nb2_sppf(dev, x.data_ptr(), i64s(x.shape), y.data_ptr(), 4, 3) != 0
+
+
+@pytest.mark.parametrize("fill", ["flood_of_ties", "best_at_row_end", "duplicates", "mostly_neg_inf"])
+def test_topk_long_rows_exact(cuda, fill):
+    """Long rows (the sampled-threshold path, with the radix passes for rows
+    it cannot make exact): exact values and indices in (value desc, index
+    asc) order on inputs that stress it, against the oracle."""
+    L, rows, k = 2 * 32768 + 100, 3, 300
+    rng = np.random.default_rng(synth.seed_of("topk_long", fill))
+    if fill == "flood_of_ties":
+        x = np.zeros((rows, L), np.float32)
+        x[:, ::997] = 1.0  # fewer ones than k: the rest are the smallest-index zeros
+    elif fill == "best_at_row_end":
+        x = rng.standard_normal((rows, L)).astype(np.float32)
+        x[:, -100:] += 10.0  # the best values all in the row's last 100
+    elif fill == "duplicates":
+        x = rng.integers(0, 50, (rows, L)).astype(np.float32)
+    else:
+        x = np.full((rows, L), -np.inf, np.float32)
+        x[:, rng.integers(0, L, 200)] = rng.standard_normal(200).astype(np.float32)
+    g, _ = one("TopK", [(rows, L), (1,)], {"axis": -1}, {1: np.array([k], np.int64)}, n_out=2)
+    ref = np_ref.run(g, {"in0": x})
+    got = run_engine(g, {"in0": x})
+    for name in ref:
+        np.testing.assert_array_equal(got[name], ref[name])
