@@ -34,7 +34,11 @@ def build(quiet: bool = True) -> bool:
     (the CPU library, and the CUDA-device library where nvcc and cuDNN are)."""
     if not os.path.isdir(os.path.join(REFERENCE_SRC, "src")):
         return os.path.exists(LIB_PATH)
-    out = subprocess.run(["make", "-C", HERE, "-j8", f"REF={REFERENCE_SRC}"], capture_output=True, text=True)
+    targets = ["all"]
+    if os.path.exists(os.path.join(HERE, "..", "nert_b200", "lib", "libnert_b200_device.so")):
+        targets.append("bench_runtime")  # the reference's runtime bench harness on the B200 handle
+    out = subprocess.run(["make", "-C", HERE, "-j8", f"REF={REFERENCE_SRC}"] + targets, capture_output=True,
+                         text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout[-2000:] + out.stderr[-2000:])
     return True

@@ -228,3 +228,21 @@ def test_reference_constant_folding_with_b200_rows(b200_device):
                 mdl.close()
     np.testing.assert_array_equal(via_cpu, want)
     assert rel_err(via_b200, want) <= TOL
+
+
+def test_reference_runtime_bench_harness_on_b200(cuda):
+    """The reference's own runtime bench harness (bench/runtime/main.cpp,
+    compiled unchanged by `make -C oracle bench_runtime`, its CUDA slot given
+    the B200 handle): every op case it runs on the device matches its
+    CpuDevice result within the harness's own tolerance, and it exits 0."""
+    import subprocess
+
+    exe = os.path.join(os.path.dirname(ref.__file__), "_ref", "nert_bench_runtime_b200")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/nert_bench_runtime_b200 was not built")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    out = r.stdout + r.stderr
+    assert r.returncode == 0, out[-3000:]
+    rows = [ln for ln in out.splitlines() if " CUDA " in ln]
+    assert rows and not any("FAIL" in ln for ln in rows), out[-3000:]
+    assert any(ln.startswith("PASSED") for ln in out.splitlines()), out[-3000:]
