@@ -1195,7 +1195,11 @@ __global__ void __launch_bounds__(256) streamk_reduce_kernel(const __grid_consta
                 break;
             }
             int64_t off;
-            if (p.conv_out) {
+            if (p.omap) { // the permuted output map of the main epilogue
+                off = (int64_t)(z / p.oz2) * p.ozs1 + (int64_t)(z % p.oz2) * p.ozs2 +
+                      (int64_t)(row / p.or2) * p.ors1 + (int64_t)(row % p.or2) * p.ors2 +
+                      (int64_t)(col / p.oc2) * p.ocs1 + (int64_t)(col % p.oc2) * p.ocs2;
+            } else if (p.conv_out) {
                 const int n_img = row / (int)p.OHW;
                 const int pix = row - n_img * (int)p.OHW;
                 off = (int64_t)z * p.out_zstride + (int64_t)n_img * p.out_img_stride + pix + (int64_t)col * p.OHW;
@@ -1332,6 +1336,9 @@ int64_t balanced_span(const nb2_device* dev, int64_t tiles, int nkb, int bn) {
     }
     const int64_t span = (tiles * nkb + G - 1) / G;
     const int64_t balanced = span + ((span + nkb - 1) / nkb + 1) * E + R;
+    // (with no margin ViT-B/16 fc1, 1200 tiles of 24 K blocks, and several
+    // ResNet-50 layers took it and lost 2-8% against two tiles in flight or
+    // the unsplit tiles: the model leaves out the epilogue overlap they have)
     return balanced * 10 < other * 9 ? span : 0;
 }
 
@@ -1391,8 +1398,8 @@ void launch(nb2_device* dev, Args& a, int64_t n_per_z, int64_t z, const float* p
     a.kper = a.nkb;
     a.part = nullptr;
     int kper = a.nkb;
-    // the reduce kernels write row-major or NCHW, not through an output map
-    const int64_t bspan = a.omap ? 0 : balanced_span(dev, tiles, a.nkb, bn);
+    // the equal-slice reduce writes row-major or NCHW, not through an output map
+    const int64_t bspan = balanced_span(dev, tiles, a.nkb, bn);
     const int ks = (a.omap || bspan > 0) ? 1 : split_k_slices(dev, tiles, a.nkb, &kper);
     if (ks > 1) {
         const size_t bytes = static_cast<size_t>(ks) * static_cast<size_t>(z) * a.M * n_per_z * sizeof(float);
