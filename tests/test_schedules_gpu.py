@@ -190,3 +190,33 @@ def test_wait_bound_expiry_reports_device_error_then_recovers(cuda):
     assert lib.nb2_device_get_wait_bound(dev) == default
     y = ops.gemm(ta, tb).cpu().numpy()
     assert rel_err(y, np_ref.run_op("Gemm", {}, [a, b])) <= TOL
+
+
+def test_balanced_split_through_output_map(cuda):
+    """A MatMul whose head-split Transpose the engine absorbs (the epilogue
+    writes through an output map) and whose 100 tiles of 144 K blocks take
+    the balanced split: the reduce writes the cut tiles through the same map.
+    Checked against the oracle's MatMul -> Reshape -> Transpose rows."""
+    from nert_b200 import _lib
+    from nert_b200 import model as nbm
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    seed = synth.seed_of("schedules", "balanced_omap")
+    g = Graph(opset=13)
+    x = g.add_input("x", [1280, 4608])
+    y = g.op("MatMul", [x, g.const("w", synth.normal((4608, 1280), 1.0 / 68, seed))], name="mm")
+    y = g.op("Reshape", [y, g.const("s", np.array([1280, 10, 128], np.int64))], name="rs")
+    y = g.op("Transpose", [y], name="tr", perm=[1, 0, 2])
+    g.add_output(y, None, FLOAT)
+    ex = nbm.analyze(g, {"x": [1280, 4608]})["exec"]
+    assert [e["op"] for e in ex] == ["MatMul"] and ex[0]["perm"] == [1, 0, 2]
+    feed = {"x": synth.normal((1280, 4608), 1.0, seed ^ 1)}
+    m = nbm.Model(g, {"x": [1280, 4608]})
+    try:
+        got = list(m.run(feed).values())[0]
+        sched = _lib.last_contraction(0)
+    finally:
+        m.close()
+    assert (sched["tile_n"], sched["k_slices"], sched["tiles"]) == (128, 0, 100), sched
+    want = list(np_ref.run(g, feed).values())[0]
+    assert rel_err(got, want) <= TOL
