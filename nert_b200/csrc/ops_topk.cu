@@ -533,31 +533,45 @@ __device__ uint32_t block_kth_key(const uint32_t* keys, int n, int j, uint32_t* 
             }
         }
         __syncthreads();
-        if (tid < 32) {
+        {
+            // Block-parallel bin search: each thread owns kBins / blockDim.x
+            // consecutive bins; a suffix sum over the threads (larger keys in
+            // higher bins) finds the one thread whose range holds the bin
+            // where the count from the top reaches `need`.
+            const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+            const int per = kBins / static_cast<int>(blockDim.x);
+            const int b0 = tid * per;
+            const uint32_t need = static_cast<uint32_t>(s_need);
             uint32_t mine = 0;
-            for (int b = 0; b < 64; ++b) {
-                mine += hist[tid * 64 + ((b + tid) & 63)]; // skewed: lanes on distinct banks
+            for (int b = 0; b < per; ++b) {
+                mine += hist[b0 + b];
             }
-            lane_tot[tid] = mine;
-            __syncwarp();
-            if (tid == 0) {
-                const int need = s_need;
-                uint32_t above = 0;
-                int sel = 0;
-                for (int l = 31; l >= 0; --l) {
-                    if (above + lane_tot[l] >= static_cast<uint32_t>(need)) {
-                        for (int b = l * 64 + 63; b >= l * 64; --b) {
-                            if (above + hist[b] >= static_cast<uint32_t>(need)) {
-                                sel = b;
-                                break;
-                            }
-                            above += hist[b];
-                        }
+            uint32_t suf = mine; // inclusive suffix within the warp
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+                suf += lane + o < 32 ? v : 0u;
+            }
+            if (lane == 0) {
+                lane_tot[warp] = suf; // the warp's total
+            }
+            __syncthreads();
+            uint32_t above_w = 0;
+            for (int w = warp + 1; w < nwarps; ++w) {
+                above_w += lane_tot[w];
+            }
+            const uint32_t incl = suf + above_w, excl = incl - mine;
+            if (excl < need && need <= incl) {
+                uint32_t above = excl;
+                int sel = b0;
+                for (int b = b0 + per - 1; b >= b0; --b) {
+                    if (above + hist[b] >= need) {
+                        sel = b;
                         break;
                     }
-                    above += lane_tot[l];
+                    above += hist[b];
                 }
-                s_need = need - static_cast<int>(above);
+                s_need = static_cast<int>(need - above);
                 s_prefix |= static_cast<uint32_t>(sel) << sh;
                 s_mask |= dm << sh;
             }
