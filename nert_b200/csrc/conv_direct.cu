@@ -64,7 +64,37 @@ __device__ __forceinline__ void direct_store(const DirectArgs& a, const float (&
     }
 }
 
-template <int MT>
+// The taps of one input channel for KT x KT filters (KT = 1 or 3, known at
+// compile time and unrolled) or any filter (KT = 0); BOUNDED = false when the
+// whole window lies inside the input (no per-tap test).
+template <int MT, int KT, bool BOUNDED>
+__device__ __forceinline__ void direct_channel(const DirectArgs& a, const float* xc, const float4* w4, int c, int ih0,
+                                               int iw0, float (&acc)[MT]) {
+    const int KH = KT ? KT : a.KH, KW = KT ? KT : a.KW;
+#pragma unroll
+    for (int kh = 0; kh < KH; ++kh) {
+        const int ih = ih0 + kh * a.dh;
+        const bool hok = !BOUNDED || (ih >= 0 && ih < a.H);
+        const int krow = (c * KH + kh) * KW;
+        const float* xr = xc + (int64_t)ih * a.W;
+#pragma unroll
+        for (int kw = 0; kw < KW; ++kw) {
+            const int iw = iw0 + kw * a.dw;
+            const float xv = (!BOUNDED || (hok && iw >= 0 && iw < a.W)) ? __ldg(xr + iw) : 0.0f;
+            const float4* wk = w4 + (krow + kw) * (MT / 4);
+#pragma unroll
+            for (int q = 0; q < MT / 4; ++q) {
+                const float4 wv = wk[q];
+                acc[4 * q] = fmaf(wv.x, xv, acc[4 * q]);
+                acc[4 * q + 1] = fmaf(wv.y, xv, acc[4 * q + 1]);
+                acc[4 * q + 2] = fmaf(wv.z, xv, acc[4 * q + 2]);
+                acc[4 * q + 3] = fmaf(wv.w, xv, acc[4 * q + 3]);
+            }
+        }
+    }
+}
+
+template <int MT, int KT>
 __global__ void __launch_bounds__(kDirectThreads) conv_direct_kernel(const __grid_constant__ DirectArgs a) {
     extern __shared__ float4 direct_smem4[];
     float* ws = reinterpret_cast<float*>(direct_smem4); // ws[(c*KH + kh)*KW + kw][m], MT per row
@@ -89,25 +119,15 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_kernel(const __gri
         acc[m] = 0.0f;
     }
     const float4* w4 = reinterpret_cast<const float4*>(ws);
-    for (int c = 0; c < a.C; ++c) {
-        const float* xc = xn + (int64_t)c * a.H * a.W;
-        for (int kh = 0; kh < a.KH; ++kh) {
-            const int ih = ih0 + kh * a.dh;
-            const bool hok = ih >= 0 && ih < a.H;
-            const int krow = (c * a.KH + kh) * a.KW;
-            for (int kw = 0; kw < a.KW; ++kw) {
-                const int iw = iw0 + kw * a.dw;
-                const float xv = (hok && iw >= 0 && iw < a.W) ? __ldg(xc + (int64_t)ih * a.W + iw) : 0.0f;
-                const float4* wk = w4 + (krow + kw) * (MT / 4);
-#pragma unroll
-                for (int q = 0; q < MT / 4; ++q) {
-                    const float4 wv = wk[q];
-                    acc[4 * q] = fmaf(wv.x, xv, acc[4 * q]);
-                    acc[4 * q + 1] = fmaf(wv.y, xv, acc[4 * q + 1]);
-                    acc[4 * q + 2] = fmaf(wv.z, xv, acc[4 * q + 2]);
-                    acc[4 * q + 3] = fmaf(wv.w, xv, acc[4 * q + 3]);
-                }
-            }
+    // a window wholly inside the input (most pixels) skips the per-tap tests
+    const bool inside = ih0 >= 0 && ih0 + (a.KH - 1) * a.dh < a.H && iw0 >= 0 && iw0 + (a.KW - 1) * a.dw < a.W;
+    if (inside) {
+        for (int c = 0; c < a.C; ++c) {
+            direct_channel<MT, KT, false>(a, xn + (int64_t)c * a.H * a.W, w4, c, ih0, iw0, acc);
+        }
+    } else {
+        for (int c = 0; c < a.C; ++c) {
+            direct_channel<MT, KT, true>(a, xn + (int64_t)c * a.H * a.W, w4, c, ih0, iw0, acc);
         }
     }
     float* yn = a.y + (int64_t)n * a.M * opix + p;
@@ -132,6 +152,11 @@ __global__ void __launch_bounds__(kDirectThreads) conv_direct_kernel(const __gri
 }
 
 int direct_width(int64_t M) { return M <= 4 ? 4 : (M <= 8 ? 8 : (M <= 16 ? 16 : 32)); }
+
+template <int MT, int KT>
+void launch_direct(dim3 grid, size_t smem, nb2_device* dev, const DirectArgs& a) {
+    conv_direct_kernel<MT, KT><<<grid, kDirectThreads, smem, dev->stream>>>(a);
+}
 
 } // namespace
 
@@ -174,28 +199,21 @@ void conv_direct(nb2_device* dev, const ConvGeom& g, const float* x, const float
     const size_t smem = static_cast<size_t>(g.C * g.KH * g.KW * mt) * sizeof(float);
     const dim3 grid(static_cast<unsigned>((g.OH * g.OW + kDirectThreads - 1) / kDirectThreads),
                     static_cast<unsigned>(g.N));
-    static bool attr[64] = {};
-    if (!attr[dev->ordinal]) {
-        for (auto fn : {conv_direct_kernel<4>, conv_direct_kernel<8>, conv_direct_kernel<16>, conv_direct_kernel<32>}) {
-            check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(kDirectSmemFloats * sizeof(float))),
-                       "cudaFuncSetAttribute(conv_direct)");
-        }
-        attr[dev->ordinal] = true;
-    }
-    switch (mt) {
-    case 4:
-        conv_direct_kernel<4><<<grid, kDirectThreads, smem, dev->stream>>>(a);
-        break;
-    case 8:
-        conv_direct_kernel<8><<<grid, kDirectThreads, smem, dev->stream>>>(a);
-        break;
-    case 16:
-        conv_direct_kernel<16><<<grid, kDirectThreads, smem, dev->stream>>>(a);
-        break;
-    default:
-        conv_direct_kernel<32><<<grid, kDirectThreads, smem, dev->stream>>>(a);
-        break;
+    // 1x1 and 3x3 filters unrolled at compile time, any other shape generic
+    const int kt = (g.KH == 1 && g.KW == 1) ? 1 : ((g.KH == 3 && g.KW == 3) ? 3 : 0);
+    switch (mt * 10 + kt) {
+    case 40: launch_direct<4, 0>(grid, smem, dev, a); break;
+    case 41: launch_direct<4, 1>(grid, smem, dev, a); break;
+    case 43: launch_direct<4, 3>(grid, smem, dev, a); break;
+    case 80: launch_direct<8, 0>(grid, smem, dev, a); break;
+    case 81: launch_direct<8, 1>(grid, smem, dev, a); break;
+    case 83: launch_direct<8, 3>(grid, smem, dev, a); break;
+    case 160: launch_direct<16, 0>(grid, smem, dev, a); break;
+    case 161: launch_direct<16, 1>(grid, smem, dev, a); break;
+    case 163: launch_direct<16, 3>(grid, smem, dev, a); break;
+    case 320: launch_direct<32, 0>(grid, smem, dev, a); break;
+    case 321: launch_direct<32, 1>(grid, smem, dev, a); break;
+    default: launch_direct<32, 3>(grid, smem, dev, a); break;
     }
     check_cuda(cudaGetLastError(), "conv_direct launch");
 }
