@@ -867,6 +867,21 @@ std::set<std::string> assign_nhwc(const Graph& g, const std::map<std::string, Te
             conv_out.insert(e.out);
         } else if (e.op == "MaxPool" && n.outputs.size() == 1) {
             unite(n.inputs[0], n.outputs[0]);
+        } else if (e.op == "Concat" || e.op == "Split" ||
+                   (e.op == "Resize" && shapes.at(n.inputs[0]).dims.size() == 4)) {
+            // the channels-last forms cut and move along the same logical
+            // axes; every 4-D tensor of the node shares one layout
+            // (Split's sizes and Resize's roi / scales / sizes are
+            // operands, not data)
+            const std::string& first = n.inputs[0];
+            if (e.op == "Concat") {
+                for (const auto& t : n.inputs) {
+                    unite(t, first);
+                }
+            }
+            for (const auto& t : n.outputs) {
+                unite(t, first);
+            }
         } else if (e.op == "GlobalAveragePool") {
             bad.insert(n.outputs[0]);
         } else if (e.op == "Relu" || e.op == "Sigmoid" || e.op == "Erf" || e.op == "Sqrt" || e.op == "Neg" ||
@@ -1505,7 +1520,11 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             nb2_device* dev = dev_;
             st.run = [=] { layernorm(dev, x, sc, bi, y, mo, io, rows, D, eps); };
         } else {
-            MoveStep ms = build_move_step(n, g_, shapes_, P, dmalloc);
+            const bool cl = (e.op == "Concat" || e.op == "Split" || e.op == "Resize") && nhwc.count(n.outputs[0]) > 0;
+            if (cl) {
+                st.label += "[nhwc]";
+            }
+            MoveStep ms = build_move_step(n, g_, shapes_, P, dmalloc, cl);
             if (!ms.run) {
                 throw LoadError(n.where() + ": op '" + n.op + "' has no row on the B200 device");
             }

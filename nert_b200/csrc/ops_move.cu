@@ -215,6 +215,23 @@ __global__ void resize_nearest2_kernel(const T* __restrict__ x, T* __restrict__ 
 
 // The same for float rows with OW % 4 == 0: four outputs of one row per
 // thread and one 16-byte store (the gathers of a quad share one input row).
+// Nearest resize of a channels-last image ([N,H,W,C] in memory, C and N
+// unchanged): each output pixel's C floats are the source pixel's, moved as
+// 16-byte vectors; lh / lw are the H and W axes' source-index tables.
+__global__ void resize_nearest_rows_kernel(const float4* __restrict__ x, float4* __restrict__ y,
+                                           const int64_t* __restrict__ lh, const int64_t* __restrict__ lw,
+                                           uint32_t H, uint32_t W, uint32_t OH, uint32_t OW, uint32_t C4,
+                                           uint32_t n4) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const uint32_t q = i % C4;
+        uint32_t t = i / C4;
+        const uint32_t ow = t % OW;
+        t /= OW;
+        const uint32_t oh = t % OH, img = t / OH;
+        y[i] = x[((img * H + static_cast<uint32_t>(lh[oh])) * W + static_cast<uint32_t>(lw[ow])) * C4 + q];
+    }
+}
+
 __global__ void resize_nearest2_vec4_kernel(const float* __restrict__ x, float4* __restrict__ y,
                                             const int64_t* __restrict__ lh, const int64_t* __restrict__ lw,
                                             uint32_t H, uint32_t W, uint32_t OH, uint32_t OW4, uint32_t n4) {
@@ -659,6 +676,33 @@ void gather(nb2_device* dev, const void* x, const int64_t* idx, void* y, int64_t
     check_cuda(cudaGetLastError(), "gather launch");
 }
 
+namespace {
+// a 4-D nearest resize that keeps axes 0 and 3 (a channels-last image) with
+// 16-byte channel rows
+bool near_rows(const ResizeTables& t, const void* x, const void* y, int64_t n, int64_t in_numel) {
+    if (t.rank != 4 || t.in_dims[3] % 4 != 0 || n >= (int64_t(1) << 31) || in_numel >= (int64_t(1) << 31) ||
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) != 0) {
+        return false;
+    }
+    for (double w : t.weight) {
+        if (w != 0.0) {
+            return false;
+        }
+    }
+    for (int d : {0, 3}) {
+        if (t.in_dims[d] != t.out_dims[d]) {
+            return false;
+        }
+        for (int64_t i = 0; i < t.out_dims[d]; ++i) {
+            if (t.lower[t.axis_off[d] + i] != i) {
+                return false;
+            }
+        }
+    }
+    return true;
+}
+} // namespace
+
 void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, const void* dev_tables, bool is_f32,
             int near2_hint) {
     ResizeDev r{};
@@ -713,6 +757,13 @@ void resize(nb2_device* dev, const void* x, void* y, const ResizeTables& t, cons
                                                                           static_cast<long long*>(y), lh, lw, H, W,
                                                                           OH, OW, static_cast<uint32_t>(n));
         }
+    } else if (is_f32 && near_rows(t, x, y, n, st)) {
+        const uint32_t n4 = static_cast<uint32_t>(n / 4);
+        resize_nearest_rows_kernel<<<blocks_for(dev, n4), 256, 0, dev->stream>>>(
+            static_cast<const float4*>(x), static_cast<float4*>(y), r.lower + t.axis_off[1], r.lower + t.axis_off[2],
+            static_cast<uint32_t>(t.in_dims[1]), static_cast<uint32_t>(t.in_dims[2]),
+            static_cast<uint32_t>(t.out_dims[1]), static_cast<uint32_t>(t.out_dims[2]),
+            static_cast<uint32_t>(t.in_dims[3] / 4), n4);
     } else if (is_f32) {
         resize_kernel<float><<<g, 256, 0, dev->stream>>>(static_cast<const float*>(x), static_cast<float*>(y), r, n);
     } else {
@@ -897,9 +948,23 @@ int64_t nearest_index(const std::string& mode, double x, int64_t in_len) {
 
 MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::string, TensorInfo>& shapes,
                          const std::function<void*(const std::string&)>& ptr,
-                         const std::function<uint8_t*(int64_t)>& dmalloc) {
+                         const std::function<uint8_t*(int64_t)>& dmalloc, bool nhwc) {
     MoveStep st;
     const auto& sh = [&](const std::string& t) -> const TensorInfo& { return shapes.at(t); };
+    if (nhwc && n.op != "Concat" && n.op != "Split" && n.op != "Resize") {
+        throw LoadError(n.where() + ": no channels-last form of '" + n.op + "'");
+    }
+    // logical axis held at memory position p of a channels-last 4-D tensor
+    constexpr int kLogicalAt[4] = {0, 2, 3, 1};
+    auto mem_dims = [&](const std::vector<int64_t>& d) {
+        if (!nhwc) {
+            return d;
+        }
+        if (d.size() != 4) {
+            throw LoadError(n.where() + ": a channels-last tensor must be 4-D");
+        }
+        return std::vector<int64_t>{d[0], d[2], d[3], d[1]};
+    };
     auto constant = [&](size_t i) -> const Constant& {
         auto it = g.constants.find(n.inputs.at(i));
         if (it == g.constants.end()) {
@@ -928,23 +993,27 @@ MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::stri
         const bool concat = n.op == "Concat";
         const TensorInfo& whole = concat ? sh(n.outputs[0]) : sh(n.inputs[0]);
         const int64_t r = static_cast<int64_t>(whole.dims.size());
-        const int64_t axis = naxis(n, n.geti("axis", 0), r);
+        int64_t axis = naxis(n, n.geti("axis", 0), r);
+        if (nhwc) { // the same cut in memory order: the channel axis is innermost
+            axis = axis == 0 ? 0 : axis == 1 ? 3 : axis - 1;
+        }
+        const std::vector<int64_t> wd = mem_dims(whole.dims);
         int64_t outer = 1, inner = 1;
         for (int64_t i = 0; i < axis; ++i) {
-            outer *= whole.dims[i];
+            outer *= wd[i];
         }
         for (int64_t i = axis + 1; i < r; ++i) {
-            inner *= whole.dims[i];
+            inner *= wd[i];
         }
         const int64_t es = dtype_size(whole.dtype);
-        const int64_t pitch = whole.dims[axis] * inner * es;
+        const int64_t pitch = wd[axis] * inner * es;
         std::vector<CopySeg> segs;
         int64_t at = 0;
         uint8_t* wp = static_cast<uint8_t*>(ptr(concat ? n.outputs[0] : n.inputs[0]));
         const size_t parts = concat ? n.inputs.size() : n.outputs.size();
         for (size_t i = 0; i < parts; ++i) {
             const std::string& t = concat ? n.inputs[i] : n.outputs[i];
-            const int64_t len = sh(t).dims[axis];
+            const int64_t len = mem_dims(sh(t).dims)[axis];
             const int64_t rb = len * inner * es;
             uint8_t* part = static_cast<uint8_t*>(ptr(t));
             CopySeg s{};
@@ -1059,9 +1128,11 @@ MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::stri
         }
         ResizeTables t;
         t.rank = static_cast<int>(rank);
-        t.in_dims = x.dims;
-        t.out_dims = y.dims;
-        for (int64_t d = 0; d < rank; ++d) {
+        t.in_dims = mem_dims(x.dims);
+        t.out_dims = mem_dims(y.dims);
+        // one table per axis, in memory order
+        for (int64_t p = 0; p < rank; ++p) {
+            const int64_t d = nhwc ? kLogicalAt[p] : p;
             t.axis_off.push_back(static_cast<int64_t>(t.lower.size()));
             for (int64_t o = 0; o < y.dims[d]; ++o) {
                 const double xs = source_coord(transform, o, x.dims[d], y.dims[d], scale[d]);

@@ -75,10 +75,12 @@ struct MoveStep {
     int launches = 1;
 };
 // Builds the step for Transpose/Concat/Split/Slice/Gather/TopK/Resize/Cast;
-// `run` is empty for any other op.
+// `run` is empty for any other op. `nhwc`: the node's 4-D tensors are held
+// channels-last ([N,H,W,C] in memory for the logical [N,C,H,W]); only
+// Concat, Split and Resize accept it.
 MoveStep build_move_step(const Node& n, const Graph& g, const std::map<std::string, TensorInfo>& shapes,
                          const std::function<void*(const std::string&)>& ptr,
-                         const std::function<uint8_t*(int64_t)>& dmalloc);
+                         const std::function<uint8_t*(int64_t)>& dmalloc, bool nhwc = false);
 } // namespace eng
 
 } // namespace nb2

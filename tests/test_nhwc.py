@@ -59,6 +59,14 @@ def test_resnet_trunk_is_channels_last_and_vit_is_not():
     assert not any(_layout(configs.vit_b16(1, layers=1)).values())
 
 
+def test_yolo_c2f_blocks_and_neck_are_channels_last():
+    lay = _layout(configs.yolov8n(1))
+    for t in ("b4.split_out1", "b4.cat_out", "b8.cat_out", "up1_out", "cat1_out", "up2_out", "n21.cat_out"):
+        assert lay[t], t
+    # 16-channel halves feed the direct CUDA-core Conv; the head reshapes
+    assert not lay["b2.cat_out"] and not lay["b2.split_out1"] and not lay["h0.cat_out"]
+
+
 def test_grouped_and_narrow_convs_keep_their_input_nchw():
     from nert_b200.onnx_io import FLOAT, Graph
 
@@ -79,6 +87,86 @@ def test_grouped_and_narrow_convs_keep_their_input_nchw():
     assert lay[t1]       # produced by a Conv, read by a C % 32 == 0 Conv
     assert not lay[t2]   # 48 channels: TMA im2col needs C % 32 == 0
     assert not lay[t3]
+
+
+def _c2f_neck_graph(n, h, w, mode="nearest"):
+    """A detector's C2f block and PAN step in miniature: stem -> stride-2
+    Conv -> 1x1 Conv -> Split(32, 32) -> bottleneck (3x3 + residual Add) ->
+    Concat(3 parts) -> 1x1 Conv -> Resize x2 -> Concat with the stem's
+    output -> 1x1 Conv (graph output)."""
+    from nert_b200 import synth
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    g = Graph(name="c2f_neck", opset=13)
+    x = g.add_input("x", [n, 3, 2 * h, 2 * w])
+    k = [0]
+
+    def conv(t, cin, cout, ks, stride=1, relu=True):
+        k[0] += 1
+        wt = synth.normal((cout, cin, ks, ks), (2.0 / (cin * ks * ks)) ** 0.5, synth.seed_of("c2f", f"w{k[0]}"))
+        bi = synth.normal((cout,), 0.1, synth.seed_of("c2f", f"b{k[0]}"))
+        y = g.op("Conv", [t, g.const(f"w{k[0]}", wt), g.const(f"b{k[0]}", bi)], name=f"conv{k[0]}",
+                 kernel_shape=[ks, ks], strides=[stride, stride], pads=[ks // 2] * 4)
+        return g.op("Relu", [y], name=f"relu{k[0]}") if relu else y
+
+    s = conv(x, 3, 64, 3)
+    d = conv(s, 64, 64, 3, 2)
+    t1 = conv(d, 64, 64, 1)
+    a, b = g.op("Split", [t1, g.const("halves", np.array([32, 32], np.int64))], n_out=2, name="split", axis=1)
+    r = g.op("Add", [b, conv(conv(b, 32, 32, 3), 32, 32, 3)], name="res")
+    t2 = conv(g.op("Concat", [a, b, r], name="cat", axis=1), 96, 64, 1)
+    up = g.const("scales", np.array([1, 1, 2, 2], np.float32))
+    u = g.op("Resize", [t2, g.const("roi", np.zeros((0,), np.float32)), up], name="up", mode=mode)
+    y = conv(g.op("Concat", [u, s], name="cat2", axis=1), 128, 64, 1, relu=False)
+    g.add_output(y, None, FLOAT)
+    feed = {"x": synth.uniform((n, 3, 2 * h, 2 * w), -1.0, 1.0, synth.seed_of("c2f", f"x{n}{h}{w}"))}
+    return g, feed
+
+
+def test_split_concat_resize_join_the_channels_last_trunk():
+    g, _ = _c2f_neck_graph(2, 12, 10)
+    lay = _layout(g)
+    for t in ("split_out0", "split_out1", "res_out", "cat_out", "up_out", "cat2_out", "relu1_out", "relu4_out"):
+        assert lay[t], t
+    assert not lay["x"] and not lay[g.outputs[0][0]]
+    assert not any(_layout(g, model.NCHW_ONLY).values())
+    # a Conv reading a 16-channel half cannot take TMA im2col: the Split's
+    # and Concat's tensors then all stay NCHW
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    for read_half in (False, True):
+        h = Graph(opset=13)
+        x = h.add_input("x", [1, 32, 8, 8])
+        t = h.op("Conv", [x, h.const("w0", np.ones((64, 32, 1, 1), np.float32))], name="c0", kernel_shape=[1, 1])
+        p, q = h.op("Split", [t, h.const("sz", np.array([48, 16], np.int64))], n_out=2, name="sp", axis=1)
+        c = h.op("Concat", [q, p], name="cc", axis=1)
+        h.add_output(h.op("Conv", [c, h.const("w1", np.ones((64, 64, 1, 1), np.float32))], name="c1",
+                          kernel_shape=[1, 1]), None, FLOAT)
+        if read_half:
+            h.add_output(h.op("Conv", [q, h.const("w2", np.ones((64, 16, 1, 1), np.float32))], name="c2",
+                              kernel_shape=[1, 1]), None, FLOAT)
+        lay = _layout(h)
+        assert [lay[v] for v in (t, p, q, c)] == [not read_half] * 4, read_half
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["nearest", "linear"])
+def test_split_concat_resize_channels_last_match_oracle(cuda, mode):
+    g, feed = _c2f_neck_graph(2, 12, 10, mode)
+    out = g.outputs[0][0]
+    ref = np_ref.run(g, feed)[out]
+    res = {}
+    for cl in (True, False):
+        m = model.Model(g, {"x": list(feed["x"].shape)}, channels_last=cl)
+        try:
+            res[cl] = m.run(feed)[out]
+            labels = [lab for lab, _ in m.profile()]
+        finally:
+            m.close()
+        for op in ("Split:", "Concat:", "Resize:"):
+            assert any(lab.startswith(op) and lab.endswith("[nhwc]") for lab in labels) == cl, (op, labels)
+        assert rel_err(res[cl], ref) <= TOL, cl
+    assert rel_err(res[True], res[False]) <= TOL
 
 
 @pytest.mark.gpu
