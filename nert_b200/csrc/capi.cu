@@ -115,14 +115,14 @@ namespace {
 
 // Bytes of the NHWC copy a converted NCHW input needs (0 when none).
 size_t nhwc_copy_bytes(const ConvGeom& g) {
-    return (g.cvec || g.cpad) ? static_cast<size_t>(g.N * g.Cin() * g.H * g.W * 4) : 0;
+    return g.converts_input() ? static_cast<size_t>(g.N * g.Cin() * g.H * g.W * 4) : 0;
 }
 
 // A Conv whose input arrives NCHW: converted to NHWC first when its layout
 // asks for it (into `xbuf`, or the device workspace when null), then run.
 void run_nchw_conv(nb2_device* dev, const ConvGeom& g, const float* x, const void* packed, float* y,
                    const Epilogue& ep, void* xbuf) {
-    if (g.cvec || g.cpad) {
+    if (g.converts_input()) {
         float* xp = static_cast<float*>(xbuf != nullptr ? xbuf : dev->scratch(nhwc_copy_bytes(g)));
         nchw_to_nhwc_pad(dev, x, xp, g.N, g.C, g.H, g.W, g.Cin());
         conv_run(dev, g, xp, packed, y, ep);

@@ -845,7 +845,7 @@ std::set<std::string> assign_nhwc(const Graph& g, const std::map<std::string, Te
             const auto& x = shapes.at(n.inputs[0]);
             if (x.dims.size() == 4) {
                 const ConvGeom cg = conv_geom(n, x, shapes.at(n.inputs[1]), shapes.at(n.outputs[0]));
-                if (!cg.nhwc_input_ok()) {
+                if (!cg.nhwc_in_place().nhwc_input_ok()) {
                     bad.insert(n.inputs[0]);
                 }
                 if (direct_conv_ok(cg)) { // the CUDA-core path reads and writes NCHW
@@ -1051,7 +1051,9 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
         st.label = n.op + (e.group > 1 ? "+fused" : "") + ":" + n.name;
         if (e.op == "Conv") {
             ConvGeom geom = conv_geom(n, shapes_.at(n.inputs[0]), shapes_.at(n.inputs[1]), shapes_.at(n.outputs[0]));
-            geom.in_nhwc = nhwc.count(n.inputs[0]) > 0;
+            if (nhwc.count(n.inputs[0]) > 0) {
+                geom = geom.nhwc_in_place();
+            }
             geom.out_nhwc = nhwc.count(e.out) > 0;
             if (geom.in_nhwc || geom.out_nhwc) {
                 st.label += geom.in_nhwc ? (geom.out_nhwc ? "[nhwc]" : "[nhwc>nchw]") : "[nchw>nhwc]";
@@ -1117,7 +1119,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
                 cudaFree(tmp);
                 weight_bytes_ += pbytes;
                 nb2_device* dev = dev_;
-                if (geom.cvec || geom.cpad) {
+                if (geom.converts_input()) {
                     // the converted input lives in the shared transform buffer
                     const int64_t cp = geom.Cin();
                     xform_need = std::max(xform_need, geom.N * cp * geom.H * geom.W * 4);
@@ -1380,7 +1382,7 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             weight_bytes_ += pbytes;
             const size_t zb = convt_zero_insert_bytes(t);
             float* xz = zb ? reinterpret_cast<float*>(dmalloc(align_up(static_cast<int64_t>(zb)))) : nullptr;
-            if (geom.cvec || geom.cpad) {
+            if (geom.converts_input()) {
                 xform_need = std::max(xform_need, geom.N * geom.Cin() * geom.H * geom.W * 4);
             }
             Epilogue ep;
@@ -1390,14 +1392,14 @@ void Model::build(const std::map<std::string, std::vector<int64_t>>& input_dims,
             nb2_device* dev = dev_;
             void** xp = &xform_;
             st.launches = contraction_launches(dev_, geom.N * geom.OH * geom.OW, geom.Mg(), geom.K(), geom.group) +
-                          (zb ? 1 : 0) + ((geom.cvec || geom.cpad) ? 1 : 0);
+                          (zb ? 1 : 0) + (geom.converts_input() ? 1 : 0);
             st.run = [=] {
                 const float* src = x;
                 if (xz) {
                     convt_zero_insert(dev, t, x, xz);
                     src = xz;
                 }
-                if (geom.cvec || geom.cpad) {
+                if (geom.converts_input()) {
                     nchw_to_nhwc_pad(dev, src, static_cast<float*>(*xp), geom.N, geom.C, geom.H, geom.W, geom.Cin());
                     conv_run(dev, geom, static_cast<const float*>(*xp), packed, y, ep);
                 } else {

@@ -32,8 +32,9 @@ namespace {
 
 // kADenseTma: row-major A whose rows are 16-byte aligned; TMA brings the raw
 // fp32 tile into shared memory and the producer warps split it in place.
-// kAConvNhwc: Conv over NHWC activations (C % 32 == 0); TMA im2col brings the
-// raw fp32 tile for one (filter tap, 32-channel block) per K block.
+// kAConvNhwc: Conv over NHWC activations (C % 4 == 0; K padded to a multiple
+// of 32 channels a tap); TMA im2col brings the raw fp32 tile for one (filter
+// tap, 32-channel block) per K block, the channels past C read as zeros.
 // kAConvCvec: Conv over x[N][H][W][cv] with cv = 4, 8 or 16 channels (C <= cv,
 // zero padded; e.g. a stem's RGB image); K ordered (tap, channel), so a
 // thread's 16 K values are 16 / cv taps of 16-byte vector loads.
@@ -1539,7 +1540,8 @@ void conv_run(nb2_device* dev, const ConvGeom& g, const float* x, const void* pa
     // (~850 cycles) bounds the main loop
     a.mode = g.cvec ? kAConvCvec : g.in_nhwc ? kAConvNhwc : g.tap_major() ? kAConvTap : kAConvGeneric;
     if (g.in_nhwc && !g.nhwc_input_ok()) {
-        fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 32 == 0 and strides <= 8");
+        fail(kStatusUnsupported, "Conv: NHWC input needs group 1, C % 4 == 0 (K padded to 32 channels a tap) "
+                                 "and strides <= 8");
     }
     if (g.cvec && (!g.cvec_input_ok(g.cvec) || g.in_nhwc)) {
         fail(kStatusUnsupported, "Conv: the narrow-channel input form needs group 1, C <= cv, cv in {4, 8, 16}");

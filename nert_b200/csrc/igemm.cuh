@@ -47,10 +47,26 @@ struct ConvGeom {
     // NHWC input holding cpad >= C channels (zero padded to a multiple of 32
     // for the TMA im2col form); 0 = exactly C.
     int64_t cpad = 0;
+    // cpad pads only the packed K layout: the NHWC input holds exactly C
+    // channels (C % 4 == 0, 16-byte pixels) and the TMA im2col copy of the
+    // last channel block reads the channels past C as zeros.
+    bool cpad_k_only = false;
     int64_t Cg() const { return C / group; }
     int64_t Mg() const { return M / group; }
     // channels per pixel of the input tensor
-    int64_t Cin() const { return cvec ? cvec : (cpad ? cpad : C); }
+    int64_t Cin() const { return cvec ? cvec : (cpad && !cpad_k_only ? cpad : C); }
+    // the NCHW input is first copied to a padded NHWC buffer
+    bool converts_input() const { return cvec != 0 || (cpad != 0 && !cpad_k_only); }
+    // this geometry with its input read channels-last where it lies
+    ConvGeom nhwc_in_place() const {
+        ConvGeom r = *this;
+        r.in_nhwc = true;
+        if (group == 1 && C % 32 != 0 && cvec == 0 && cpad == 0) {
+            r.cpad = (C + 31) / 32 * 32;
+            r.cpad_k_only = true;
+        }
+        return r;
+    }
     // channels per filter tap in the packed K layout
     int64_t Cpad() const { return cvec ? cvec : (cpad ? cpad : Cg()); }
     int64_t K() const { return Cpad() * KH * KW; }
@@ -61,7 +77,7 @@ struct ConvGeom {
     // TMA im2col limits for a 4-D map: traversal strides 1..8, box corners in
     // [-128, 127] and filter offsets in [0, 255] (kept well inside here).
     bool nhwc_input_ok() const {
-        return group == 1 && Cin() % 32 == 0 && sh >= 1 && sh <= 8 && sw >= 1 && sw <= 8 && ph <= 64 && pw <= 64 &&
+        return group == 1 && Cpad() % 32 == 0 && Cin() % 4 == 0 && sh >= 1 && sh <= 8 && sw >= 1 && sw <= 8 && ph <= 64 && pw <= 64 &&
                pad_bottom() >= -64 && pad_bottom() <= 64 && pad_right() >= -64 && pad_right() <= 64 &&
                dh * (KH - 1) <= 64 && dw * (KW - 1) <= 64;
     }

@@ -27,6 +27,11 @@ CHAINS = [
     ("5x3_s3x1_m42", 2, 3, 25, 11, 64, 42, (5, 3), (3, 1), (2, 1, 2, 1), (1, 1), False, False, False),
     ("pool_gap", 2, 3, 33, 31, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, True, True),
     ("b4_56x56", 4, 16, 56, 56, 64, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), True, False, False),
+    # C % 32 != 0: the last 32-channel block of each tap reads past C as zeros
+    ("c80_3x3_m80", 2, 3, 20, 20, 80, 80, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), False, False, False),
+    ("c48_1x1s2_res", 2, 5, 17, 19, 48, 64, (1, 1), (2, 2), (0, 0, 0, 0), (1, 1), True, False, False),
+    ("c36_3x3_pool", 1, 3, 21, 23, 36, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), False, True, False),
+    ("c100_5x5s2_dil", 2, 3, 23, 21, 100, 40, (5, 5), (2, 2), (4, 4, 3, 3), (2, 2), False, False, False),
 ]
 
 
@@ -67,6 +72,15 @@ def test_yolo_c2f_blocks_and_neck_are_channels_last():
     assert not lay["b2.cat_out"] and not lay["b2.split_out1"] and not lay["h0.cat_out"]
 
 
+def test_channels_need_16_byte_pixels_for_channels_last():
+    lay = _layout(_chain(("c42", 1, 3, 12, 12, 42, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), False, False,
+                          False))[0])
+    assert not lay["head_relu_out"]  # 42 channels: 168-byte pixels
+    lay = _layout(_chain(("c44", 1, 3, 12, 12, 44, 64, (3, 3), (1, 1), (1, 1, 1, 1), (1, 1), False, False,
+                          False))[0])
+    assert lay["head_relu_out"]
+
+
 def test_grouped_and_narrow_convs_keep_their_input_nchw():
     from nert_b200.onnx_io import FLOAT, Graph
 
@@ -85,7 +99,7 @@ def test_grouped_and_narrow_convs_keep_their_input_nchw():
     lay = _layout(g)
     assert not lay[t0]   # read by a grouped Conv
     assert lay[t1]       # produced by a Conv, read by a C % 32 == 0 Conv
-    assert not lay[t2]   # 48 channels: TMA im2col needs C % 32 == 0
+    assert not lay[t2]   # read by the direct CUDA-core Conv (8 outputs)
     assert not lay[t3]
 
 
@@ -130,20 +144,20 @@ def test_split_concat_resize_join_the_channels_last_trunk():
         assert lay[t], t
     assert not lay["x"] and not lay[g.outputs[0][0]]
     assert not any(_layout(g, model.NCHW_ONLY).values())
-    # a Conv reading a 16-channel half cannot take TMA im2col: the Split's
-    # and Concat's tensors then all stay NCHW
+    # a Conv reading a 22-channel half (88-byte pixels) cannot take TMA
+    # im2col: the Split's and Concat's tensors then all stay NCHW
     from nert_b200.onnx_io import FLOAT, Graph
 
     for read_half in (False, True):
         h = Graph(opset=13)
         x = h.add_input("x", [1, 32, 8, 8])
         t = h.op("Conv", [x, h.const("w0", np.ones((64, 32, 1, 1), np.float32))], name="c0", kernel_shape=[1, 1])
-        p, q = h.op("Split", [t, h.const("sz", np.array([48, 16], np.int64))], n_out=2, name="sp", axis=1)
+        p, q = h.op("Split", [t, h.const("sz", np.array([42, 22], np.int64))], n_out=2, name="sp", axis=1)
         c = h.op("Concat", [q, p], name="cc", axis=1)
         h.add_output(h.op("Conv", [c, h.const("w1", np.ones((64, 64, 1, 1), np.float32))], name="c1",
                           kernel_shape=[1, 1]), None, FLOAT)
         if read_half:
-            h.add_output(h.op("Conv", [q, h.const("w2", np.ones((64, 16, 1, 1), np.float32))], name="c2",
+            h.add_output(h.op("Conv", [q, h.const("w2", np.ones((64, 22, 1, 1), np.float32))], name="c2",
                               kernel_shape=[1, 1]), None, FLOAT)
         lay = _layout(h)
         assert [lay[v] for v in (t, p, q, c)] == [not read_half] * 4, read_half
