@@ -72,6 +72,10 @@ GEMMS = [
     # 100 and 196 tiles on 148 SMs: the balanced split
     ("balanced_100_tiles_2560x640x4096", 2560, 640, 4096, dict(tile_n=128, two_in_flight=0, k_slices=0)),
     ("balanced_196_tiles_1792x1792x2304", 1792, 1792, 2304, dict(tile_n=128, two_in_flight=0, k_slices=0)),
+    # 300 tiles of 24 K blocks (ViT-B/16 b32 q/k/v/proj): a last wave of 4
+    # tiles after two full ones stays unsplit (the balanced split measured 5%
+    # slower per ViT forward there)
+    ("sparse_tail_unsplit_6304x768x768", 6304, 768, 768, dict(tile_n=128, two_in_flight=0, k_slices=1)),
 ]
 
 
