@@ -292,9 +292,9 @@ typedef struct nb2_model nb2_model;
 #define NB2_MODEL_NO_FUSION 1 /* run every node as its own row */
 #define NB2_MODEL_NO_GRAPH 2  /* launch rows one by one instead of a CUDA-graph replay */
 /* Keep every activation NCHW. By default a Conv trunk whose tensors only meet
- * Conv (group 1, C % 32 == 0 inputs), MaxPool, GlobalAveragePool and
- * layout-free elementwise rows is kept channels-last (NHWC) inside the arena;
- * graph inputs and outputs are NCHW either way. */
+ * Conv (group 1, C % 4 == 0 inputs), MaxPool, GlobalAveragePool, Concat,
+ * Split, 4-D Resize and layout-free elementwise rows is kept channels-last
+ * (NHWC) inside the arena; graph inputs and outputs are NCHW either way. */
 #define NB2_MODEL_NCHW_ONLY 4
 /* Run attention chains (MatMul Q K^T, scale, Softmax, MatMul with V) as
  * separate rows instead of the fused attention step. */

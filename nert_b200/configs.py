@@ -404,8 +404,8 @@ def conv_chain(batch: int, cin: int, h: int, w: int, c: int, m: int, kernel=(3, 
     input [N,cin,H,W] -> Conv 1x1 (cin->c) + Relu [-> MaxPool 3x3/2 pad 1]
     -> Conv(kernel, strides, pads, dilations; c->m) [+ 1x1 strided skip] + Relu
     -> Conv 1x1 (m->16) [-> GlobalAveragePool] -> output.
-    Inside the engine the middle Conv reads and writes channels-last when
-    c % 32 == 0; the first writes it and the last reads it. Returns
+    Inside the engine the middle Conv reads channels-last when c % 4 == 0
+    (the first Conv writes it that way). Returns
     (graph, feed).
     """
     b = _Builder(tag)
