@@ -213,8 +213,6 @@ __global__ void resize_nearest2_kernel(const T* __restrict__ x, T* __restrict__ 
     }
 }
 
-// The same for float rows with OW % 4 == 0: four outputs of one row per
-// thread and one 16-byte store (the gathers of a quad share one input row).
 // Nearest resize of a channels-last image ([N,H,W,C] in memory, C and N
 // unchanged): each output pixel's C floats are the source pixel's, moved as
 // 16-byte vectors; lh / lw are the H and W axes' source-index tables.
@@ -232,6 +230,9 @@ __global__ void resize_nearest_rows_kernel(const float4* __restrict__ x, float4*
     }
 }
 
+// resize_nearest2_kernel for float rows with OW % 4 == 0: four outputs of one
+// row per thread and one 16-byte store (the gathers of a quad share one input
+// row).
 __global__ void resize_nearest2_vec4_kernel(const float* __restrict__ x, float4* __restrict__ y,
                                             const int64_t* __restrict__ lh, const int64_t* __restrict__ lw,
                                             uint32_t H, uint32_t W, uint32_t OH, uint32_t OW4, uint32_t n4) {
