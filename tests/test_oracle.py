@@ -198,3 +198,85 @@ def test_np_ref_conv_transpose_matches_reference(case):
     got = np_ref.run(g, {"x": x})[y]
     assert got.shape == want.shape
     assert np.abs(got.astype(np.float64) - want).max() <= 1e-5 * np.abs(want).max()
+
+
+def _movement_graph(kind):
+    """Seeded single-node graphs for the rows the random cases above leave
+    out: normalisation, the data-movement rows (with their constant
+    operands) and the int64-producing TopK. Returns (graph, feed)."""
+    from nert_b200.onnx_io import INT64
+
+    seed = synth.seed_of("oracle_moves", kind)
+    g = Graph(name=kind, opset=17 if kind == "layernorm" else 13)
+    x4 = (2, 6, 5, 7)
+    feed = {"x": synth.normal(x4, 1.0, seed)}
+    x = g.add_input("x", list(x4))
+    outs = []
+    if kind == "layernorm":
+        feed = {"x": synth.normal((3, 7, 48), 2.0, seed)}
+        x = g.inputs[0][0]
+        g.inputs[0] = (x, [3, 7, 48], FLOAT)
+        outs = [g.op("LayerNormalization", [x, g.const("s", synth.normal((48,), 1.0, seed ^ 1)),
+                                             g.const("b", synth.normal((48,), 1.0, seed ^ 2))],
+                     name="ln", axis=-1, epsilon=1e-6)]
+    elif kind == "erf_gelu":
+        t = g.op("Div", [x, g.const("r2", np.array(1.4142135, np.float32))], name="d")
+        t = g.op("Add", [g.op("Erf", [t], name="e"), g.const("one", np.array(1.0, np.float32))], name="a")
+        outs = [g.op("Mul", [g.op("Mul", [x, t], name="m"), g.const("h", np.array(0.5, np.float32))], name="m2")]
+    elif kind == "transpose":
+        outs = [g.op("Transpose", [x], name="t", perm=[0, 2, 3, 1])]
+    elif kind == "concat_split":
+        a, b, c = g.op("Split", [x, g.const("sz", np.array([1, 3, 2], np.int64))], n_out=3, name="sp", axis=1)
+        outs = [g.op("Concat", [c, a, b], name="cat", axis=1)]
+    elif kind == "resize_nearest":
+        outs = [g.op("Resize", [x, g.const("roi", np.zeros((0,), np.float32)),
+                                g.const("sc", np.array([1, 1, 2, 2], np.float32))], name="r", mode="nearest")]
+    elif kind == "resize_linear_sizes":
+        outs = [g.op("Resize", [x, g.const("roi", np.zeros((0,), np.float32)), g.const("sc", np.zeros((0,), np.float32)),
+                                g.const("sizes", np.array([2, 6, 9, 4], np.int64))], name="r", mode="linear")]
+    elif kind == "gather_negative":
+        outs = [g.op("Gather", [x, g.const("idx", np.array([[4, -1], [0, -5]], np.int64))], name="ga", axis=3)]
+    elif kind == "slice_negative_step":
+        outs = [g.op("Slice", [x, g.const("st", np.array([-1, 1], np.int64)), g.const("en", np.array([-100, 6], np.int64)),
+                               g.const("ax", np.array([3, 1], np.int64)), g.const("sp", np.array([-2, 2], np.int64))],
+                     name="sl")]
+    elif kind == "reduce_mean":
+        outs = [g.op("ReduceMean", [x], name="rm", axes=[2, 3], keepdims=1)]
+    elif kind == "topk":
+        feed = {"x": synth.normal((3, 50), 1.0, seed)}
+        g.inputs[0] = ("x", [3, 50], FLOAT)
+        v, i = g.op("TopK", ["x", g.const("k", np.array([7], np.int64))], n_out=2, name="tk", axis=-1)
+        g.add_output(v, None, FLOAT)
+        g.add_output(i, None, INT64)
+        return g, feed
+    elif kind == "elementwise":
+        y = g.add_input("y", list(x4))
+        feed["y"] = np.abs(synth.normal(x4, 1.0, seed ^ 3)) + np.float32(0.5)
+        t = g.op("Sub", [g.op("Relu", [x], name="re"), g.op("Sqrt", [y], name="sq")], name="su")
+        outs = [g.op("Pow", [y, g.const("p", np.array(1.5, np.float32))], name="pw"), t]
+    for o in outs:
+        g.add_output(o, None, FLOAT)
+    return g, feed
+
+
+MOVEMENT_KINDS = ["layernorm", "erf_gelu", "transpose", "concat_split", "resize_nearest", "resize_linear_sizes",
+                  "gather_negative", "slice_negative_step", "reduce_mean", "topk", "elementwise"]
+
+
+@needs_ref
+@pytest.mark.parametrize("kind", MOVEMENT_KINDS)
+def test_np_ref_matches_reference_movement_rows(kind):
+    """Float outputs within 1e-6 x max|ref| (the reference accumulates
+    LayerNormalization and ReduceMean in double as np_ref does); int64 outputs
+    (TopK indices) equal."""
+    g, feed = _movement_graph(kind)
+    want = ref.run_graph(g, feed)
+    got = np_ref.run(g, feed)
+    assert set(got) >= set(want)
+    for name, b in want.items():
+        a = got[name]
+        assert a.shape == b.shape, name
+        if b.dtype == np.int64:
+            np.testing.assert_array_equal(a, b, err_msg=name)
+        else:
+            assert np.abs(a.astype(np.float64) - b).max() <= 1e-6 * max(1.0, np.abs(b).max()), name
