@@ -64,6 +64,24 @@ def test_resnet_trunk_is_channels_last_and_vit_is_not():
     assert not any(_layout(configs.vit_b16(1, layers=1)).values())
 
 
+def test_a_reshaped_split_half_keeps_the_block_nchw():
+    """A Split output that also feeds a reshape (no channels-last form)
+    makes the Split's input, both halves and the Concat NCHW."""
+    from nert_b200.onnx_io import FLOAT, Graph
+
+    h = Graph(opset=13)
+    x = h.add_input("x", [1, 32, 8, 8])
+    t = h.op("Conv", [x, h.const("w0", np.ones((64, 32, 3, 3), np.float32))], name="c0", kernel_shape=[3, 3],
+             pads=[1, 1, 1, 1])
+    p, q = h.op("Split", [t, h.const("sz", np.array([32, 32], np.int64))], n_out=2, name="sp", axis=1)
+    c = h.op("Concat", [p, q], name="cc", axis=1)
+    h.add_output(h.op("Conv", [c, h.const("w1", np.ones((64, 64, 3, 3), np.float32))], name="c1",
+                      kernel_shape=[3, 3], pads=[1, 1, 1, 1]), None, FLOAT)
+    h.add_output(h.op("Reshape", [q, h.const("shape", np.array([1, -1], np.int64))], name="flat"), None, FLOAT)
+    lay = _layout(h)
+    assert not any(lay[v] for v in (t, p, q, c))
+
+
 def test_yolo_c2f_blocks_and_neck_are_channels_last():
     lay = _layout(configs.yolov8n(1))
     for t in ("b4.split_out1", "b4.cat_out", "b8.cat_out", "up1_out", "cat1_out", "up2_out", "n21.cat_out"):
